@@ -1,0 +1,342 @@
+"""Benchmark: 8B-class Q4_K decode at batch 1 through the B200 provider.
+
+Workload: a Llama-style decoder with 32 layers, d_model
+4096, 32 query / 8 KV heads of 128, SwiGLU FFN 14336, vocabulary 128256,
+RMSNorm eps 1e-5, RoPE theta 500000; projections Q4_K, token embedding and
+output Q6_K; fp16 KV cache. Random-init weights from the seeded synthetic
+generator (no checkpoint), a 512-token prompt of random ids, then greedy
+decoding. One bench step = 256 greedy decode tokens at positions 512..767.
+
+value  tokens/s with everything resident in HBM: each step replays the
+       captured decode graph 256 times, the argmax feeding the next token on
+       the device; CUDA events on the provider's stream.
+e2e    tokens/s through the engine-facing vtable (plan_token with a host
+       logits buffer): every token is a kernel-argument upload of
+       {token, position}, the graph replay, the 513 KB logits download into
+       pinned host memory and the host greedy argmax.
+
+--impl reference times the Fyodor engine's own CPU path (compiled from the
+reference sources into oracle/_ref) on this host's cores for the same
+workload and metric.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT = 512
+DECODE = 256
+CFG8B = dict(layers=32, embedding=4096, heads=32, kv_heads=8, feed_forward=14336, vocabulary=128256, context=1024,
+             rope_base=500000.0, epsilon=1e-5, seed=1234, norm_mode=1)
+# algorithmic bytes per token: weights + mean KV read
+WEIGHT_BYTES_8B = 4_357_877_024
+
+
+def kv_bytes(position):  # fp16 K+V of every layer at attention length position+1
+    return 131_072 * (position + 1)
+
+
+def mean_bytes_per_token():
+    return WEIGHT_BYTES_8B + sum(kv_bytes(p) for p in range(PROMPT, PROMPT + DECODE)) / DECODE
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.QUERY,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_env():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def init_dist(world):
+    if world <= 1:
+        return None
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    return dist
+
+
+def max_over_ranks(dist, value):
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------------- CPU reference
+def cpu_reference_rate(model, sample_seconds, max_tokens=64):
+    """Decode tokens through the engine's own CPU provider (its SIMD kernels and
+    worker pool, as fyodor-bench -b cpu) on this model; returns (tok/s, tokens,
+    threads)."""
+    import oracle as O
+    from tests.patterns import bench_tokens
+    threads = os.cpu_count() or 1
+    os.environ["NYA_CPU_THREADS"] = str(threads)
+    s = O.RefSession(model.ptr, 1024, model.vocabulary, provider="cpu")
+    toks = bench_tokens(max_tokens, model.vocabulary)
+    s.run(toks[:1])  # warm the worker pool and page in the weights
+    n, t0 = 0, time.perf_counter()
+    while n < max_tokens - 1 and (time.perf_counter() - t0 < sample_seconds or n < 2):
+        s.run(toks[n + 1:n + 2])
+        n += 1
+    rate = n / (time.perf_counter() - t0)
+    s.close()
+    return rate, n, threads
+
+
+# ----------------------------------------------------------------------------- provider arm
+def run_provider(args):
+    import torch
+    import fyodor_b200 as F
+    from tests.patterns import bench_tokens
+    rank, world, local = dist_env()
+    os.environ["NYA_CUDA_DEVICE"] = str(local)
+    torch.cuda.set_device(local)
+    dist = init_dist(world)
+    t_setup = time.perf_counter()
+    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **CFG8B)
+    provider = F.Provider()
+    capacity = PROMPT + DECODE
+    plan = provider.plan(model, capacity)
+    if plan is None:
+        raise SystemExit("the provider declined the 8B plan")
+    prompt = bench_tokens(PROMPT, model.vocabulary)
+    if plan.prefill(prompt, 0) != 0:
+        raise SystemExit("prefill failed")
+    first = int(np.argmax(plan.logits))
+    setup_s = time.perf_counter() - t_setup
+    launches = int(plan.launches_per_token()) + 1 - 1  # graph nodes per greedy step (advance replaces request)
+
+    for _ in range(args.warmup):
+        if plan.time_greedy(first, PROMPT, DECODE) < 0:
+            raise SystemExit("warm-up failed")
+    barrier(dist)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        total_ms = 0.0
+        for _ in range(args.steps):
+            ms = plan.time_greedy(first, PROMPT, DECODE)
+            if ms < 0:
+                raise SystemExit("timed step failed")
+            total_ms += ms
+    torch.cuda.synchronize()
+    barrier(dist)
+    total_ms = max_over_ranks(dist, total_ms)
+    tokens = args.steps * DECODE
+    value = tokens * world / (total_ms / 1000.0)
+
+    # e2e through the vtable with host buffers (pinned logits buffer)
+    pinned = torch.empty(model.vocabulary, dtype=torch.float32, pin_memory=True)
+    plan.logits = pinned.numpy()
+    e2e_steps = max(1, min(args.steps, 3))
+    barrier(dist)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        t = first
+        for i in range(DECODE):
+            if plan.token(t, PROMPT + i) != 0:
+                raise SystemExit("e2e token failed")
+            t = int(np.argmax(plan.logits))
+    e2e_s = max_over_ranks(dist, time.perf_counter() - t0)
+    e2e_value = e2e_steps * DECODE * world / e2e_s
+
+    # dominant kernel (fused gate/up GEMV, 66 MB of Q4_K) timed alone
+    gate_ms, gate_bytes = plan.time_projection(0, 2, 20)
+    qkv_ms, qkv_bytes = plan.time_projection(0, 0, 20)
+    down_ms, down_bytes = plan.time_projection(0, 3, 20)
+    o_ms, o_bytes = plan.time_projection(0, 1, 20)
+    lg_ms, lg_bytes = plan.time_projection(0, 4, 10)
+    breakdown = plan.profile(first, PROMPT, 4)
+    peaks, peak_kind = measured_peaks()
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    achieved = gate_bytes / (gate_ms / 1000.0) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            traffic = json.load(f).get("qgemv_gateup_8b")
+    except (OSError, ValueError):
+        pass
+    bpt = mean_bytes_per_token()
+    step_gbs = bpt * value / world / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, n, threads = cpu_reference_rate(model, args.cpu_seconds)
+        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "reference",
+               "sample": "%d decode tokens of the same 8B model through the Fyodor engine's CPU provider "
+                         "(nya_llm_session_run, NYA_CPU_THREADS=%d) from an empty cache; prompt not prefilled" % (n, threads)}
+    line = {
+        "metric": "8B Q4_K decode tok/s (bs1)",
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak" if world > 1 else "strong",
+        "vs_baseline": None,
+        "dtype": "q4_k weights, s8 limb x u8/s8 int MMA, fp32 accumulate, fp16 KV",
+        "data": "synthetic (seeded random-init weights, random prompt ids)",
+        "config": {"workload": "8B-class Llama decode: prompt 512 then 256 greedy tokens per step, batch 1",
+                   "layers": 32, "d_model": 4096, "heads": "32/8", "ffn": 14336, "vocab": 128256,
+                   "weights": "Q4_K projections, Q6_K embedding/output", "kv": "fp16",
+                   "parallelism": "replicas" if world > 1 else "single-gpu",
+                   "l2": "inputs larger than L2 (4.36 GB of weights per token)"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * DECODE,
+                "d2h_bytes_per_step": 4 * model.vocabulary * DECODE},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": traffic,
+                     "kernel": "qgemv gate/up+SwiGLU (Q4_K 2x14336x4096), timed alone",
+                     "peak_source": peak_kind},
+        "step_roofline": {"bytes_per_token": int(bpt), "achieved_gbs": round(step_gbs, 1),
+                          "frac": round(step_gbs / hbm, 4), "tok_s_at_peak": round(hbm * 1e9 / bpt, 1)},
+        "kernels": {"qkv": [round(qkv_ms * 1e3, 2), round(qkv_bytes / qkv_ms / 1e6, 1)],
+                    "o": [round(o_ms * 1e3, 2), round(o_bytes / o_ms / 1e6, 1)],
+                    "gateup": [round(gate_ms * 1e3, 2), round(achieved, 1)],
+                    "down": [round(down_ms * 1e3, 2), round(down_bytes / down_ms / 1e6, 1)],
+                    "logits": [round(lg_ms * 1e3, 2), round(lg_bytes / lg_ms / 1e6, 1)],
+                    "units": "[us per launch, GB/s]",
+                    "step_ms_by_class": None if breakdown is None else
+                    {"matrix": round(float(breakdown[0]), 4), "attention": round(float(breakdown[1]), 4),
+                     "other": round(float(breakdown[2]), 4)}},
+        "gpu_launches": int(args.steps * DECODE * (launches)),
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+        "setup_s": round(setup_s, 1),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    plan.close()
+    provider.close()
+    model.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    import fyodor_b200 as F
+    import oracle as O
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    if not O.reference_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libnya_ref.so was not built"}))
+        return
+    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **CFG8B)
+    per_step = max(1, args.ref_tokens)
+    threads = os.cpu_count() or 1
+    os.environ["NYA_CPU_THREADS"] = str(threads)
+    s = O.RefSession(model.ptr, 1024, model.vocabulary, provider="cpu")
+    from tests.patterns import bench_tokens
+    toks = bench_tokens(1 + (args.warmup + args.steps) * per_step, model.vocabulary)
+    s.run(toks[:1])
+    pos = 1
+    for _ in range(args.warmup):
+        for _ in range(per_step):
+            s.run(toks[pos:pos + 1]); pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for _ in range(per_step):
+            s.run(toks[pos:pos + 1]); pos += 1
+    elapsed = time.perf_counter() - t0
+    value = args.steps * per_step / elapsed
+    s.close()
+    line = {"impl": "reference", "metric": "8B Q4_K decode tok/s (bs1)", "value": round(value, 3), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(elapsed * 1000 / args.steps, 2), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "q4_k weights, fp32 (engine CPU provider)",
+            "data": "synthetic (seeded random-init weights)",
+            "config": {"workload": "8B-class Llama decode, batch 1 (bounded CPU sample: %d tokens per step)" % per_step},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
+                             "sample": "%d decode tokens per step through nya_llm_session_run with the engine's "
+                                       "cpu provider, positions 1..%d" % (per_step, pos)},
+            "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="fyodor", choices=["fyodor", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--ref-tokens", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_provider(args)
+
+
+if __name__ == "__main__":
+    main()

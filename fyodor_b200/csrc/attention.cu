@@ -1,0 +1,248 @@
+// attention.cu - split-K GQA decode attention over the fp16 KV cache.
+//
+// For every sequence s, KV head kh and its G = heads/kv_heads query heads:
+//   out[h] = sum_t softmax_t(q_h . k_t * scale) v_t   over t in [0, L_s)
+// (reference: the engine's scalar loop, backend/core/llm_cpu.c:510-535, and
+// nya_attention_split/_combine, CUDA/resident.cu:175-269, which keep F32 KV
+// and materialize the score row in global memory).
+//
+// Here the context of each (s, kh) is cut into `splits` partitions, one CTA
+// each. A CTA streams its partition of K and V once, keeps an online softmax
+// (running max, running sum, unnormalized output) per query head in
+// registers, and writes {m, l, o[hd]} per head to a scratch slot. The CTA
+// that finishes last for (s, kh) - an atomic counter, no waiting - merges the
+// slots in partition order and writes the normalized output, so the result
+// does not depend on scheduling. Nothing of size L is materialized.
+//
+// Inside a CTA each warp takes 32 positions at a time: lane j computes the
+// full 128-wide dot products of position j with all G query heads (K row read
+// as 16-byte vectors, query broadcast from shared memory), the warp updates
+// the online softmax, then the lanes switch to 4 output dimensions each and
+// accumulate p * v over the 32 positions.
+#include "common.cuh"
+#include "kernels.h"
+#include <cfloat>
+
+namespace fyb {
+
+constexpr int AT_WARPS = 4;
+constexpr int AT_THREADS = AT_WARPS * 32;
+
+struct AtParams {
+    const float *q;
+    const __half *k, *v;
+    unsigned long long seq_stride;
+    const unsigned *lengths, *request;
+    unsigned length, heads, kv_heads, capacity, splits;
+    float scale;
+    float *out;
+    float *partials;
+    unsigned *counters;
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
+{
+    constexpr int DPL = HD / 32;  // output dims per lane
+    __shared__ __align__(16) float qs[G][HD];
+    __shared__ __align__(16) float pbuf[AT_WARPS][32][G];
+    __shared__ float wm[AT_WARPS][G], wl[AT_WARPS][G];
+    __shared__ __align__(16) float wo[AT_WARPS][G][HD];
+    __shared__ unsigned last_flag;
+
+    const unsigned sp = blockIdx.x, kh = blockIdx.y, seq = blockIdx.z;
+    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+    pdl_launch_dependents();
+    pdl_wait();
+    unsigned L = p.length;
+    if (p.lengths) L = p.lengths[seq];
+    else if (p.request) L = p.request[1] + 1;
+    const unsigned chunk = (L + p.splits - 1) / p.splits;
+    const unsigned c0 = min(L, sp * chunk), c1 = min(L, c0 + chunk);
+
+    const __half *K = p.k + seq * p.seq_stride + (size_t)kh * p.capacity * HD;
+    const __half *V = p.v + seq * p.seq_stride + (size_t)kh * p.capacity * HD;
+    const float *qg = p.q + ((size_t)seq * p.heads + (size_t)kh * G) * HD;
+    for (unsigned i = threadIdx.x; i < G * HD; i += AT_THREADS) qs[i / HD][i % HD] = qg[i];
+    __syncthreads();
+
+    float m[G], l[G], o[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY; l[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) o[g][e] = 0.f;
+    }
+
+    for (unsigned base = c0 + warp * 32; base < c1; base += AT_WARPS * 32) {
+        const unsigned t = base + lane;
+        const bool valid = t < c1;
+        float s[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) s[g] = 0.f;
+        if (valid) {
+            const uint4 *krow = reinterpret_cast<const uint4 *>(K + (size_t)t * HD);
+#pragma unroll 4
+            for (int c = 0; c < HD / 8; ++c) {
+                uint4 kk = __ldg(krow + c);
+                const __half2 *h2 = reinterpret_cast<const __half2 *>(&kk);
+                float kf[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float2 f2 = __half22float2(h2[e]);
+                    kf[2 * e] = f2.x; kf[2 * e + 1] = f2.y;
+                }
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][8 * c]);
+                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][8 * c + 4]);
+                    float acc = s[g];
+                    acc = fmaf(qa.x, kf[0], acc); acc = fmaf(qa.y, kf[1], acc);
+                    acc = fmaf(qa.z, kf[2], acc); acc = fmaf(qa.w, kf[3], acc);
+                    acc = fmaf(qb.x, kf[4], acc); acc = fmaf(qb.y, kf[5], acc);
+                    acc = fmaf(qb.z, kf[6], acc); acc = fmaf(qb.w, kf[7], acc);
+                    s[g] = acc;
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float sv = valid ? s[g] * p.scale : -INFINITY;
+            const float mt = warp_max(sv);
+            const float mn = fmaxf(m[g], mt);
+            const float alpha = mn == -INFINITY ? 1.f : expf(m[g] - mn);
+            const float pv = valid ? expf(sv - mn) : 0.f;
+            l[g] = l[g] * alpha + warp_sum(pv);
+            m[g] = mn;
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) o[g][e] *= alpha;
+            pbuf[warp][lane][g] = pv;
+        }
+        __syncwarp();
+        const unsigned n = min(32u, c1 - base);
+        for (unsigned j = 0; j < n; ++j) {
+            const __half *vrow = V + (size_t)(base + j) * HD + lane * DPL;
+            float vf[DPL];
+            if constexpr (DPL == 4) {
+                uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vrow));
+                float2 a = __half22float2(*reinterpret_cast<__half2 *>(&vv.x));
+                float2 b = __half22float2(*reinterpret_cast<__half2 *>(&vv.y));
+                vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
+            } else {
+                unsigned vv = __ldg(reinterpret_cast<const unsigned *>(vrow));
+                float2 a = __half22float2(*reinterpret_cast<__half2 *>(&vv));
+                vf[0] = a.x; vf[1] = a.y;
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float pj = pbuf[warp][j][g];
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pj, vf[e], o[g][e]);
+            }
+        }
+        __syncwarp();
+    }
+
+    // merge the warps of this CTA
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        if (lane == 0) { wm[warp][g] = m[g]; wl[warp][g] = l[g]; }
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) wo[warp][g][lane * DPL + e] = o[g][e];
+    }
+    __syncthreads();
+    const size_t pair = (size_t)seq * p.kv_heads + kh;
+    float *slot = p.partials + (pair * p.splits + sp) * (size_t)(G * (HD + 2));
+    for (unsigned i = threadIdx.x; i < G * HD; i += AT_THREADS) {
+        const unsigned g = i / HD, d = i % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < AT_WARPS; ++w) M = fmaxf(M, wm[w][g]);
+        float acc = 0.f, den = 0.f;
+        for (int w = 0; w < AT_WARPS; ++w) {
+            const float f = wm[w][g] == -INFINITY ? 0.f : expf(wm[w][g] - M);
+            acc += wo[w][g][d] * f;
+            den += wl[w][g] * f;
+        }
+        slot[g * (HD + 2) + d] = acc;
+        if (d == 0) { slot[g * (HD + 2) + HD] = M; slot[g * (HD + 2) + HD + 1] = den; }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned old = atomicAdd(p.counters + pair, 1u);
+        last_flag = old == p.splits - 1;
+    }
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    const float *all = p.partials + pair * p.splits * (size_t)(G * (HD + 2));
+    for (unsigned i = threadIdx.x; i < G * HD; i += AT_THREADS) {
+        const unsigned g = i / HD, d = i % HD;
+        float M = -INFINITY;
+        for (unsigned s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, __ldcg(all + s2 * (G * (HD + 2)) + g * (HD + 2) + HD));
+        float acc = 0.f, den = 0.f;
+        for (unsigned s2 = 0; s2 < p.splits; ++s2) {
+            const float *sl = all + s2 * (G * (HD + 2)) + g * (HD + 2);
+            const float ms = __ldcg(sl + HD);
+            const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+            acc += __ldcg(sl + d) * f;
+            den += __ldcg(sl + HD + 1) * f;
+        }
+        p.out[((size_t)seq * p.heads + (size_t)kh * G + g) * HD + d] = acc / den;
+    }
+    if (threadIdx.x == 0) p.counters[pair] = 0;
+}
+
+size_t attention_workspace_bytes(const AttentionLaunch &L)
+{
+    const unsigned G = L.heads / L.kv_heads;
+    size_t pairs = (size_t)L.nseq * L.kv_heads;
+    size_t partial = pairs * L.splits * G * (L.head_dim + 2) * sizeof(float);
+    return (partial + 255) / 256 * 256 + (pairs * sizeof(unsigned) + 255) / 256 * 256;
+}
+
+template <int HD, int G>
+static cudaError_t launch_at(const AtParams &p, dim3 grid, cudaStream_t s, bool pdl)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(AT_THREADS);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attention_kernel<HD, G>, p);
+}
+
+int launch_attention(const AttentionLaunch &L, cudaStream_t s)
+{
+    if (!L.q || !L.k || !L.v || !L.out || L.kv_heads == 0 || L.heads % L.kv_heads || L.splits == 0 ||
+        L.capacity == 0 || L.nseq == 0)
+        return -1;
+    const unsigned G = L.heads / L.kv_heads;
+    if (!L.workspace || L.workspace_bytes < attention_workspace_bytes(L)) return -1;
+    AtParams p;
+    p.q = L.q; p.k = L.k; p.v = L.v;
+    p.seq_stride = L.seq_stride;
+    p.lengths = L.lengths; p.request = L.request; p.length = L.length;
+    p.heads = L.heads; p.kv_heads = L.kv_heads; p.capacity = L.capacity; p.splits = L.splits;
+    p.scale = L.scale;
+    p.out = L.out;
+    size_t pairs = (size_t)L.nseq * L.kv_heads;
+    size_t partial = (pairs * L.splits * G * (L.head_dim + 2) * sizeof(float) + 255) / 256 * 256;
+    p.partials = (float *)L.workspace;
+    p.counters = (unsigned *)((unsigned char *)L.workspace + partial);
+    dim3 grid(L.splits, L.kv_heads, L.nseq);
+    cudaError_t e = cudaErrorInvalidValue;
+#define FYB_AT(HDV, GV) if (L.head_dim == HDV && G == GV) e = launch_at<HDV, GV>(p, grid, s, L.pdl);
+    FYB_AT(128, 1) FYB_AT(128, 2) FYB_AT(128, 4) FYB_AT(128, 8)
+    FYB_AT(64, 1) FYB_AT(64, 2) FYB_AT(64, 4) FYB_AT(64, 8)
+#undef FYB_AT
+    if (e == cudaErrorInvalidValue) return -1;
+    return e == cudaSuccess ? 0 : -2;
+}
+
+}  // namespace fyb

@@ -1,0 +1,126 @@
+/* fyodor_b200.h - C ABI of the B200 provider for the Fyodor inference engine.
+ *
+ * The engine binds exactly one symbol, the provider vtable:
+ *
+ *   const nya_backend_interface *nya_cuda_backend(void);
+ *
+ * which replaces the reference provider's export in CUDA/cuda.c:457-462 and is
+ * registered by backend/core/compute.c:7-9,25-27 when the engine is built with
+ * NYA_ENABLE_CUDA. Its fields follow backend/include/compute_backend.h:12-29;
+ * every return convention is the engine's (0 = output ready, -1 = decline or
+ * failure, NULL plan = run the CPU reference).
+ *
+ * The fyb_* functions below are extensions for tools, tests and benchmarks
+ * that need device-level access (no counterpart in the reference unless a
+ * line says otherwise). They take plain pointers and sizes; "stream" is a
+ * cudaStream_t passed as void* (NULL = the legacy default stream). Device
+ * entry points return 0 on success, -1 for invalid arguments (nothing is
+ * launched) and -2 for a CUDA launch failure.
+ */
+#ifndef FYODOR_B200_H
+#define FYODOR_B200_H
+
+#include "fyodor_b200_abi.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Provider vtable. Replaces CUDA/cuda.c:457-462 (nya_cuda_backend). */
+const nya_backend_interface *nya_cuda_backend(void);
+
+/* Library identification (no counterpart in the reference). */
+const char *fyb_version(void);
+/* Number of CUDA devices visible to this process; 0 when none. */
+int fyb_device_count(void);
+
+/* ---- device-level kernels ---------------------------------------------- */
+
+/* out[i] = value i of a GGUF tensor, bit-exact with the engine's
+   nya_llm_tensor_value (backend/core/llm_quant.c:91-142). Device pointers. */
+int fyb_dequantize(const void *weights, size_t count, unsigned type, float *out, void *stream);
+
+/* Scratch needed by fyb_quant_matmul for one shape (bytes; 0 when none). */
+size_t fyb_quant_matmul_workspace(size_t rows, size_t columns, unsigned type, size_t batch);
+
+/* Y[b][r] = sum_k W[r][k] * X[b][k] on the device, the batched form of the
+   engine's nya_compute_matmul_typed (backend/include/compute.h:80-83): W in
+   GGUF row-major block storage, X batch-major [batch][columns], Y
+   [batch][rows]. Q4_K/Q6_K with batch <= 2 run the tensor-core GEMV; every
+   other case runs the type-generic kernel. `workspace` must hold
+   fyb_quant_matmul_workspace() bytes, all zero before the first call; calls
+   leave it zeroed. Q6_K weights are repacked into the workspace's tail on
+   every call, so this entry point is for testing, not a hot loop (plans
+   repack once). */
+int fyb_quant_matmul(const void *weights, size_t rows, size_t columns, unsigned type,
+    const float *x, float *y, size_t batch, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Decode attention over an fp16 KV cache for a ragged batch of sequences
+   (no reference counterpart at this level; the engine's semantics are
+   backend/core/llm_cpu.c:510-535 with an F32 cache).
+   q   [nseq][heads][head_dim] f32, out [nseq][heads][head_dim] f32
+   k,v per sequence s at k + s*seq_stride: [kv_heads][capacity][head_dim] f16
+   lengths[s] = attended positions of sequence s (device array, 1..capacity).
+   splits = context partitions per (sequence, kv head); 0 picks a default.
+   workspace: fyb_attention_workspace() bytes, zero before the first call. */
+size_t fyb_attention_workspace(unsigned nseq, unsigned heads, unsigned kv_heads, unsigned head_dim, unsigned splits);
+int fyb_attention_decode(const float *q, const void *k_cache, const void *v_cache, size_t seq_stride,
+    const unsigned *lengths, unsigned nseq, unsigned heads, unsigned kv_heads, unsigned head_dim,
+    unsigned capacity, float scale, float *out, unsigned splits, void *workspace, size_t workspace_bytes,
+    void *stream);
+
+/* ---- resident plans ---------------------------------------------------- */
+
+/* Greedy decode entirely on the device: starting from `token` at `position`,
+   run `steps` tokens, each taking the argmax of the previous logits (first
+   index of the maximum, as nya_llm_sample with temperature 0 does,
+   backend/core/llm_cpu.c:896-905). tokens_out[i] receives the i-th generated
+   token. `plan` is a state returned by the vtable's plan_create. */
+int fyb_plan_decode_greedy(void *plan, uint32_t token, size_t position, size_t steps, uint32_t *tokens_out);
+
+/* Times `steps` device-side greedy steps with CUDA events on the plan's
+   stream (no host synchronization between steps); returns milliseconds or
+   a negative value on failure. */
+double fyb_plan_time_greedy(void *plan, uint32_t token, size_t position, size_t steps);
+
+/* Kernel launches issued per decode step by the plan (graph nodes). */
+unsigned long long fyb_plan_launches_per_token(const void *plan);
+
+/* Average duration (ms) of each kernel class of one decode step measured
+   with CUDA events around eager launches: out[0] matrix kernels, out[1]
+   attention, out[2] other. Returns 0 on success. */
+int fyb_plan_profile(void *plan, uint32_t token, size_t position, size_t steps, double *out);
+
+/* Average milliseconds of one stand-alone launch of a fused projection
+   kernel of `layer` (which: 0 QKV+RoPE+KV append, 1 attention output,
+   2 gate/up+SwiGLU, 3 down, 4 logits+argmax), timed over `reps` launches
+   with CUDA events; *bytes receives the kernel's algorithmic bytes per
+   launch (weights, input vector, norm weights, outputs). */
+double fyb_plan_time_projection(void *plan, unsigned layer, unsigned which, unsigned reps, size_t *bytes);
+
+/* ---- synthetic GGUF-layout models (no reference counterpart) -------------
+   Builds an in-memory model in the engine's own binding layout
+   (backend/core/llm_gguf.c:1013-1118): LLaMA tensors, block formats as
+   given, random contents drawn from a seeded counter-based generator. */
+typedef struct fyb_synth_config {
+    uint32_t layers, embedding, heads, kv_heads, feed_forward, vocabulary, context;
+    uint32_t matrix_type;   /* type of q/k/v/o/gate/up/down */
+    uint32_t embed_type;    /* token_embd */
+    uint32_t output_type;   /* output */
+    float rope_base, epsilon;
+    uint64_t seed;
+    int norm_mode;          /* 0: all ones, 1: N(1, 0.01), 2: N(0, 1) */
+    int threads;            /* host threads for filling; 0 = all cores */
+    int centered;           /* Q4_K only: choose each group's min so its mean
+                               weight is near zero (mins then are not uniform) */
+} fyb_synth_config;
+nya_llm_context *fyb_synth_create(const fyb_synth_config *config);
+void fyb_synth_free(nya_llm_context *model);
+/* Fill `bytes` of one tensor the way fyb_synth_create does (type-aware
+   values: uniform quants, |N(0,1)|*0.01 fp16 scales). */
+void fyb_synth_fill(void *data, size_t rows, size_t columns, uint32_t type, uint64_t seed, uint64_t stream_id);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,126 @@
+"""GPU parity of the quantized matvec / small-batch matmul through the C ABI.
+
+Oracle: the engine's scalar kernel (oracle.matvec, pinned bit-exact to the
+compiled engine) plus the double-precision forward-error bound of
+test_quant_kernels.c:13-25 (|a - s| <= 1e-6 * (1 + sum |w x|)). Full-size
+projection shapes use the north-star bound |a - e| <= 1e-3 * (1 + |e|).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import fyodor_b200 as F
+import oracle as O
+from tests.patterns import k_quant_blocks, quant_kernel_inputs, quant_kernel_weights
+
+pytestmark = pytest.mark.gpu
+TYPES = [F.F32, F.F16, F.BF16, F.Q4_0, F.Q8_0, F.Q4_K, F.Q6_K]
+
+
+def double_bound_ok(values, x, actual):
+    prod = values.astype(np.float64) * x.astype(np.float64)
+    s = prod.sum(axis=-1)
+    mag = np.abs(prod).sum(axis=-1)
+    return np.all(np.isfinite(actual)) and np.all(np.abs(actual.astype(np.float64) - s) <= 1e-6 * (1 + mag))
+
+
+@pytest.mark.parametrize("type_id", TYPES)
+def test_matvec_quant_kernel_patterns(provider, type_id):
+    rows, cols = 65, 1024
+    data = quant_kernel_weights(type_id, rows, cols)
+    values = O.dequantize(data, type_id, rows * cols).reshape(rows, cols)
+    for p in range(3):
+        x = quant_kernel_inputs(cols, p)
+        y = provider.matvec(data, rows, cols, type_id, x)
+        assert y is not None
+        assert double_bound_ok(values, x, y)
+        e = O.matvec(data, type_id, x, cols, rows)
+        assert np.all(np.abs(y[:17] - e[:17]) <= 1.5e-4 * (1 + np.abs(e[:17])))
+
+
+@pytest.mark.parametrize("type_id", TYPES)
+@pytest.mark.parametrize("batch", [2, 3, 17, 65])
+def test_matmul_batches(provider, type_id, batch):
+    rows, cols = 65, 1024
+    data = quant_kernel_weights(type_id, rows, cols)
+    values = O.dequantize(data, type_id, rows * cols).reshape(rows, cols)
+    xs = (((np.arange(batch * cols) % 61) - 30) / 31).astype(np.float32).reshape(batch, cols)
+    y = provider.matmul(data, rows, cols, type_id, xs, batch)
+    assert y is not None
+    for b in range(batch):
+        assert double_bound_ok(values, xs[b], y[b]), b
+
+
+@pytest.mark.parametrize("kind,type_id", [(0, F.Q4_K), (1, F.Q6_K)])
+def test_k_quant_matvec_exact(provider, kind, type_id):
+    """check_k_quants: the CUDA matvec must equal the double dot exactly."""
+    data, expected = k_quant_blocks(kind)
+    x = np.array([((i % 23) - 11) / 16.0 for i in range(512)], np.float32)
+    y = provider.matvec(data, 2, 512, type_id, x)
+    dot = expected.reshape(2, 512).astype(np.float64) @ x.astype(np.float64)
+    assert (y.astype(np.float64) == dot).all()
+
+
+def test_boundary_rejections(provider):
+    """test_compute.c:99-106: invalid sizes decline with -1 before any write."""
+    api, st = provider.api, provider.state
+    w = np.ones(4, np.float32)
+    x = np.ones(4, np.float32)
+    y = np.full(4, 7.0, np.float32)
+    P = lambda a: C.c_void_p(a.ctypes.data)
+    assert api.matvec(st, P(w), (1 << 64) - 1, 2, 0, P(x), P(y)) == -1
+    assert api.matvec(st, P(w), 0, 2, 0, P(x), P(y)) == -1
+    assert api.matvec(st, None, 1, 1, 0, P(x), P(y)) == -1
+    assert api.matvec(st, P(w), 1, 255, F.Q4_K, P(x), P(y)) == -1  # columns not a block multiple
+    assert api.matvec(st, P(w), 1, 4, 99, P(x), P(y)) == -1        # unknown storage type
+    assert api.matmul(st, P(w), 1, 4, 0, P(x), P(y), 513) == -1     # batch above 512
+    assert (y == 7.0).all()
+    assert provider.active()
+
+
+def test_cached_weight_reuse_and_resizing(provider):
+    """test_compute.c:57-85: alternate buffers and shapes through the cache."""
+    small = (np.arange(6) / 10.0).astype(np.float32)
+    large = (((np.arange(325) % 17) - 8) / 19.0).astype(np.float32)
+    for p in range(6):
+        rows, cols, w = (2, 3, small) if p % 2 == 0 else (5, 65, large)
+        x = ((np.arange(cols) + p) / 71.0).astype(np.float32)
+        y = provider.matvec(w, rows, cols, F.F32, x)
+        e = w.reshape(rows, cols).astype(np.float64) @ x.astype(np.float64)
+        assert np.all(np.abs(y - e) <= 1e-4 * (1 + np.abs(e)))
+
+
+SWEEP = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+
+
+@pytest.mark.parametrize("type_id", [F.Q4_K, F.Q6_K])
+@pytest.mark.parametrize("rows,cols", SWEEP)
+def test_projection_sweep(provider, type_id, rows, cols):
+    """C2 shapes with BASELINE value distributions; batches 1, 2 and 4."""
+    nbytes = rows * F.row_bytes(type_id, cols)
+    data = np.empty(nbytes, np.uint8)
+    F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, type_id, 2024, rows * 7 + cols)
+    rng = np.random.default_rng(rows + cols)
+    for batch in (1, 2, 4):
+        xs = rng.standard_normal((batch, cols)).astype(np.float32)
+        y = provider.matmul(data, rows, cols, type_id, xs, batch)
+        assert y is not None
+        for b in range(batch):
+            e = O.matvec(data, type_id, xs[b], cols, rows)
+            err = np.abs(y[b] - e) / (1 + np.abs(e))
+            assert err.max() <= 1e-3, (batch, b, float(err.max()))
+
+
+def test_dequantize_bit_exact_all_types():
+    import torch
+    for type_id in [F.F32, F.F16, F.BF16, F.Q4_0, F.Q8_0, F.Q4_K, F.Q6_K]:
+        rows, cols = 33, 1024
+        data = quant_kernel_weights(type_id, rows, cols)
+        expected = O.dequantize(data, type_id, rows * cols)
+        d = torch.from_numpy(data).cuda()
+        out = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+        assert F.lib.fyb_dequantize(C.c_void_p(d.data_ptr()), rows * cols, type_id, C.c_void_p(out.data_ptr()), None) == 0
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        assert (got.view(np.uint32) == expected.view(np.uint32)).all(), type_id

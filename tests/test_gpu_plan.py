@@ -1,0 +1,140 @@
+"""GPU parity of the resident plan (full decode) through the provider vtable.
+
+Two oracles per model: the restated engine with an fp16 KV cache (same
+cache semantics as the provider; tight bound) and the compiled engine's F32
+KV logits stored in tests/golden/small_models.npz (scaled error bound 1e-3
+of test_inference.c:219). Greedy tokens must match the fp16-KV oracle."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import fyodor_b200 as F
+import oracle as O
+from tests.conftest import ROOT
+from tests.patterns import SMALL_MODELS, bench_tokens
+
+pytestmark = pytest.mark.gpu
+GOLD = np.load(os.path.join(ROOT, "tests", "golden", "small_models.npz"))
+
+
+def scaled_error(a, b):
+    return float(np.max(np.abs(a - b) / (1 + np.abs(b))))
+
+
+@pytest.mark.parametrize("name,cfg,tokens", SMALL_MODELS)
+def test_plan_logits(provider, name, cfg, tokens):
+    m = F.SynthModel(**cfg)
+    plan = provider.plan(m, len(tokens))
+    assert plan is not None
+    ref16 = O.Session(m.ptr, len(tokens), m.vocabulary, kv_f16=True)
+    for i, t in enumerate(tokens):
+        assert plan.token(t, i) == 0
+        got = plan.logits.copy()
+        e16 = ref16.forward(t, i)
+        assert scaled_error(got, e16) <= 1e-3, (i, scaled_error(got, e16))
+        assert scaled_error(got, GOLD[name + "_logits"][i]) <= 1e-3, i
+        assert np.argmax(got) == np.argmax(e16)
+    kv = plan.read_kv(cfg["layers"] - 1, 0, len(tokens))
+    k16, v16 = ref16.read_kv(cfg["layers"] - 1, 0, len(tokens), m.kv_dim)
+    assert scaled_error(kv[0], k16) <= 2e-3 and scaled_error(kv[1], v16) <= 2e-3
+    st = plan.stats()
+    assert st["graph_captures"] == 1 and st["graph_replays"] == len(tokens)
+    assert st["kv_bytes"] == cfg["layers"] * m.kv_dim * len(tokens) * 2 * 2
+
+
+@pytest.mark.parametrize("name,cfg,tokens", SMALL_MODELS)
+def test_greedy_64_steps(provider, name, cfg, tokens):
+    cfg = dict(cfg, context=80)
+    m = F.SynthModel(**cfg)
+    plan = provider.plan(m, 80)
+    ref16 = O.Session(m.ptr, 80, m.vocabulary, kv_f16=True)
+    first = tokens[0]
+    got = plan.decode_greedy(first, 0, 64)
+    assert got is not None
+    t, expected = first, []
+    for i in range(64):
+        t = O.argmax(ref16.forward(t, i))
+        expected.append(t)
+    assert list(got) == expected
+
+
+def test_prefill_then_decode_matches_tokens(provider):
+    name, cfg, tokens = SMALL_MODELS[0]
+    m = F.SynthModel(**cfg)
+    a = provider.plan(m, 32)
+    b = provider.plan(m, 32)
+    assert a.prefill(np.array(tokens[:8], np.uint32), 0) == 0
+    la = a.logits.copy()
+    for i, t in enumerate(tokens[:8]):
+        assert b.token(t, i, logits=(i == 7)) == 0
+    assert scaled_error(la, b.logits) <= 1e-6
+    assert a.token(tokens[8], 8) == 0 and b.token(tokens[8], 8) == 0
+    assert scaled_error(a.logits, b.logits) <= 1e-6
+
+
+def test_plan_argument_validation(provider):
+    name, cfg, tokens = SMALL_MODELS[0]
+    m = F.SynthModel(**cfg)
+    p = provider.plan(m, 16)
+    assert p.token(m.vocabulary, 0) == -1        # token outside the vocabulary
+    assert p.token(1, 3) == -1                   # skips positions 0..2
+    assert p.token(1, 16) == -1                  # beyond capacity
+    assert p.api.plan_token(p.ptr, 1, 0, 1, None) == -1  # logits without output
+    assert p.token(1, 0) == 0                    # still usable afterwards
+    assert provider.plan(m, m.config.context + 1) is None  # capacity above the model context
+    assert p.read_kv(0, 0, 2) is None            # only the valid prefix is readable
+
+
+def test_8b_layer_shapes(provider):
+    """Two layers at the 8B geometry (d 4096, 32/8 heads, FFN 14336, V 128256)."""
+    m = F.SynthModel(layers=2, embedding=4096, heads=32, kv_heads=8, feed_forward=14336, vocabulary=128256,
+                     context=16, seed=99, norm_mode=2, centered=1)
+    plan = provider.plan(m, 8)
+    ref16 = O.Session(m.ptr, 8, m.vocabulary, kv_f16=True)
+    for i, t in enumerate(bench_tokens(3, m.vocabulary)):
+        assert plan.token(int(t), i) == 0
+        e = ref16.forward(int(t), i)
+        assert scaled_error(plan.logits, e) <= 1e-3, i
+
+
+def _env_run(code, **env):
+    e = dict(os.environ, **{k: str(v) for k, v in env.items()})
+    return subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=e, capture_output=True, text=True, timeout=300)
+
+
+def test_fail_after_injection():
+    """NYA_CUDA_FAIL_AFTER=N fails the step at position N (resident.inc:192-198)."""
+    code = ("import fyodor_b200 as F\n"
+            "m=F.SynthModel(layers=1,embedding=512,heads=4,kv_heads=2,feed_forward=512,vocabulary=256,context=8)\n"
+            "p=F.Provider().plan(m,8)\n"
+            "print([p.token(3,i) for i in range(4)])\n")
+    r = _env_run(code, NYA_CUDA_FAIL_AFTER=2)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.strip() == "[0, 0, -1, -1]"
+
+
+def test_allocation_failure_injection():
+    """NYA_CUDA_FAIL_ALLOCATION_AFTER=N declines the plan and rolls back."""
+    code = ("import fyodor_b200 as F\n"
+            "m=F.SynthModel(layers=1,embedding=512,heads=4,kv_heads=2,feed_forward=512,vocabulary=256,context=8)\n"
+            "pr=F.Provider(); print(pr.plan(m,8) is None, pr.active())\n")
+    r = _env_run(code, NYA_CUDA_FAIL_ALLOCATION_AFTER=3)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.strip() == "True True"
+
+
+def test_graphs_disabled_matches():
+    code = ("import fyodor_b200 as F, numpy as np\n"
+            "m=F.SynthModel(layers=2,embedding=512,heads=4,kv_heads=2,feed_forward=512,vocabulary=256,context=8,seed=4)\n"
+            "p=F.Provider().plan(m,8)\n"
+            "out=[]\n"
+            "for i in range(4):\n"
+            "    p.token(5+i,i); out.append(p.logits.copy())\n"
+            "np.save('/tmp/fyb_graphs.npy' if __import__('os').environ.get('NYA_CUDA_GRAPHS','1')!='0' else '/tmp/fyb_eager.npy', np.stack(out))\n")
+    assert _env_run(code).returncode == 0
+    assert _env_run(code, NYA_CUDA_GRAPHS=0).returncode == 0
+    a, b = np.load("/tmp/fyb_graphs.npy"), np.load("/tmp/fyb_eager.npy")
+    assert (a == b).all()
