@@ -171,13 +171,18 @@ class SynthModel:
 
 # ---------------------------------------------------------------- provider
 class Provider:
-    """A provider context: what nya_compute_create_for("cuda") owns."""
+    """A provider context: what nya_compute_create_for("cuda") owns.
+
+    Plans must be freed before their context (backend/include/compute.h:6-8);
+    close() frees any plan still alive first."""
 
     def __init__(self):
+        import weakref
         self.api = api()
         self.state = self.api.create()
         if not self.state:
             raise RuntimeError("the B200 provider declined (no sm_100 device visible)")
+        self._plans = weakref.WeakSet()
 
     def active(self):
         return bool(self.api.active(self.state))
@@ -196,10 +201,14 @@ class Provider:
         p = self.api.plan_create(self.state, C.c_void_p(model.ptr), capacity)
         if not p:
             return None
-        return Plan(self, p, model)
+        plan = Plan(self, p, model)
+        self._plans.add(plan)
+        return plan
 
     def close(self):
         if self.state:
+            for plan in list(self._plans):
+                plan.close()
             self.api.destroy(self.state)
             self.state = None
 

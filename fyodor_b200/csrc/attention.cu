@@ -205,6 +205,8 @@ size_t attention_workspace_bytes(const AttentionLaunch &L)
 template <int HD, int G>
 static cudaError_t launch_at(const AtParams &p, dim3 grid, cudaStream_t s, bool pdl)
 {
+    cudaFuncSetAttribute(attention_kernel<HD, G>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(AT_THREADS);

@@ -55,6 +55,47 @@ FYB_DEV unsigned ldg_stream_u1(const void *p)
 }
 FYB_DEV void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2::evict_last [%0];" :: "l"(p)); }
 
+// ---- mbarrier + bulk (TMA, non-tensor) copies into shared memory ----------
+FYB_DEV void mbar_init(uint64_t *bar, unsigned count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+FYB_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+FYB_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+FYB_DEV void mbar_expect_tx(uint64_t *bar, unsigned bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+FYB_DEV bool mbar_try_wait(uint64_t *bar, unsigned phase)
+{
+    unsigned ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(phase) : "memory");
+    return ok != 0;
+}
+// Waits for the phase with an iteration bound; false means the copy never
+// landed (the caller raises ERR_TIMEOUT instead of spinning forever).
+FYB_DEV bool mbar_wait_bounded(uint64_t *bar, unsigned phase)
+{
+    for (unsigned i = 0; i < (1u << 22); ++i)
+        if (mbar_try_wait(bar, phase)) return true;
+    return false;
+}
+// global -> shared bulk copy completing on `bar`; both addresses 16-byte
+// aligned and `bytes` a multiple of 16. Weights are streamed once: evict first.
+FYB_DEV void bulk_copy_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar)
+{
+    asm volatile(
+        "{\n .reg .b64 pol;\n createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n"
+        " cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], pol;\n}\n"
+        :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+FYB_DEV void ldmatrix_x4(unsigned (&r)[4], const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
+}
+
 // L2-coherent loads for data produced by other CTAs of the same launch.
 FYB_DEV float ldcg_f32(const float *p) { return __ldcg(p); }
 

@@ -18,35 +18,31 @@ int launch_gather_batch(const void *w, size_t row_bytes, unsigned type, size_t n
     unsigned count, float *out, cudaStream_t s);
 
 // ---------------------------------------------------------------- qgemv.cu
-// Device layout of a K-quant matrix used by the tensor-core GEMV.
-//   Q4_K: the GGUF bytes unchanged (rows x nblk x 144 B).
-//   Q6_K: repacked by repack_q6k(): three regions
-//         bits  rows x nblk x 192 B   (ql 128 + qh 64 per block; inside every
-//                                       32-byte run the bytes are interleaved
-//                                       [0-3,16-19,4-7,20-23,8-11,24-27,12-15,28-31])
-//         scale rows x nblk x 16 B    (the int8 sub-block scales)
-//         d     rows x nblk x 4 B     (the fp16 super-block scale widened to f32)
-struct QMatrix {
-    const unsigned char *bits = nullptr;
-    const signed char *scales = nullptr;
-    const float *d = nullptr;
-    unsigned rows = 0;
-    unsigned cols = 0;
-    unsigned type = 0;
+// Tensor-core GEMV weights: Q4_K / Q6_K matrices repacked into units of
+// 16 rows x 256 columns, unit (tile t, block b) at units + (t*nblk + b)*unit,
+// unit = 2304 B (Q4_K) or 3360 B (Q6_K). A fused matrix stacks the tiles of
+// several tensors (REPACK_QKV puts rows 2i and 2i+1 of every 16-row tile in
+// the same lane; REPACK_GATEUP interleaves 8 gate rows with 8 up rows).
+enum RepackMode { REPACK_PLAIN = 0, REPACK_QKV = 1, REPACK_GATEUP = 2 };
+struct QWeights {
+    const unsigned char *units = nullptr;
+    unsigned type = 0, cols = 0, tiles = 0;
 };
-size_t q6k_repacked_bytes(size_t rows, size_t cols);
-int repack_q6k(const void *raw, size_t rows, size_t cols, void *dst, QMatrix *out, cudaStream_t s);
-QMatrix q4k_matrix(const void *raw, size_t rows, size_t cols);
+size_t qunits_bytes(unsigned type, size_t tiles, size_t cols);
+// Repack `tiles` tiles of a raw GGUF matrix (rows x cols, device memory) into
+// dst_units; REPACK_GATEUP reads the up rows from src1.
+int repack_units(const void *src0, const void *src1, size_t rows, size_t cols, unsigned type, int mode,
+    void *dst_units, size_t tiles, cudaStream_t s);
 
 enum QgEpilogue { EPI_STORE = 0, EPI_QKV = 1, EPI_SWIGLU = 2, EPI_LOGITS = 3 };
 
-// One fused GEMV launch. Up to three matrices ("segments") share the input
-// vector and are tiled independently (EPI_SWIGLU pairs segment 0 and 1 row
-// for row instead).
+// One fused GEMV launch over a repacked matrix whose tiles belong to up to
+// three output segments (QKV: q, k, v; SWIGLU: gate and up rows paired).
 struct QgemvLaunch {
     int epilogue = EPI_STORE;
+    QWeights w;
     int nseg = 1;
-    QMatrix seg[3];
+    unsigned seg_rows[3] = {0, 0, 0};
     float *out[3] = {nullptr, nullptr, nullptr};   // STORE/LOGITS/SWIGLU: out[0]; QKV: q
     __half *kcache = nullptr, *vcache = nullptr;   // QKV: this layer's [kv_heads][capacity][hd]
     size_t out_stride = 0;                          // per-vector output stride (floats)
@@ -67,14 +63,18 @@ struct QgemvLaunch {
     unsigned long long *argmax_key = nullptr;  // [nvec]
     unsigned *argmax_token = nullptr;          // [nvec] result token
     unsigned *tiles_done = nullptr;
-    // scratch for the stream-K fix-up (see qgemv_workspace_bytes)
-    void *workspace = nullptr;
-    size_t workspace_bytes = 0;
+    // stream-K scratch: per-tile counters (zero before the first launch;
+    // launches leave them zero) and partial sums
+    unsigned *counters = nullptr;
+    size_t counters_capacity = 0;  // entries
+    float *partials = nullptr;
+    size_t partials_bytes = 0;
     unsigned *error = nullptr;
     int grid = 0;       // CTAs (0: one per SM)
     bool pdl = false;   // programmatic dependent launch
 };
-size_t qgemv_workspace_bytes(const QgemvLaunch &L, int grid);
+unsigned qgemv_tiles(const QgemvLaunch &L);
+size_t qgemv_partials_bytes(const QgemvLaunch &L, int grid);
 int qgemv_supported(unsigned type, size_t cols, size_t nvec);
 int launch_qgemv(const QgemvLaunch &L, cudaStream_t s);
 

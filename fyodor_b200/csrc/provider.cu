@@ -83,9 +83,8 @@ struct CachedWeight {
     const void *source = nullptr;
     size_t rows = 0, cols = 0, bytes = 0;
     unsigned type = 0;
-    void *dev = nullptr;       // GGUF bytes
-    void *repacked = nullptr;  // Q6_K tensor-core layout
-    QMatrix qm;
+    void *dev = nullptr;  // GGUF bytes (generic types) or tensor-core units (K-quants)
+    QWeights qw;
 };
 
 struct Context {
@@ -96,8 +95,10 @@ struct Context {
     bool failed = false;
     float *dx = nullptr, *dy = nullptr;
     size_t dx_bytes = 0, dy_bytes = 0;
-    void *ws = nullptr;
-    size_t ws_bytes = 0;
+    unsigned *counters = nullptr;  // stream-K tile counters, kept zero between launches
+    size_t counters_bytes = 0;
+    float *partials = nullptr;
+    size_t partials_bytes = 0;
     int sms = 148;
 };
 
@@ -109,8 +110,8 @@ static void context_free(Context *c)
     {
         DeviceScope scope(c->device);
         if (c->stream) cudaStreamSynchronize(c->stream);
-        for (auto &w : c->weights) { cudaFree(w.dev); cudaFree(w.repacked); }
-        cudaFree(c->dx); cudaFree(c->dy); cudaFree(c->ws);
+        for (auto &w : c->weights) cudaFree(w.dev);
+        cudaFree(c->dx); cudaFree(c->dy); cudaFree(c->counters); cudaFree(c->partials);
         if (c->stream) cudaStreamDestroy(c->stream);
     }
     delete c;
@@ -154,11 +155,34 @@ static int grow(void **p, size_t *cap, size_t bytes, bool zero)
     if (*cap >= bytes) return 0;
     void *n = nullptr;
     if (cudaMalloc(&n, bytes) != cudaSuccess) { cudaGetLastError(); return -1; }
-    if (zero && cudaMemset(n, 0, bytes) != cudaSuccess) { cudaFree(n); return -1; }
+    if (zero && (cudaMemset(n, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)) { cudaFree(n); return -1; }
     if (*p) cudaFree(*p);
     *p = n;
     *cap = bytes;
     return 0;
+}
+
+// Tensor-core units of a raw device matrix (freed by the caller).
+static int repack_plain(const void *raw, size_t rows, size_t cols, unsigned type, void **units, QWeights *qw,
+    cudaStream_t s)
+{
+    const size_t tiles = (rows + 15) / 16;
+    if (cudaMalloc(units, qunits_bytes(type, tiles, cols)) != cudaSuccess) { cudaGetLastError(); return -1; }
+    if (repack_units(raw, nullptr, rows, cols, type, REPACK_PLAIN, *units, tiles, s) ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        cudaFree(*units); *units = nullptr; return -1;
+    }
+    qw->units = (const unsigned char *)*units; qw->type = type; qw->cols = (unsigned)cols; qw->tiles = (unsigned)tiles;
+    return 0;
+}
+
+// Host-to-device copy ordered on `s`. A plain cudaMemcpy from pageable memory
+// may return before its DMA lands and is ordered only on the legacy stream,
+// which the provider's non-blocking stream does not wait for (the reference
+// documents the same hazard in CUDA/cuda.c:399-403).
+static bool upload(void *dst, const void *src, size_t bytes, cudaStream_t s)
+{
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s) == cudaSuccess;
 }
 
 static CachedWeight *cached_weight(Context *c, const void *w, size_t rows, size_t cols, unsigned type, size_t bytes)
@@ -166,44 +190,56 @@ static CachedWeight *cached_weight(Context *c, const void *w, size_t rows, size_
     for (auto &e : c->weights)
         if (e.source == w && e.rows == rows && e.cols == cols && e.type == type) return &e;
     if (c->weights.size() >= WEIGHT_LIMIT) return nullptr;
-    size_t extra = type == T_Q6_K ? q6k_repacked_bytes(rows, cols) : 0;
-    if (bytes + extra > c->cache_limit - std::min(c->cache_limit, c->cached_bytes)) return nullptr;
+    const bool tc = qgemv_supported(type, cols, 1);
+    const size_t resident = tc ? qunits_bytes(type, (rows + 15) / 16, cols) : bytes;
+    if (resident > c->cache_limit - std::min(c->cache_limit, c->cached_bytes)) return nullptr;
     CachedWeight e;
-    e.source = w; e.rows = rows; e.cols = cols; e.type = type; e.bytes = bytes + extra;
-    if (cudaMalloc(&e.dev, bytes) != cudaSuccess) { cudaGetLastError(); return nullptr; }
-    if (cudaMemcpy(e.dev, w, bytes, cudaMemcpyHostToDevice) != cudaSuccess) { cudaFree(e.dev); return nullptr; }
-    if (type == T_Q4_K) e.qm = q4k_matrix(e.dev, rows, cols);
-    if (type == T_Q6_K && cols % 256 == 0) {
-        if (cudaMalloc(&e.repacked, extra) != cudaSuccess ||
-            repack_q6k(e.dev, rows, cols, e.repacked, &e.qm, c->stream) != 0) {
-            cudaGetLastError(); cudaFree(e.dev); cudaFree(e.repacked); return nullptr;
-        }
+    e.source = w; e.rows = rows; e.cols = cols; e.type = type; e.bytes = resident;
+    void *raw = nullptr;
+    if (cudaMalloc(&raw, bytes) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+    if (!upload(raw, w, bytes, c->stream)) { cudaFree(raw); return nullptr; }
+    if (tc) {
+        const int r = repack_plain(raw, rows, cols, type, &e.dev, &e.qw, c->stream);
+        cudaFree(raw);
+        if (r) return nullptr;
+    } else {
+        e.dev = raw;
     }
     c->cached_bytes += e.bytes;
     c->weights.push_back(e);
     return &c->weights.back();
 }
 
-// Shared device-side matmul on already-resident data.
-static int device_matmul(const QMatrix *qm, const void *raw, size_t row_bytes, size_t rows, size_t cols,
-    unsigned type, const float *x, float *y, size_t batch, void **ws, size_t *ws_bytes, cudaStream_t s, int sms)
+struct Scratch {
+    unsigned **counters;
+    size_t *counters_bytes;
+    float **partials;
+    size_t *partials_bytes;
+};
+
+// Y[b] = W X[b] on resident data; K-quants run the tensor-core GEMV two
+// vectors per launch, every other type the generic kernel.
+static int device_matmul(const QWeights *qw, const void *raw, size_t row_bytes, size_t rows, size_t cols,
+    unsigned type, const float *x, float *y, size_t batch, const Scratch &sc, cudaStream_t s, int sms)
 {
-    if (qm && qm->bits && qgemv_supported(type, cols, 1)) {
+    if (qw && qw->units) {
         for (size_t b0 = 0; b0 < batch; b0 += 2) {
+            if (!qgemv_supported(type, cols, std::min<size_t>(2, batch - b0))) return -1;
             QgemvLaunch L;
             L.epilogue = EPI_STORE;
-            L.nseg = 1;
-            L.seg[0] = *qm;
+            L.w = *qw;
+            L.seg_rows[0] = (unsigned)rows;
             L.nvec = (int)std::min<size_t>(2, batch - b0);
             L.x = x + b0 * cols;
             L.out[0] = y + b0 * rows;
             L.out_stride = rows;
             L.grid = sms;
-            size_t need = qgemv_workspace_bytes(L, sms);
-            if (ws_bytes && grow(ws, ws_bytes, need, true) != 0) return -2;
-            L.workspace = *ws;
-            L.workspace_bytes = ws_bytes ? *ws_bytes : need;
-            int r = launch_qgemv(L, s);
+            if (grow((void **)sc.counters, sc.counters_bytes, (size_t)qw->tiles * 4, true) ||
+                grow((void **)sc.partials, sc.partials_bytes, qgemv_partials_bytes(L, sms), false))
+                return -2;
+            L.counters = *sc.counters; L.counters_capacity = *sc.counters_bytes / 4;
+            L.partials = *sc.partials; L.partials_bytes = *sc.partials_bytes;
+            const int r = launch_qgemv(L, s);
             if (r) return r;
         }
         return 0;
@@ -231,8 +267,9 @@ static int context_matmul(Context *c, const void *w, size_t rows, size_t cols, u
             grow((void **)&c->dy, &c->dy_bytes, rows * batch * sizeof(float), false))
             break;
         if (cudaMemcpyAsync(c->dx, x, cols * batch * sizeof(float), cudaMemcpyHostToDevice, c->stream) != cudaSuccess) break;
-        if (device_matmul(e->qm.bits ? &e->qm : nullptr, e->dev, row_bytes, rows, cols, type, c->dx, c->dy, batch,
-                          &c->ws, &c->ws_bytes, c->stream, c->sms) != 0)
+        const Scratch sc{&c->counters, &c->counters_bytes, &c->partials, &c->partials_bytes};
+        if (device_matmul(e->qw.units ? &e->qw : nullptr, e->dev, row_bytes, rows, cols, type, c->dx, c->dy, batch,
+                          sc, c->stream, c->sms) != 0)
             break;
         if (cudaMemcpyAsync(y, c->dy, rows * batch * sizeof(float), cudaMemcpyDeviceToHost, c->stream) != cudaSuccess) break;
         if (cudaStreamSynchronize(c->stream) != cudaSuccess) break;
@@ -249,11 +286,12 @@ static int context_matmul(Context *c, const void *w, size_t rows, size_t cols, u
 // Resident plan
 // ======================================================================
 struct LayerW {
-    QMatrix q, k, v, o, gate, up, down;
+    QWeights qkv, o, gateup, down;
     const float *attn_norm = nullptr, *ffn_norm = nullptr;
 };
 
 enum StepMode { STEP_LOGITS = 0, STEP_NO_LOGITS = 1, STEP_GREEDY = 2 };
+enum KernelClass { KC_MATRIX = 0, KC_ATTENTION = 1, KC_OTHER = 2 };
 
 struct Plan {
     Context *ctx = nullptr;
@@ -263,7 +301,7 @@ struct Plan {
     float eps = 1e-5f;
     std::vector<void *> allocations;
     std::vector<LayerW> layers;
-    QMatrix out_head;
+    QWeights out_head;
     const void *embd = nullptr;
     size_t embd_row_bytes = 0;
     unsigned embd_type = 0;
@@ -275,8 +313,10 @@ struct Plan {
     unsigned *request = nullptr;  // {token, position, step, 0}
     unsigned long long *argmax_key = nullptr;
     unsigned *argmax_token = nullptr, *tiles_done = nullptr, *tokens_log = nullptr;
-    void *gemv_ws = nullptr;
-    size_t gemv_ws_bytes = 0;
+    unsigned *counters = nullptr;   // stream-K tile counters shared by every GEMV of the step
+    size_t counters_capacity = 0;
+    float *partials = nullptr;
+    size_t partials_bytes = 0;
     void *attn_ws = nullptr;
     size_t attn_ws_bytes = 0;
     unsigned attn_splits = 1;
@@ -292,8 +332,6 @@ struct Plan {
     // profiling: when set, an event is recorded after every launch
     std::vector<std::pair<cudaEvent_t, int>> *marks = nullptr;
 };
-
-enum KernelClass { KC_MATRIX = 0, KC_ATTENTION = 1, KC_OTHER = 2 };
 
 static void *plan_alloc(Plan *p, size_t bytes)
 {
@@ -343,7 +381,7 @@ __global__ void advance_kernel(unsigned *req, const unsigned *argmax_token, unsi
     req[2] += 1;
 }
 
-static int launch_plain(Plan *p, void (*k)(unsigned *, const unsigned *, unsigned *), bool pdl)
+static int launch_advance(Plan *p, bool pdl)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
@@ -354,115 +392,153 @@ static int launch_plain(Plan *p, void (*k)(unsigned *, const unsigned *, unsigne
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k, p->request, (const unsigned *)p->argmax_token, p->tokens_log) == cudaSuccess ? 0 : -2;
+    return cudaLaunchKernelEx(&cfg, advance_kernel, p->request, (const unsigned *)p->argmax_token, p->tokens_log) ==
+           cudaSuccess ? 0 : -2;
+}
+
+// ---- launch descriptions of the fused kernels of one layer ----------------
+static QgemvLaunch gemv_base(const Plan *p)
+{
+    QgemvLaunch L;
+    L.counters = p->counters; L.counters_capacity = p->counters_capacity;
+    L.partials = p->partials; L.partials_bytes = p->partials_bytes;
+    L.error = p->err_dev;
+    L.grid = p->ctx->sms;
+    L.eps = p->eps;
+    return L;
+}
+
+static QgemvLaunch qkv_launch(const Plan *p, unsigned l)
+{
+    QgemvLaunch L = gemv_base(p);
+    L.epilogue = EPI_QKV;
+    L.w = p->layers[l].qkv;
+    L.nseg = 3;
+    L.seg_rows[0] = p->H * p->hd; L.seg_rows[1] = p->Hkv * p->hd; L.seg_rows[2] = p->Hkv * p->hd;
+    L.out[0] = p->q;
+    L.kcache = p->kcache + (size_t)l * p->Hkv * p->capacity * p->hd;
+    L.vcache = p->vcache + (size_t)l * p->Hkv * p->capacity * p->hd;
+    L.norm_w = p->layers[l].attn_norm;
+    L.rope_cos = p->rope_cos; L.rope_sin = p->rope_sin;
+    L.request = p->request;
+    L.head_dim = p->hd;
+    L.capacity = (unsigned)p->capacity;
+    return L;
+}
+
+static QgemvLaunch o_launch(const Plan *p, unsigned l)
+{
+    QgemvLaunch L = gemv_base(p);
+    L.w = p->layers[l].o;
+    L.seg_rows[0] = p->d;
+    L.out[0] = p->delta;
+    L.x = p->attn;
+    return L;
+}
+
+static QgemvLaunch gateup_launch(const Plan *p, unsigned l)
+{
+    QgemvLaunch L = gemv_base(p);
+    L.epilogue = EPI_SWIGLU;
+    L.w = p->layers[l].gateup;
+    L.nseg = 2;
+    L.seg_rows[0] = p->ffn; L.seg_rows[1] = p->ffn;
+    L.out[0] = p->h;
+    L.norm_w = p->layers[l].ffn_norm;
+    return L;
+}
+
+static QgemvLaunch down_launch(const Plan *p, unsigned l)
+{
+    QgemvLaunch L = gemv_base(p);
+    L.w = p->layers[l].down;
+    L.seg_rows[0] = p->d;
+    L.out[0] = p->delta;
+    L.x = p->h;
+    return L;
+}
+
+static QgemvLaunch logits_launch(const Plan *p)
+{
+    QgemvLaunch L = gemv_base(p);
+    L.epilogue = EPI_LOGITS;
+    L.w = p->out_head;
+    L.seg_rows[0] = p->V;
+    L.out[0] = p->logits;
+    L.norm_w = p->out_norm;
+    L.argmax_key = p->argmax_key; L.argmax_token = p->argmax_token; L.tiles_done = p->tiles_done;
+    return L;
+}
+
+static AttentionLaunch attention_launch(const Plan *p, unsigned l)
+{
+    AttentionLaunch A;
+    A.q = p->q;
+    A.k = p->kcache + (size_t)l * p->Hkv * p->capacity * p->hd;
+    A.v = p->vcache + (size_t)l * p->Hkv * p->capacity * p->hd;
+    A.request = p->request;
+    A.nseq = 1; A.heads = p->H; A.kv_heads = p->Hkv; A.head_dim = p->hd;
+    A.capacity = (unsigned)p->capacity;
+    A.scale = 1.0f / std::sqrt((float)p->hd);
+    A.out = p->attn;
+    A.splits = p->attn_splits;
+    A.workspace = p->attn_ws; A.workspace_bytes = p->attn_ws_bytes;
+    return A;
 }
 
 // Enqueue one decode step reading {token, position} from p->request.
+// Residual stream: x[cur] holds the stream, `delta` the last branch output
+// not yet added; the kernel that adds it writes the sum to x[cur ^ 1].
 static int enqueue_step(Plan *p, StepMode mode)
 {
     cudaStream_t s = p->ctx->stream;
     const bool pdl = true;
-    const int grid = p->ctx->sms;
     p->launches = 0;
     int kc = KC_OTHER;
 #define RUN(expr) do { int r_ = (expr); ++p->launches; if (r_) return r_; \
         if (p->marks) { cudaEvent_t ev; cudaEventCreate(&ev); cudaEventRecord(ev, s); p->marks->push_back({ev, kc}); } } while (0)
-    kc = KC_OTHER;
     RUN(launch_gather(p->embd, p->embd_row_bytes, p->embd_type, p->d, p->request, 0, p->x[0], s, false));
     int cur = 0;
-    bool pending = false;  // delta holds an unadded branch output
+    bool pending = false;
     for (unsigned l = 0; l < p->nl; ++l) {
-        const LayerW &w = p->layers[l];
-        QgemvLaunch L;
-        L.epilogue = EPI_QKV;
-        L.nseg = 3;
-        L.seg[0] = w.q; L.seg[1] = w.k; L.seg[2] = w.v;
-        L.out[0] = p->q;
-        L.kcache = p->kcache + (size_t)l * p->Hkv * p->capacity * p->hd;
-        L.vcache = p->vcache + (size_t)l * p->Hkv * p->capacity * p->hd;
+        kc = KC_MATRIX;
+        QgemvLaunch L = qkv_launch(p, l);
         L.x = p->x[cur];
         if (pending) { L.delta = p->delta; L.x_out = p->x[cur ^ 1]; }
-        L.norm_w = w.attn_norm;
-        L.eps = p->eps;
-        L.rope_cos = p->rope_cos; L.rope_sin = p->rope_sin;
-        L.request = p->request;
-        L.head_dim = p->hd;
-        L.capacity = (unsigned)p->capacity;
-        L.workspace = p->gemv_ws; L.workspace_bytes = p->gemv_ws_bytes;
-        L.error = p->err_dev;
-        L.grid = grid; L.pdl = pdl;
-        kc = KC_MATRIX;
+        L.pdl = pdl;
         RUN(launch_qgemv(L, s));
         if (pending) cur ^= 1;
 
-        AttentionLaunch A;
-        A.q = p->q;
-        A.k = L.kcache; A.v = L.vcache;
-        A.request = p->request;
-        A.nseq = 1; A.heads = p->H; A.kv_heads = p->Hkv; A.head_dim = p->hd;
-        A.capacity = (unsigned)p->capacity;
-        A.scale = 1.0f / std::sqrt((float)p->hd);
-        A.out = p->attn;
-        A.splits = p->attn_splits;
-        A.workspace = p->attn_ws; A.workspace_bytes = p->attn_ws_bytes;
-        A.pdl = pdl;
         kc = KC_ATTENTION;
+        AttentionLaunch A = attention_launch(p, l);
+        A.pdl = pdl;
         RUN(launch_attention(A, s));
-        kc = KC_MATRIX;
 
-        QgemvLaunch O;
-        O.epilogue = EPI_STORE;
-        O.seg[0] = w.o;
-        O.out[0] = p->delta;
-        O.x = p->attn;
-        O.workspace = p->gemv_ws; O.workspace_bytes = p->gemv_ws_bytes;
-        O.error = p->err_dev;
-        O.grid = grid; O.pdl = pdl;
+        kc = KC_MATRIX;
+        QgemvLaunch O = o_launch(p, l);
+        O.pdl = pdl;
         RUN(launch_qgemv(O, s));
 
-        QgemvLaunch G;
-        G.epilogue = EPI_SWIGLU;
-        G.nseg = 2;
-        G.seg[0] = w.gate; G.seg[1] = w.up;
-        G.out[0] = p->h;
+        QgemvLaunch G = gateup_launch(p, l);
         G.x = p->x[cur]; G.delta = p->delta; G.x_out = p->x[cur ^ 1];
-        G.norm_w = w.ffn_norm; G.eps = p->eps;
-        G.workspace = p->gemv_ws; G.workspace_bytes = p->gemv_ws_bytes;
-        G.error = p->err_dev;
-        G.grid = grid; G.pdl = pdl;
+        G.pdl = pdl;
         RUN(launch_qgemv(G, s));
         cur ^= 1;
 
-        QgemvLaunch D;
-        D.epilogue = EPI_STORE;
-        D.seg[0] = w.down;
-        D.out[0] = p->delta;
-        D.x = p->h;
-        D.workspace = p->gemv_ws; D.workspace_bytes = p->gemv_ws_bytes;
-        D.error = p->err_dev;
-        D.grid = grid; D.pdl = pdl;
+        QgemvLaunch D = down_launch(p, l);
+        D.pdl = pdl;
         RUN(launch_qgemv(D, s));
         pending = true;
     }
-    if (mode == STEP_NO_LOGITS) {
-        // the residual stream is complete in x[cur] + delta; nothing reads it
-        return 0;
-    }
-    QgemvLaunch Lg;
-    Lg.epilogue = EPI_LOGITS;
-    Lg.seg[0] = p->out_head;
-    Lg.out[0] = p->logits;
+    if (mode == STEP_NO_LOGITS) return 0;  // the KV cache is what the next step reads
+    kc = KC_MATRIX;
+    QgemvLaunch Lg = logits_launch(p);
     Lg.x = p->x[cur];
     Lg.delta = pending ? p->delta : nullptr;
-    Lg.norm_w = p->out_norm; Lg.eps = p->eps;
-    Lg.argmax_key = p->argmax_key; Lg.argmax_token = p->argmax_token; Lg.tiles_done = p->tiles_done;
-    Lg.workspace = p->gemv_ws; Lg.workspace_bytes = p->gemv_ws_bytes;
-    Lg.error = p->err_dev;
-    Lg.grid = grid; Lg.pdl = pdl;
-    kc = KC_MATRIX;
+    Lg.pdl = pdl;
     RUN(launch_qgemv(Lg, s));
     kc = KC_OTHER;
-    if (mode == STEP_GREEDY) RUN(launch_plain(p, advance_kernel, pdl));
+    if (mode == STEP_GREEDY) RUN(launch_advance(p, pdl));
 #undef RUN
     return 0;
 }
@@ -470,15 +546,15 @@ static int enqueue_step(Plan *p, StepMode mode)
 static int run_step(Plan *p, StepMode mode)
 {
     cudaStream_t s = p->ctx->stream;
-    if (!p->use_graphs) {
-        int r = enqueue_step(p, mode);
+    if (!p->use_graphs || p->marks) {
+        const int r = enqueue_step(p, mode);
         p->stats.kernel_launches += p->launches;
         return r;
     }
     if (!p->graphs[mode]) {
         cudaGraph_t g = nullptr;
         if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return -2;
-        int r = enqueue_step(p, mode);
+        const int r = enqueue_step(p, mode);
         cudaError_t e = cudaStreamEndCapture(s, &g);
         if (r || e != cudaSuccess) { if (g) cudaGraphDestroy(g); debug("graph capture", e); return -2; }
         e = cudaGraphInstantiateWithFlags(&p->graphs[mode], g, 0);
@@ -506,25 +582,37 @@ static bool supported_matrix(const nya_llm_tensor *t, size_t cols, size_t rows)
            t->dimensions[1] == rows && qgemv_supported(t->type, cols, 1);
 }
 
-// Device copy of one matrix in the tensor-core layout.
-static int upload_matrix(Plan *p, const nya_llm_tensor *t, QMatrix *out)
+// Upload the raw GGUF bytes of up to three tensors and repack them, tile
+// after tile, into one fused unit array.
+static int upload_fused(Plan *p, const nya_llm_tensor *const *t, int n, int mode, QWeights *out)
 {
-    const size_t cols = (size_t)t->dimensions[0], rows = (size_t)t->dimensions[1];
-    if (t->type == T_Q4_K) {
-        void *d = plan_alloc(p, t->data_size);
-        if (!d || cudaMemcpy(d, t->data, t->data_size, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
-        *out = q4k_matrix(d, rows, cols);
-        return 0;
+    const unsigned type = t[0]->type;
+    const size_t cols = (size_t)t[0]->dimensions[0];
+    size_t tiles[3] = {0, 0, 0}, total = 0;
+    if (mode == REPACK_GATEUP) { tiles[0] = ((size_t)t[0]->dimensions[1] + 7) / 8; total = tiles[0]; }
+    else for (int i = 0; i < n; ++i) { tiles[i] = ((size_t)t[i]->dimensions[1] + 15) / 16; total += tiles[i]; }
+    unsigned char *units = (unsigned char *)plan_alloc(p, qunits_bytes(type, total, cols));
+    if (!units) return -1;
+    void *raw[3] = {nullptr, nullptr, nullptr};
+    int r = 0;
+    for (int i = 0; i < n && !r; ++i) {
+        if (cudaMalloc(&raw[i], t[i]->data_size) != cudaSuccess ||
+            !upload(raw[i], t[i]->data, t[i]->data_size, p->ctx->stream)) r = -1;
     }
-    void *raw = nullptr;
-    if (cudaMalloc(&raw, t->data_size) != cudaSuccess) { cudaGetLastError(); return -1; }
-    void *d = plan_alloc(p, q6k_repacked_bytes(rows, cols));
-    int r = -1;
-    if (d && cudaMemcpy(raw, t->data, t->data_size, cudaMemcpyHostToDevice) == cudaSuccess &&
-        repack_q6k(raw, rows, cols, d, out, p->ctx->stream) == 0 && cudaStreamSynchronize(p->ctx->stream) == cudaSuccess)
-        r = 0;
-    cudaFree(raw);
-    return r;
+    size_t at = 0;
+    if (!r && mode == REPACK_GATEUP)
+        r = repack_units(raw[0], raw[1], (size_t)t[0]->dimensions[1], cols, type, mode, units, total, p->ctx->stream);
+    for (int i = 0; !r && mode != REPACK_GATEUP && i < n; ++i) {
+        r = repack_units(raw[i], nullptr, (size_t)t[i]->dimensions[1], cols, type, mode,
+                         units + qunits_bytes(type, at, cols), tiles[i], p->ctx->stream);
+        at += tiles[i];
+    }
+    if (cudaStreamSynchronize(p->ctx->stream) != cudaSuccess) r = -1;  // raw buffers are read until here
+    for (int i = 0; i < n; ++i) cudaFree(raw[i]);
+    cudaGetLastError();
+    if (r) return -1;
+    out->units = units; out->type = type; out->cols = (unsigned)cols; out->tiles = (unsigned)total;
+    return 0;
 }
 
 static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity)
@@ -565,11 +653,8 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
 
     // admission: weights + KV + scratch against the budget (resident.inc:155-168)
     size_t weights = 0;
-    for (size_t i = 0; i < m->tensor_count; ++i) {
-        const nya_llm_tensor &t = m->tensors[i];
-        weights += t.type == T_Q6_K && t.dimension_count == 2 && &t != m->token_embedding
-                       ? q6k_repacked_bytes((size_t)t.dimensions[1], (size_t)t.dimensions[0]) : t.data_size;
-    }
+    for (size_t i = 0; i < m->tensor_count; ++i) weights += m->tensors[i].data_size;
+    if (m->output == m->token_embedding) weights += m->output->data_size;  // gather copy + units
     const size_t kv_bytes = (size_t)nl * Hkv * capacity * hd * sizeof(__half) * 2;
     const size_t act = ((size_t)d * 3 + (size_t)H * hd * 2 + ffn + V) * sizeof(float) + 2 * capacity * (hd / 2) * sizeof(float);
     if (weights + kv_bytes + act > c->cache_limit) return plan_decline("weights plus KV/scratch exceed the memory budget");
@@ -602,33 +687,38 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
     p->tokens_log = (unsigned *)A(capacity * 4 + 64);
     if (ok && cudaHostAlloc((void **)&p->err_host, 64, cudaHostAllocMapped) != cudaSuccess) { cudaGetLastError(); ok = false; }
     if (ok) { std::memset(p->err_host, 0, 64); ok = cudaHostGetDevicePointer((void **)&p->err_dev, p->err_host, 0) == cudaSuccess; }
-    if (ok) ok = cudaMemset(p->argmax_key, 0, 64) == cudaSuccess && cudaMemset(p->tiles_done, 0, 64) == cudaSuccess &&
-                 cudaMemset(p->request, 0, 64) == cudaSuccess;
+    if (ok) ok = cudaMemsetAsync(p->argmax_key, 0, 64, c->stream) == cudaSuccess &&
+                 cudaMemsetAsync(p->tiles_done, 0, 64, c->stream) == cudaSuccess &&
+                 cudaMemsetAsync(p->request, 0, 64, c->stream) == cudaSuccess;
 
-    // weights
+    // weights, repacked into fused tensor-core matrices
     p->layers.resize(nl);
     for (unsigned i = 0; ok && i < nl; ++i) {
         const nya_llm_layer &w = m->layers[i];
         LayerW &L = p->layers[i];
-        ok = upload_matrix(p, w.query, &L.q) == 0 && upload_matrix(p, w.key, &L.k) == 0 &&
-             upload_matrix(p, w.value, &L.v) == 0 && upload_matrix(p, w.attention_output, &L.o) == 0 &&
-             upload_matrix(p, w.feed_forward_gate, &L.gate) == 0 && upload_matrix(p, w.feed_forward_up, &L.up) == 0 &&
-             upload_matrix(p, w.feed_forward_down, &L.down) == 0;
+        const nya_llm_tensor *qkv[3] = {w.query, w.key, w.value};
+        const nya_llm_tensor *o[1] = {w.attention_output};
+        const nya_llm_tensor *gu[2] = {w.feed_forward_gate, w.feed_forward_up};
+        const nya_llm_tensor *dn[1] = {w.feed_forward_down};
+        ok = upload_fused(p, qkv, 3, REPACK_QKV, &L.qkv) == 0 && upload_fused(p, o, 1, REPACK_PLAIN, &L.o) == 0 &&
+             upload_fused(p, gu, 2, REPACK_GATEUP, &L.gateup) == 0 && upload_fused(p, dn, 1, REPACK_PLAIN, &L.down) == 0;
         if (!ok) break;
         float *an = (float *)A(d * 4), *fn = (float *)A(d * 4);
-        ok = ok && cudaMemcpy(an, w.attention_norm->data, d * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-             cudaMemcpy(fn, w.feed_forward_norm->data, d * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+        ok = ok && upload(an, w.attention_norm->data, d * 4, c->stream) && upload(fn, w.feed_forward_norm->data, d * 4, c->stream);
         L.attn_norm = an; L.ffn_norm = fn;
     }
-    if (ok) ok = upload_matrix(p, m->output, &p->out_head) == 0;
+    if (ok) {
+        const nya_llm_tensor *out[1] = {m->output};
+        ok = upload_fused(p, out, 1, REPACK_PLAIN, &p->out_head) == 0;
+    }
     if (ok) {
         void *e = A(m->token_embedding->data_size);
-        ok = ok && cudaMemcpy(e, m->token_embedding->data, m->token_embedding->data_size, cudaMemcpyHostToDevice) == cudaSuccess;
+        ok = ok && upload(e, m->token_embedding->data, m->token_embedding->data_size, c->stream);
         p->embd = e;
         p->embd_type = m->token_embedding->type;
         p->embd_row_bytes = d / eblock * ebytes;
         float *on = (float *)A(d * 4);
-        ok = ok && cudaMemcpy(on, m->output_norm->data, d * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+        ok = ok && upload(on, m->output_norm->data, d * 4, c->stream);
         p->out_norm = on;
     }
     // RoPE tables with the engine's own host formula (llm_cpu.c:216-229, :428-432)
@@ -638,33 +728,34 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
         for (unsigned j = 0; j < pairs; ++j) freq[j] = powf(m->rope_frequency_base, -(float)j / (float)pairs) / 1.0f;
         for (size_t t = 0; t < capacity; ++t)
             for (unsigned j = 0; j < pairs; ++j) {
-                float angle = (float)t * freq[j];
+                const float angle = (float)t * freq[j];
                 co[t * pairs + j] = cosf(angle);
                 si[t * pairs + j] = sinf(angle);
             }
-        ok = cudaMemcpy(p->rope_cos, co.data(), co.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-             cudaMemcpy(p->rope_sin, si.data(), si.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+        ok = upload(p->rope_cos, co.data(), co.size() * 4, c->stream) && upload(p->rope_sin, si.data(), si.size() * 4, c->stream) &&
+             cudaStreamSynchronize(c->stream) == cudaSuccess;
     }
-    // workspaces: the largest GEMV of the step, and the attention partials
+    // stream-K scratch for the largest GEMV of the step; attention partials
     if (ok) {
-        size_t need = 0;
-        const LayerW &L = p->layers[0];
-        QgemvLaunch q3; q3.epilogue = EPI_QKV; q3.nseg = 3; q3.seg[0] = L.q; q3.seg[1] = L.k; q3.seg[2] = L.v;
-        need = std::max(need, qgemv_workspace_bytes(q3, c->sms));
-        QgemvLaunch o; o.seg[0] = L.o; need = std::max(need, qgemv_workspace_bytes(o, c->sms));
-        QgemvLaunch g; g.epilogue = EPI_SWIGLU; g.nseg = 2; g.seg[0] = L.gate; g.seg[1] = L.up;
-        need = std::max(need, qgemv_workspace_bytes(g, c->sms));
-        QgemvLaunch dn; dn.seg[0] = L.down; need = std::max(need, qgemv_workspace_bytes(dn, c->sms));
-        QgemvLaunch lg; lg.epilogue = EPI_LOGITS; lg.seg[0] = p->out_head; need = std::max(need, qgemv_workspace_bytes(lg, c->sms));
-        p->gemv_ws = A(need); p->gemv_ws_bytes = need;
-        // split the context so (kv heads x splits) covers about two CTAs per SM
-        p->attn_splits = std::max(1u, (unsigned)(2 * c->sms) / Hkv);
+        const QgemvLaunch all[5] = {qkv_launch(p, 0), o_launch(p, 0), gateup_launch(p, 0), down_launch(p, 0), logits_launch(p)};
+        size_t tiles = 0, partial = 0;
+        for (const auto &L : all) {
+            tiles = std::max<size_t>(tiles, qgemv_tiles(L));
+            partial = std::max(partial, qgemv_partials_bytes(L, c->sms));
+        }
+        p->counters_capacity = tiles;
+        p->counters = (unsigned *)A(tiles * 4);
+        p->partials_bytes = partial;
+        p->partials = (float *)A(partial);
+        // one partition per ~128 positions of the context, at most 32
+        p->attn_splits = (unsigned)std::min<size_t>(32, std::max<size_t>(1, (capacity + 127) / 128));
         AttentionLaunch al; al.nseq = 1; al.heads = H; al.kv_heads = Hkv; al.head_dim = hd; al.splits = p->attn_splits;
         p->attn_ws_bytes = attention_workspace_bytes(al);
         p->attn_ws = A(p->attn_ws_bytes);
-        if (ok) ok = cudaMemset(p->gemv_ws, 0, need) == cudaSuccess && cudaMemset(p->attn_ws, 0, p->attn_ws_bytes) == cudaSuccess;
+        if (ok) ok = cudaMemsetAsync(p->counters, 0, tiles * 4, c->stream) == cudaSuccess &&
+                     cudaMemsetAsync(p->attn_ws, 0, p->attn_ws_bytes, c->stream) == cudaSuccess;
     }
-    if (ok) ok = cudaDeviceSynchronize() == cudaSuccess;
+    if (ok) ok = cudaStreamSynchronize(c->stream) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
     if (!ok) {
         debug("resident plan setup failed; rolling back", cudaGetLastError());
         plan_free(p);
@@ -672,8 +763,7 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
     }
     p->stats.weights_bytes = weights;
     p->stats.kv_bytes = kv_bytes;
-    size_t scratch = act + p->gemv_ws_bytes + p->attn_ws_bytes;
-    p->stats.scratch_bytes = scratch;
+    p->stats.scratch_bytes = act + p->counters_capacity * 4 + p->partials_bytes + p->attn_ws_bytes;
     p->stats.prefill_batch = 1;
     return p;
 }
@@ -818,42 +908,58 @@ extern "C" int fyb_dequantize(const void *w, size_t count, unsigned type, float 
     return launch_dequant(w, type, count, out, (cudaStream_t)stream);
 }
 
-extern "C" size_t fyb_quant_matmul_workspace(size_t rows, size_t cols, unsigned type, size_t batch)
+// Workspace of fyb_quant_matmul for one shape: [tile counters][partials][units].
+static void qm_layout(size_t rows, size_t cols, unsigned type, int sms, size_t *counters, size_t *partials, size_t *units)
 {
-    (void)batch;
-    if ((type != T_Q4_K && type != T_Q6_K) || !qgemv_supported(type, cols, 1)) return 0;
+    QgemvLaunch L;
+    L.w.type = type; L.w.cols = (unsigned)cols; L.w.tiles = (unsigned)((rows + 15) / 16);
+    L.seg_rows[0] = (unsigned)rows;
+    *counters = ((size_t)L.w.tiles * 4 + 255) / 256 * 256;
+    *partials = (qgemv_partials_bytes(L, sms) + 255) / 256 * 256;
+    *units = qunits_bytes(type, L.w.tiles, cols);
+}
+
+static int current_sms()
+{
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaGetLastError();
-    QgemvLaunch L;
-    L.seg[0].rows = (unsigned)rows; L.seg[0].cols = (unsigned)cols; L.seg[0].type = type;
-    size_t ws = qgemv_workspace_bytes(L, sms);
-    if (type == T_Q6_K) ws += q6k_repacked_bytes(rows, cols);
-    return ws;
+    return sms > 0 ? sms : 148;
+}
+
+extern "C" size_t fyb_quant_matmul_workspace(size_t rows, size_t cols, unsigned type, size_t batch)
+{
+    (void)batch;
+    if (!qgemv_supported(type, cols, 1) || rows == 0) return 0;
+    size_t a, b, u;
+    qm_layout(rows, cols, type, current_sms(), &a, &b, &u);
+    return a + b + u;
 }
 
 extern "C" int fyb_quant_matmul(const void *w, size_t rows, size_t cols, unsigned type, const float *x, float *y,
     size_t batch, void *workspace, size_t workspace_bytes, void *stream)
 {
     size_t block, bbytes;
-    if (!w || !x || !y || !rows || !cols || !batch || !type_geometry(type, &block, &bbytes) || cols % block) return -1;
+    if (!w || !x || !y || !rows || !cols || !batch || rows > 0x7fffffffu || !type_geometry(type, &block, &bbytes) ||
+        cols % block)
+        return -1;
     cudaStream_t s = (cudaStream_t)stream;
-    int dev = 0, sms = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = current_sms();
     const size_t row_bytes = cols / block * bbytes;
-    if ((type == T_Q4_K || type == T_Q6_K) && qgemv_supported(type, cols, 1)) {
-        size_t need = fyb_quant_matmul_workspace(rows, cols, type, batch);
-        if (!workspace || workspace_bytes < need) return -1;
-        QMatrix qm = q4k_matrix(w, rows, cols);
-        size_t gemv_bytes = need;
-        if (type == T_Q6_K) {
-            gemv_bytes = need - q6k_repacked_bytes(rows, cols);
-            void *tail = (unsigned char *)workspace + gemv_bytes;
-            if (repack_q6k(w, rows, cols, tail, &qm, s)) return -2;
-        }
-        return device_matmul(&qm, w, row_bytes, rows, cols, type, x, y, batch, &workspace, nullptr, s, sms) ? -2 : 0;
-    }
-    return launch_generic_matmul(w, row_bytes, rows, cols, type, x, cols, y, rows, batch, s);
+    if (!qgemv_supported(type, cols, 1))
+        return launch_generic_matmul(w, row_bytes, rows, cols, type, x, cols, y, rows, batch, s);
+    size_t cb, pb, ub;
+    qm_layout(rows, cols, type, sms, &cb, &pb, &ub);
+    if (!workspace || workspace_bytes < cb + pb + ub) return -1;
+    unsigned char *ws = (unsigned char *)workspace;
+    QWeights qw;
+    qw.units = ws + cb + pb; qw.type = type; qw.cols = (unsigned)cols; qw.tiles = (unsigned)((rows + 15) / 16);
+    if (repack_units(w, nullptr, rows, cols, type, REPACK_PLAIN, ws + cb + pb, qw.tiles, s)) return -2;
+    unsigned *counters = (unsigned *)ws;
+    float *partials = (float *)(ws + cb);
+    size_t cbytes = cb, pbytes = pb;
+    const Scratch sc{&counters, &cbytes, &partials, &pbytes};
+    return device_matmul(&qw, w, row_bytes, rows, cols, type, x, y, batch, sc, s, sms) ? -2 : 0;
 }
 
 extern "C" size_t fyb_attention_workspace(unsigned nseq, unsigned heads, unsigned kv_heads, unsigned head_dim, unsigned splits)
@@ -968,45 +1074,33 @@ extern "C" double fyb_plan_time_projection(void *opaque, unsigned layer, unsigne
     Plan *p = (Plan *)opaque;
     if (!p || p->failed || layer >= p->nl || which > 4 || reps == 0) return -1.0;
     DeviceScope scope(p->ctx->device);
-    const LayerW &w = p->layers[layer];
     QgemvLaunch L;
-    L.workspace = p->gemv_ws; L.workspace_bytes = p->gemv_ws_bytes;
-    L.error = p->err_dev;
-    L.grid = p->ctx->sms;
-    L.eps = p->eps;
-    size_t weight_bytes = 0, in_bytes = (size_t)p->d * 4, out_bytes = 0, norm_bytes = 0;
-    auto wbytes = [](const QMatrix &m) {
-        return m.type == T_Q4_K ? (size_t)m.rows * (m.cols / 256) * 144 : (size_t)m.rows * (m.cols / 256) * 210;
-    };
+    size_t in_bytes = (size_t)p->d * 4, out_bytes = 0, norm_bytes = 0;
     switch (which) {
     case 0:
-        L.epilogue = EPI_QKV; L.nseg = 3; L.seg[0] = w.q; L.seg[1] = w.k; L.seg[2] = w.v;
-        L.out[0] = p->q; L.kcache = p->kcache; L.vcache = p->vcache; L.x = p->x[0]; L.norm_w = w.attn_norm;
-        L.rope_cos = p->rope_cos; L.rope_sin = p->rope_sin; L.request = p->request; L.head_dim = p->hd;
-        L.capacity = (unsigned)p->capacity;
-        weight_bytes = wbytes(w.q) + wbytes(w.k) + wbytes(w.v);
+        L = qkv_launch(p, layer); L.x = p->x[0];
         norm_bytes = (size_t)p->d * 4;
         out_bytes = (size_t)p->H * p->hd * 4 + (size_t)2 * p->Hkv * p->hd * 2;
         break;
     case 1:
-        L.seg[0] = w.o; L.out[0] = p->delta; L.x = p->attn;
-        weight_bytes = wbytes(w.o); out_bytes = (size_t)p->d * 4; in_bytes = (size_t)p->H * p->hd * 4;
+        L = o_launch(p, layer);
+        out_bytes = (size_t)p->d * 4; in_bytes = (size_t)p->H * p->hd * 4;
         break;
     case 2:
-        L.epilogue = EPI_SWIGLU; L.nseg = 2; L.seg[0] = w.gate; L.seg[1] = w.up; L.out[0] = p->h;
-        L.x = p->x[0]; L.norm_w = w.ffn_norm;
-        weight_bytes = wbytes(w.gate) + wbytes(w.up); norm_bytes = (size_t)p->d * 4; out_bytes = (size_t)p->ffn * 4;
+        L = gateup_launch(p, layer); L.x = p->x[0];
+        norm_bytes = (size_t)p->d * 4; out_bytes = (size_t)p->ffn * 4;
         break;
     case 3:
-        L.seg[0] = w.down; L.out[0] = p->delta; L.x = p->h;
-        weight_bytes = wbytes(w.down); in_bytes = (size_t)p->ffn * 4; out_bytes = (size_t)p->d * 4;
+        L = down_launch(p, layer);
+        in_bytes = (size_t)p->ffn * 4; out_bytes = (size_t)p->d * 4;
         break;
     default:
-        L.epilogue = EPI_LOGITS; L.seg[0] = p->out_head; L.out[0] = p->logits; L.x = p->x[0]; L.norm_w = p->out_norm;
-        L.argmax_key = p->argmax_key; L.argmax_token = p->argmax_token; L.tiles_done = p->tiles_done;
-        weight_bytes = wbytes(p->out_head); norm_bytes = (size_t)p->d * 4; out_bytes = (size_t)p->V * 4;
+        L = logits_launch(p); L.x = p->x[0];
+        norm_bytes = (size_t)p->d * 4; out_bytes = (size_t)p->V * 4;
         break;
     }
+    // GGUF bytes of the weights (the repacked units have the same size)
+    const size_t weight_bytes = qunits_bytes(L.w.type, L.w.tiles, L.w.cols);
     if (bytes) *bytes = weight_bytes + in_bytes + norm_bytes + out_bytes;
     cudaEvent_t a, b;
     cudaEventCreate(&a); cudaEventCreate(&b);

@@ -94,22 +94,40 @@ def test_cached_weight_reuse_and_resizing(provider):
 SWEEP = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
 
 
+def double_reference(data, type_id, xs, cols, rows, chunk=8192):
+    """sum_k w*x and sum_k |w*x| in double over the exactly dequantized
+    weights (the forward-error oracle of test_quant_kernels.c:13-25)."""
+    rb = F.row_bytes(type_id, cols)
+    s = np.empty((xs.shape[0], rows))
+    mag = np.empty((xs.shape[0], rows))
+    x64 = xs.astype(np.float64)
+    for r0 in range(0, rows, chunk):
+        n = min(chunk, rows - r0)
+        w = O.dequantize(data[r0 * rb:(r0 + n) * rb], type_id, n * cols).reshape(n, cols).astype(np.float64)
+        s[:, r0:r0 + n] = x64 @ w.T
+        mag[:, r0:r0 + n] = np.abs(x64) @ np.abs(w).T
+    return s, mag
+
+
 @pytest.mark.parametrize("type_id", [F.Q4_K, F.Q6_K])
 @pytest.mark.parametrize("rows,cols", SWEEP)
 def test_projection_sweep(provider, type_id, rows, cols):
-    """C2 shapes with BASELINE value distributions; batches 1, 2 and 4."""
+    """C2 shapes with BASELINE value distributions; batches 1, 2 and 4.
+    Bounds: the reference's forward-error bound against the double dot,
+    |a - s| <= 1e-6 (1 + sum|w x|), and the north-star 1e-3 relative."""
     nbytes = rows * F.row_bytes(type_id, cols)
     data = np.empty(nbytes, np.uint8)
     F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, type_id, 2024, rows * 7 + cols)
     rng = np.random.default_rng(rows + cols)
+    xs = rng.standard_normal((4, cols)).astype(np.float32)
+    s, mag = double_reference(data, type_id, xs, cols, rows)
     for batch in (1, 2, 4):
-        xs = rng.standard_normal((batch, cols)).astype(np.float32)
-        y = provider.matmul(data, rows, cols, type_id, xs, batch)
+        y = provider.matmul(data, rows, cols, type_id, xs[:batch], batch)
         assert y is not None
         for b in range(batch):
-            e = O.matvec(data, type_id, xs[b], cols, rows)
-            err = np.abs(y[b] - e) / (1 + np.abs(e))
-            assert err.max() <= 1e-3, (batch, b, float(err.max()))
+            err = np.abs(y[b].astype(np.float64) - s[b])
+            assert np.all(err <= 1e-6 * (1 + mag[b])), (batch, b, float((err / (1 + mag[b])).max()))
+            assert np.all(err <= 1e-3 * (1 + np.abs(s[b]))), (batch, b)
 
 
 def test_dequantize_bit_exact_all_types():
@@ -124,3 +142,16 @@ def test_dequantize_bit_exact_all_types():
         torch.cuda.synchronize()
         got = out.cpu().numpy()
         assert (got.view(np.uint32) == expected.view(np.uint32)).all(), type_id
+
+
+def test_f32_257x1025_like_engine_test(provider):
+    """test_compute.c check_matvec(257, 1025): every row of three passes."""
+    rows, cols = 257, 1025
+    i = np.arange(rows * cols)
+    w = (((i % 23) - 11) / 17.0).astype(np.float32)
+    for p in range(3):
+        x = ((((np.arange(cols) % 13) - 6 + p)) / 7.0).astype(np.float32)
+        y = provider.matvec(w, rows, cols, F.F32, x)
+        e = w.reshape(rows, cols).astype(np.float64) @ x.astype(np.float64)
+        bad = np.nonzero(np.abs(y - e) > 1e-4 * (1 + np.abs(e)))[0]
+        assert bad.size == 0, (p, bad[:8].tolist(), y[bad[:4]].tolist(), e[bad[:4]].tolist())

