@@ -322,8 +322,43 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- profiling modes
+KERNELS = {"qkv": 0, "o": 1, "gateup": 2, "down": 3, "logits": 4}
+
+
+def run_kernel_mode(args):
+    """One 8B-shaped layer (plus the output head): time `--reps` stand-alone
+    launches of one fused projection kernel. Small enough (about 1 GB on the
+    device) for a full ncu capture of a single launch."""
+    import fyodor_b200 as F
+    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K,
+                         **dict(CFG8B, layers=1, context=64))
+    provider = F.Provider()
+    plan = provider.plan(model, 64)
+    ms, nbytes = plan.time_projection(0, KERNELS[args.kernel], args.reps)
+    print(json.dumps({"kernel": args.kernel, "reps": args.reps, "us_per_launch": round(ms * 1000, 3),
+                      "bytes_per_launch": nbytes, "gb_s": round(nbytes / ms / 1e6, 1)}))
+
+
+def run_steps_mode(args):
+    """A few 8B decode steps launched eagerly (one launch per kernel, graphs
+    off) so an ncu launch list shows every kernel of a step."""
+    os.environ["NYA_CUDA_GRAPHS"] = "0"
+    import fyodor_b200 as F
+    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **dict(CFG8B, context=64))
+    provider = F.Provider()
+    plan = provider.plan(model, 64)
+    for i in range(args.eager_steps):
+        if plan.token(17 + i, i) != 0:
+            raise SystemExit("decode step failed")
+    print(json.dumps({"eager_steps": args.eager_steps, "kernel_launches": plan.stats()["kernel_launches"]}))
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", choices=sorted(KERNELS), help="time one fused kernel of an 8B layer")
+    ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--eager-steps", type=int, default=0, help="run N eager 8B decode steps (profiling)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -332,7 +367,11 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel_mode(args)
+    elif args.eager_steps:
+        run_steps_mode(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_provider(args)

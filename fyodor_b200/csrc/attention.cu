@@ -82,27 +82,34 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
 #pragma unroll
         for (int g = 0; g < G; ++g) s[g] = 0.f;
         if (valid) {
+            // the whole K row in two batches of loads, then the dot products
             const uint4 *krow = reinterpret_cast<const uint4 *>(K + (size_t)t * HD);
-#pragma unroll 4
-            for (int c = 0; c < HD / 8; ++c) {
-                uint4 kk = __ldg(krow + c);
-                const __half2 *h2 = reinterpret_cast<const __half2 *>(&kk);
-                float kf[8];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    float2 f2 = __half22float2(h2[e]);
-                    kf[2 * e] = f2.x; kf[2 * e + 1] = f2.y;
-                }
+            for (int half = 0; half < 2; ++half) {
+                uint4 kk[HD / 16];
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][8 * c]);
-                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][8 * c + 4]);
-                    float acc = s[g];
-                    acc = fmaf(qa.x, kf[0], acc); acc = fmaf(qa.y, kf[1], acc);
-                    acc = fmaf(qa.z, kf[2], acc); acc = fmaf(qa.w, kf[3], acc);
-                    acc = fmaf(qb.x, kf[4], acc); acc = fmaf(qb.y, kf[5], acc);
-                    acc = fmaf(qb.z, kf[6], acc); acc = fmaf(qb.w, kf[7], acc);
-                    s[g] = acc;
+                for (int c = 0; c < HD / 16; ++c) kk[c] = __ldg(krow + half * (HD / 16) + c);
+#pragma unroll
+                for (int c = 0; c < HD / 16; ++c) {
+                    const __half2 *h2 = reinterpret_cast<const __half2 *>(&kk[c]);
+                    float kf[8];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f2 = __half22float2(h2[e]);
+                        kf[2 * e] = f2.x; kf[2 * e + 1] = f2.y;
+                    }
+                    const int col = 8 * (half * (HD / 16) + c);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][col]);
+                        const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][col + 4]);
+                        float acc = s[g];
+                        acc = fmaf(qa.x, kf[0], acc); acc = fmaf(qa.y, kf[1], acc);
+                        acc = fmaf(qa.z, kf[2], acc); acc = fmaf(qa.w, kf[3], acc);
+                        acc = fmaf(qb.x, kf[4], acc); acc = fmaf(qb.y, kf[5], acc);
+                        acc = fmaf(qb.z, kf[6], acc); acc = fmaf(qb.w, kf[7], acc);
+                        s[g] = acc;
+                    }
                 }
             }
         }
@@ -121,24 +128,35 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
         }
         __syncwarp();
         const unsigned n = min(32u, c1 - base);
-        for (unsigned j = 0; j < n; ++j) {
-            const __half *vrow = V + (size_t)(base + j) * HD + lane * DPL;
-            float vf[DPL];
-            if constexpr (DPL == 4) {
-                uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vrow));
-                float2 a = __half22float2(*reinterpret_cast<__half2 *>(&vv.x));
-                float2 b = __half22float2(*reinterpret_cast<__half2 *>(&vv.y));
-                vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
-            } else {
-                unsigned vv = __ldg(reinterpret_cast<const unsigned *>(vrow));
-                float2 a = __half22float2(*reinterpret_cast<__half2 *>(&vv));
-                vf[0] = a.x; vf[1] = a.y;
+        // V rows of the tile: all loads first (8 at a time), then the FMAs
+#pragma unroll
+        for (unsigned j0 = 0; j0 < 32; j0 += 8) {
+            if (j0 >= n) break;
+            float vf[8][DPL];
+#pragma unroll
+            for (unsigned jj = 0; jj < 8; ++jj) {
+                const unsigned j = j0 + jj < n ? j0 + jj : n - 1;
+                const __half *vrow = V + (size_t)(base + j) * HD + lane * DPL;
+                if constexpr (DPL == 4) {
+                    uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vrow));
+                    const float2 a = __half22float2(*reinterpret_cast<__half2 *>(&vv.x));
+                    const float2 b = __half22float2(*reinterpret_cast<__half2 *>(&vv.y));
+                    vf[jj][0] = a.x; vf[jj][1] = a.y; vf[jj][2] = b.x; vf[jj][3] = b.y;
+                } else {
+                    unsigned vv = __ldg(reinterpret_cast<const unsigned *>(vrow));
+                    const float2 a = __half22float2(*reinterpret_cast<__half2 *>(&vv));
+                    vf[jj][0] = a.x; vf[jj][1] = a.y;
+                }
             }
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float pj = pbuf[warp][j][g];
+            for (unsigned jj = 0; jj < 8; ++jj) {
+                if (j0 + jj >= n) break;
 #pragma unroll
-                for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pj, vf[e], o[g][e]);
+                for (int g = 0; g < G; ++g) {
+                    const float pj = pbuf[warp][j0 + jj][g];
+#pragma unroll
+                    for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pj, vf[jj][e], o[g][e]);
+                }
             }
         }
         __syncwarp();

@@ -31,7 +31,7 @@
 //
 // Work split: units are taken in tile-major order and every warp of the grid
 // owns one contiguous range (stream-K). Each warp streams its units with
-// cp.async.bulk into a private 4-stage shared-memory ring (mbarrier per
+// cp.async.bulk into a private shared-memory ring (mbarrier per
 // stage, bounded waits) - the first stages are issued before the
 // programmatic-dependent-launch wait, as weights never depend on the
 // previous kernel. A tile finished by one warp goes straight to the
@@ -44,9 +44,15 @@
 
 namespace fyb {
 
-constexpr int QG_WARPS = 8;
+#ifndef FYB_QG_WARPS
+#define FYB_QG_WARPS 16
+#endif
+#ifndef FYB_QG_STAGES
+#define FYB_QG_STAGES 2
+#endif
+constexpr int QG_WARPS = FYB_QG_WARPS;   // warps per CTA, one CTA per SM
 constexpr int QG_THREADS = QG_WARPS * 32;
-constexpr int QG_STAGES = 4;
+constexpr int QG_STAGES = FYB_QG_STAGES; // bulk-copy stages per warp
 constexpr int QG_XPAD = 16;  // limb-row stride = 16 (mod 128) bytes: conflict-free B fragments
 
 constexpr unsigned Q4_UNIT = 2304;  // qs [p4][h2][r16][16] | hdr [r16][16]
@@ -153,12 +159,15 @@ FYB_DEV void compute_unit(const unsigned char *u, unsigned blk, const signed cha
     if constexpr (TYPE == T_Q4_K) {
         const uint4 hA = *reinterpret_cast<const uint4 *>(u + 2048 + gid * 16);
         const uint4 hB = *reinterpret_cast<const uint4 *>(u + 2048 + (gid + 8) * 16);
-        const unsigned scA0 = hA.y & 0x3F3F3F3Fu, mnA0 = hA.z & 0x3F3F3F3Fu;
-        const unsigned scA1 = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
-        const unsigned mnA1 = ((hA.w >> 4) & 0x0F0F0F0Fu) | ((hA.z >> 2) & 0x30303030u);
-        const unsigned scB0 = hB.y & 0x3F3F3F3Fu, mnB0 = hB.z & 0x3F3F3F3Fu;
-        const unsigned scB1 = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
-        const unsigned mnB1 = ((hB.w >> 4) & 0x0F0F0F0Fu) | ((hB.z >> 2) & 0x30303030u);
+        // the 8 six-bit scales of both rows, unpacked once (llm_quant.c:249)
+        const unsigned scA0 = hA.y & 0x3F3F3F3Fu, scA1 = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
+        const unsigned scB0 = hB.y & 0x3F3F3F3Fu, scB1 = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
+        int sA[8], sB[8];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            sA[g] = ubyte(scA0, g); sA[g + 4] = ubyte(scA1, g);
+            sB[g] = ubyte(scB0, g); sB[g + 4] = ubyte(scB1, g);
+        }
 #pragma unroll
         for (int pr = 0; pr < 4; ++pr) {
             unsigned q[4];
@@ -177,35 +186,33 @@ FYB_DEV void compute_unit(const unsigned char *u, unsigned blk, const signed cha
             int dlo[4] = {0, 0, 0, 0}, dhi[4] = {0, 0, 0, 0};
             mma_u8s8_k32(dlo, alo, blo0, blo1);
             mma_u8s8_k32(dhi, ahi, bhi0, bhi1);
-            const int g0 = 2 * pr, g1 = 2 * pr + 1;
-            const int sA0 = ubyte(g0 < 4 ? scA0 : scA1, g0 & 3), sA1 = ubyte(g1 < 4 ? scA0 : scA1, g1 & 3);
-            const int sB0 = ubyte(g0 < 4 ? scB0 : scB1, g0 & 3), sB1 = ubyte(g1 < 4 ? scB0 : scB1, g1 & 3);
-            T0 += sA0 * dlo[0] + sA1 * dhi[0];
-            T1 += sA0 * dlo[1] + sA1 * dhi[1];
-            T2 += sB0 * dlo[2] + sB1 * dhi[2];
-            T3 += sB0 * dlo[3] + sB1 * dhi[3];
+            T0 += sA[2 * pr] * dlo[0] + sA[2 * pr + 1] * dhi[0];
+            T1 += sA[2 * pr] * dlo[1] + sA[2 * pr + 1] * dhi[1];
+            T2 += sB[2 * pr] * dlo[2] + sB[2 * pr + 1] * dhi[2];
+            T3 += sB[2 * pr] * dlo[3] + sB[2 * pr + 1] * dhi[3];
         }
         const float dA = half_bits_to_float((unsigned short)(hA.x & 0xffffu));
-        const float mA = half_bits_to_float((unsigned short)(hA.x >> 16));
         const float dB = half_bits_to_float((unsigned short)(hB.x & 0xffffu));
-        const float mB = half_bits_to_float((unsigned short)(hB.x >> 16));
         const int E = vec < (unsigned)nvec ? exps[vec * nblk + blk] : 0;
         const float f0 = pow2f(E - 6 - 7 * l0), f1 = pow2f(E - 6 - 7 * (l0 + 1));
         accA = fmaf(dA, fmaf((float)T0, f0, (float)T1 * f1), accA);
         accB = fmaf(dB, fmaf((float)T2, f0, (float)T3 * f1), accB);
-        if ((tig & 1) == 0 && vec < (unsigned)nvec) {
+        // minimum term -dmin * sum_g m_g * sum(x_g): lane tig&1 == 0 adds it for
+        // row A, its neighbour for row B (the pair is summed when the tile ends)
+        if (vec < (unsigned)nvec) {
+            const uint4 h = (tig & 1) ? hB : hA;
+            const unsigned mn0 = h.z & 0x3F3F3F3Fu, mn1 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
             const float *gs = gsums + (size_t)vec * ngroups + blk * 8;  // this block's 8 group sums
             const float4 s0 = *reinterpret_cast<const float4 *>(gs);
             const float4 s1 = *reinterpret_cast<const float4 *>(gs + 4);
-            const float sx[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-            float bA = 0.f, bB = 0.f;
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-                bA = fmaf((float)ubyte(g < 4 ? mnA0 : mnA1, g & 3), sx[g], bA);
-                bB = fmaf((float)ubyte(g < 4 ? mnB0 : mnB1, g & 3), sx[g], bB);
-            }
-            accA = fmaf(-mA, bA, accA);
-            accB = fmaf(-mB, bB, accB);
+            float b = (float)ubyte(mn0, 0) * s0.x;
+            b = fmaf((float)ubyte(mn0, 1), s0.y, b); b = fmaf((float)ubyte(mn0, 2), s0.z, b);
+            b = fmaf((float)ubyte(mn0, 3), s0.w, b); b = fmaf((float)ubyte(mn1, 0), s1.x, b);
+            b = fmaf((float)ubyte(mn1, 1), s1.y, b); b = fmaf((float)ubyte(mn1, 2), s1.z, b);
+            b = fmaf((float)ubyte(mn1, 3), s1.w, b);
+            const float dmin = half_bits_to_float((unsigned short)(h.x >> 16));
+            if (tig & 1) accB = fmaf(-dmin, b, accB);
+            else accA = fmaf(-dmin, b, accA);
         }
     } else {
         const uint4 sA = *reinterpret_cast<const uint4 *>(u + 3072 + gid * 16);
