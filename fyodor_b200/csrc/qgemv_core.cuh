@@ -1,0 +1,253 @@
+// qgemv_core.cuh - device building blocks of the K-quant tensor-core GEMV,
+// shared by the stand-alone GEMV kernel (qgemv.cu) and the persistent
+// decode kernel (decode.cu). The scheme is described in qgemv.cu.
+#pragma once
+#include "common.cuh"
+#include "kernels.h"
+#include <cmath>
+
+namespace fyb {
+
+#ifndef FYB_QG_WARPS
+#define FYB_QG_WARPS 16
+#endif
+#ifndef FYB_QG_STAGES
+#define FYB_QG_STAGES 2
+#endif
+constexpr int QG_WARPS = FYB_QG_WARPS;   // warps per CTA, one CTA per SM
+constexpr int QG_THREADS = QG_WARPS * 32;
+constexpr int QG_STAGES = FYB_QG_STAGES; // bulk-copy stages per warp
+constexpr int QG_XPAD = 16;  // limb-row stride = 16 (mod 128) bytes: conflict-free B fragments
+
+constexpr unsigned Q4_UNIT = 2304;  // qs [p4][h2][r16][16] | hdr [r16][16]
+constexpr unsigned Q6_UNIT = 3360;  // ql [c4][h2][r16][16] | qh [c2][h2][r16][16] | sc [r16][16] | d [r16] f16
+__host__ __device__ constexpr unsigned unit_bytes(unsigned type) { return type == T_Q4_K ? Q4_UNIT : Q6_UNIT; }
+
+// ------------------------------------------------------------ byte helpers
+FYB_DEV int ubyte(unsigned w, int i) { return (int)((w >> (8 * i)) & 0xffu); }
+FYB_DEV int sbyte(unsigned w, int i) { return (int)(signed char)((w >> (8 * i)) & 0xffu); }
+FYB_DEV float pow2f(int e) { return e < -126 ? 0.0f : __int_as_float((e + 127) << 23); }
+
+// Signed Q6_K quants (q - 32) of four packed values: low nibbles from ql
+// (high nibble for quarters 2 and 3), two high bits from qh at bit 2*Q.
+template <int Q>
+FYB_DEV unsigned q6_signed(unsigned ql, unsigned qh)
+{
+    const unsigned lo = (Q >> 1) ? (ql >> 4) : ql;
+    unsigned hi;
+    if (Q == 0) hi = qh << 4;
+    else if (Q == 1) hi = qh << 2;
+    else if (Q == 2) hi = qh;
+    else hi = qh >> 2;
+    const unsigned v = (lo & 0x0F0F0F0Fu) | ((hi & 0x30303030u) ^ 0x20202020u);
+    const unsigned s = v & 0x20202020u;
+    return v + 6u * s;  // sign-extend bit 5 into bits 6 and 7 of every byte
+}
+
+// ldmatrix.x4 of a [h2][r16][16 B] block: lane i addresses row (i&7)+8*((i>>3)&1),
+// half (i>>4). Result regs: (r gid, bytes 4t..), (r gid+8, 4t..), (r gid, 16+4t..), (r gid+8, 16+4t..)
+FYB_DEV void load_frag(unsigned (&r)[4], const unsigned char *base, unsigned lane)
+{
+    const unsigned row = (lane & 7) + 8 * ((lane >> 3) & 1), half = lane >> 4;
+    ldmatrix_x4(r, base + half * 256 + row * 16);
+}
+
+// ------------------------------------------------------------ per-unit math
+// Accumulates one unit (16 rows x 256 columns, from shared memory) into
+// accA (row gid) / accB (row gid+8). Lane (gid, tig) holds matrix columns
+// 2*tig and 2*tig+1 = vector tig/2, limbs 2*(tig&1) and 2*(tig&1)+1.
+template <unsigned TYPE>
+FYB_DEV void compute_unit(const unsigned char *u, unsigned blk, const signed char *xl, unsigned xstride,
+    bool brow_ok, const int *exps, unsigned nblk, const float *gsums, unsigned ngroups, int nvec,
+    unsigned lane, float &accA, float &accB)
+{
+    const unsigned gid = lane >> 2, tig = lane & 3, vec = tig >> 1;
+    const int l0 = 2 * (tig & 1);
+    const signed char *xrow = xl + (size_t)(brow_ok ? gid : 0) * xstride + blk * 256u;
+    int T0 = 0, T1 = 0, T2 = 0, T3 = 0;
+    if constexpr (TYPE == T_Q4_K) {
+        const uint4 hA = *reinterpret_cast<const uint4 *>(u + 2048 + gid * 16);
+        const uint4 hB = *reinterpret_cast<const uint4 *>(u + 2048 + (gid + 8) * 16);
+        // the 8 six-bit scales of both rows, unpacked once (llm_quant.c:249)
+        const unsigned scA0 = hA.y & 0x3F3F3F3Fu, scA1 = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
+        const unsigned scB0 = hB.y & 0x3F3F3F3Fu, scB1 = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
+        int sA[8], sB[8];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            sA[g] = ubyte(scA0, g); sA[g + 4] = ubyte(scA1, g);
+            sB[g] = ubyte(scB0, g); sB[g + 4] = ubyte(scB1, g);
+        }
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) {
+            unsigned q[4];
+            load_frag(q, u + pr * 512, lane);
+            unsigned blo0 = 0, blo1 = 0, bhi0 = 0, bhi1 = 0;
+            if (brow_ok) {
+                const signed char *g0 = xrow + 64 * pr, *g1 = g0 + 32;
+                blo0 = *reinterpret_cast<const unsigned *>(g0 + 4 * tig);
+                blo1 = *reinterpret_cast<const unsigned *>(g0 + 16 + 4 * tig);
+                bhi0 = *reinterpret_cast<const unsigned *>(g1 + 4 * tig);
+                bhi1 = *reinterpret_cast<const unsigned *>(g1 + 16 + 4 * tig);
+            }
+            const unsigned alo[4] = {q[0] & 0x0F0F0F0Fu, q[1] & 0x0F0F0F0Fu, q[2] & 0x0F0F0F0Fu, q[3] & 0x0F0F0F0Fu};
+            const unsigned ahi[4] = {(q[0] >> 4) & 0x0F0F0F0Fu, (q[1] >> 4) & 0x0F0F0F0Fu,
+                                     (q[2] >> 4) & 0x0F0F0F0Fu, (q[3] >> 4) & 0x0F0F0F0Fu};
+            int dlo[4] = {0, 0, 0, 0}, dhi[4] = {0, 0, 0, 0};
+            mma_u8s8_k32(dlo, alo, blo0, blo1);
+            mma_u8s8_k32(dhi, ahi, bhi0, bhi1);
+            T0 += sA[2 * pr] * dlo[0] + sA[2 * pr + 1] * dhi[0];
+            T1 += sA[2 * pr] * dlo[1] + sA[2 * pr + 1] * dhi[1];
+            T2 += sB[2 * pr] * dlo[2] + sB[2 * pr + 1] * dhi[2];
+            T3 += sB[2 * pr] * dlo[3] + sB[2 * pr + 1] * dhi[3];
+        }
+        const float dA = half_bits_to_float((unsigned short)(hA.x & 0xffffu));
+        const float dB = half_bits_to_float((unsigned short)(hB.x & 0xffffu));
+        const int E = vec < (unsigned)nvec ? exps[vec * nblk + blk] : 0;
+        const float f0 = pow2f(E - 6 - 7 * l0), f1 = pow2f(E - 6 - 7 * (l0 + 1));
+        accA = fmaf(dA, fmaf((float)T0, f0, (float)T1 * f1), accA);
+        accB = fmaf(dB, fmaf((float)T2, f0, (float)T3 * f1), accB);
+        // minimum term -dmin * sum_g m_g * sum(x_g): lane tig&1 == 0 adds it for
+        // row A, its neighbour for row B (the pair is summed when the tile ends)
+        if (vec < (unsigned)nvec) {
+            const uint4 h = (tig & 1) ? hB : hA;
+            const unsigned mn0 = h.z & 0x3F3F3F3Fu, mn1 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+            const float *gs = gsums + (size_t)vec * ngroups + blk * 8;  // this block's 8 group sums
+            const float4 s0 = *reinterpret_cast<const float4 *>(gs);
+            const float4 s1 = *reinterpret_cast<const float4 *>(gs + 4);
+            float b = (float)ubyte(mn0, 0) * s0.x;
+            b = fmaf((float)ubyte(mn0, 1), s0.y, b); b = fmaf((float)ubyte(mn0, 2), s0.z, b);
+            b = fmaf((float)ubyte(mn0, 3), s0.w, b); b = fmaf((float)ubyte(mn1, 0), s1.x, b);
+            b = fmaf((float)ubyte(mn1, 1), s1.y, b); b = fmaf((float)ubyte(mn1, 2), s1.z, b);
+            b = fmaf((float)ubyte(mn1, 3), s1.w, b);
+            const float dmin = half_bits_to_float((unsigned short)(h.x >> 16));
+            if (tig & 1) accB = fmaf(-dmin, b, accB);
+            else accA = fmaf(-dmin, b, accA);
+        }
+    } else {
+        const uint4 sA = *reinterpret_cast<const uint4 *>(u + 3072 + gid * 16);
+        const uint4 sB = *reinterpret_cast<const uint4 *>(u + 3072 + (gid + 8) * 16);
+        const float dA = half_bits_to_float(*reinterpret_cast<const unsigned short *>(u + 3328 + gid * 2));
+        const float dB = half_bits_to_float(*reinterpret_cast<const unsigned short *>(u + 3328 + (gid + 8) * 2));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            unsigned qh[4];
+            load_frag(qh, u + 2048 + h * 512, lane);
+#pragma unroll
+            for (int c2 = 0; c2 < 2; ++c2) {
+                unsigned ql[4];
+                load_frag(ql, u + (2 * h + c2) * 512, lane);
+#pragma unroll
+                for (int hiq = 0; hiq < 2; ++hiq) {
+                    const int Q = c2 + 2 * hiq;  // quarter: ql chunk c2, nibble hiq
+                    unsigned a[4];
+#define FYB_Q6(QQ) for (int i = 0; i < 4; ++i) a[i] = q6_signed<QQ>(ql[i], qh[i]);
+                    if (Q == 0) { FYB_Q6(0) } else if (Q == 1) { FYB_Q6(1) } else if (Q == 2) { FYB_Q6(2) } else { FYB_Q6(3) }
+#undef FYB_Q6
+                    unsigned b1 = 0, b2 = 0;
+                    if (brow_ok) {
+                        b1 = *reinterpret_cast<const unsigned *>(xrow + h * 128 + Q * 32 + 4 * tig);
+                        b2 = *reinterpret_cast<const unsigned *>(xrow + h * 128 + Q * 32 + 16 + 4 * tig);
+                    }
+                    int d1[4] = {0, 0, 0, 0}, d2[4] = {0, 0, 0, 0};
+                    asm volatile(
+                        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                        : "+r"(d1[0]), "+r"(d1[1]), "+r"(d1[2]), "+r"(d1[3]) : "r"(a[0]), "r"(a[1]), "r"(b1));
+                    asm volatile(
+                        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                        : "+r"(d2[0]), "+r"(d2[1]), "+r"(d2[2]), "+r"(d2[3]) : "r"(a[2]), "r"(a[3]), "r"(b2));
+                    const int g = h * 8 + Q * 2;  // first of the two 16-value scale groups
+                    const unsigned wA = (&sA.x)[g >> 2], wB = (&sB.x)[g >> 2];
+                    const int s1A = sbyte(wA, g & 3), s2A = sbyte(wA, (g & 3) + 1);
+                    const int s1B = sbyte(wB, g & 3), s2B = sbyte(wB, (g & 3) + 1);
+                    T0 += s1A * d1[0] + s2A * d2[0];
+                    T1 += s1A * d1[1] + s2A * d2[1];
+                    T2 += s1B * d1[2] + s2B * d2[2];
+                    T3 += s1B * d1[3] + s2B * d2[3];
+                }
+            }
+        }
+        const int E = vec < (unsigned)nvec ? exps[vec * nblk + blk] : 0;
+        const float f0 = pow2f(E - 6 - 7 * l0), f1 = pow2f(E - 6 - 7 * (l0 + 1));
+        accA = fmaf(dA, fmaf((float)T0, f0, (float)T1 * f1), accA);
+        accB = fmaf(dB, fmaf((float)T2, f0, (float)T3 * f1), accB);
+        (void)gsums; (void)ngroups;
+    }
+}
+
+FYB_DEV double block_sum_double(double v, double *red)
+{
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double t = 0;
+    for (int w = 0; w < QG_WARPS; ++w) t += red[w];
+    return t;
+}
+
+FYB_DEV void load16(const float *src, float (&v)[16])
+{
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 t = __ldcg(s4 + i);
+        v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    }
+}
+
+// Limb split of one 16-value slot `sl` of vector `v` (x already residual-
+// added and normalized): fp32 group sums (pairs of slots, adjacent lanes),
+// the block exponent (16 slots = 16 adjacent lanes) and four signed limbs.
+// Every lane of the warp must call it (shuffles); `ok` marks real slots.
+FYB_DEV void prep_slot(float (&x)[16], bool ok, unsigned v, unsigned sl, unsigned K, unsigned nblk, signed char *xl,
+    unsigned xstride, int *exps, float *gsums, unsigned *error)
+{
+        float gs = 0.f, mx = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) { gs = __fadd_rn(gs, x[j]); mx = fmaxf(mx, fabsf(x[j])); }
+        const float other = __shfl_xor_sync(0xffffffffu, gs, 1);
+        if (ok && (sl & 1) == 0) gsums[v * (K / 32) + sl / 2] = __fadd_rn(gs, other);
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        int E = 0;
+        const bool bad = !(mx <= 3.0e38f);  // inf or NaN in the block
+        if (!bad && mx > 0.f) {
+            frexpf(mx, &E);
+            if (E < -120) E = -120;  // below 2^-121 the limbs round to zero anyway
+        }
+        if (ok && (sl & 15) == 0) exps[v * nblk + sl / 16] = E;
+        if (ok && bad && error) *(volatile unsigned *)error = ERR_NONFINITE;
+        const float sc = pow2f(6 - E);
+        unsigned words[4][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            unsigned t[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float r = bad ? 0.f : __fmul_rn(x[4 * q + i], sc);
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    const float m = __fadd_rn(r, 12582912.0f);  // rint via the 1.5*2^23 magic
+                    const float X = __fsub_rn(m, 12582912.0f);
+                    t[l][i] = __float_as_uint(m);
+                    r = __fmul_rn(__fsub_rn(r, X), 128.0f);
+                }
+            }
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const unsigned lo = __byte_perm(t[l][0], t[l][1], 0x0040);
+                const unsigned hi = __byte_perm(t[l][2], t[l][3], 0x0040);
+                words[l][q] = __byte_perm(lo, hi, 0x5410);
+            }
+        }
+        if (ok) {
+#pragma unroll
+            for (int l = 0; l < 4; ++l)
+                *reinterpret_cast<uint4 *>(xl + (size_t)(v * 4 + l) * xstride + 16 * sl) =
+                    make_uint4(words[l][0], words[l][1], words[l][2], words[l][3]);
+        }
+}
+
+}  // namespace fyb
