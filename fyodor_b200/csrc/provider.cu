@@ -1074,31 +1074,37 @@ extern "C" double fyb_plan_time_projection(void *opaque, unsigned layer, unsigne
     Plan *p = (Plan *)opaque;
     if (!p || p->failed || layer >= p->nl || which > 4 || reps == 0) return -1.0;
     DeviceScope scope(p->ctx->device);
-    QgemvLaunch L;
     size_t in_bytes = (size_t)p->d * 4, out_bytes = 0, norm_bytes = 0;
-    switch (which) {
-    case 0:
-        L = qkv_launch(p, layer); L.x = p->x[0];
-        norm_bytes = (size_t)p->d * 4;
-        out_bytes = (size_t)p->H * p->hd * 4 + (size_t)2 * p->Hkv * p->hd * 2;
-        break;
-    case 1:
-        L = o_launch(p, layer);
-        out_bytes = (size_t)p->d * 4; in_bytes = (size_t)p->H * p->hd * 4;
-        break;
-    case 2:
-        L = gateup_launch(p, layer); L.x = p->x[0];
-        norm_bytes = (size_t)p->d * 4; out_bytes = (size_t)p->ffn * 4;
-        break;
-    case 3:
-        L = down_launch(p, layer);
-        in_bytes = (size_t)p->ffn * 4; out_bytes = (size_t)p->d * 4;
-        break;
-    default:
-        L = logits_launch(p); L.x = p->x[0];
-        norm_bytes = (size_t)p->d * 4; out_bytes = (size_t)p->V * 4;
-        break;
-    }
+    // launch i reads layer (layer + i) % layers, so back-to-back launches do
+    // not find the previous launch's weights in L2 (unless the model is small)
+    auto make = [&](unsigned l) {
+        QgemvLaunch L;
+        switch (which) {
+        case 0:
+            L = qkv_launch(p, l); L.x = p->x[0];
+            norm_bytes = (size_t)p->d * 4;
+            out_bytes = (size_t)p->H * p->hd * 4 + (size_t)2 * p->Hkv * p->hd * 2;
+            break;
+        case 1:
+            L = o_launch(p, l);
+            out_bytes = (size_t)p->d * 4; in_bytes = (size_t)p->H * p->hd * 4;
+            break;
+        case 2:
+            L = gateup_launch(p, l); L.x = p->x[0];
+            norm_bytes = (size_t)p->d * 4; out_bytes = (size_t)p->ffn * 4;
+            break;
+        case 3:
+            L = down_launch(p, l);
+            in_bytes = (size_t)p->ffn * 4; out_bytes = (size_t)p->d * 4;
+            break;
+        default:
+            L = logits_launch(p); L.x = p->x[0];
+            norm_bytes = (size_t)p->d * 4; out_bytes = (size_t)p->V * 4;
+            break;
+        }
+        return L;
+    };
+    QgemvLaunch L = make(layer);
     // GGUF bytes of the weights (the repacked units have the same size)
     const size_t weight_bytes = qunits_bytes(L.w.type, L.w.tiles, L.w.cols);
     if (bytes) *bytes = weight_bytes + in_bytes + norm_bytes + out_bytes;
@@ -1107,7 +1113,7 @@ extern "C" double fyb_plan_time_projection(void *opaque, unsigned layer, unsigne
     if (launch_qgemv(L, p->ctx->stream)) { cudaEventDestroy(a); cudaEventDestroy(b); return -1.0; }  // warm-up
     cudaEventRecord(a, p->ctx->stream);
     int r = 0;
-    for (unsigned i = 0; i < reps && !r; ++i) r = launch_qgemv(L, p->ctx->stream);
+    for (unsigned i = 0; i < reps && !r; ++i) r = launch_qgemv(make((layer + 1 + i) % p->nl), p->ctx->stream);
     cudaEventRecord(b, p->ctx->stream);
     float ms = -1.f;
     if (r || cudaEventSynchronize(b) != cudaSuccess || cudaEventElapsedTime(&ms, a, b) != cudaSuccess) ms = -1.f;

@@ -95,7 +95,9 @@ int fyb_plan_profile(void *plan, uint32_t token, size_t position, size_t steps, 
    kernel of `layer` (which: 0 QKV+RoPE+KV append, 1 attention output,
    2 gate/up+SwiGLU, 3 down, 4 logits+argmax), timed over `reps` launches
    with CUDA events; *bytes receives the kernel's algorithmic bytes per
-   launch (weights, input vector, norm weights, outputs). */
+   launch (weights, input vector, norm weights, outputs). Timed launch i
+   uses layer (layer + 1 + i) % layers, so with many layers consecutive
+   launches read different weights (more bytes than L2 holds). */
 double fyb_plan_time_projection(void *plan, unsigned layer, unsigned which, unsigned reps, size_t *bytes);
 
 /* ---- synthetic GGUF-layout models (no reference counterpart) -------------

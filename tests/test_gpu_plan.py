@@ -53,7 +53,9 @@ def test_plan_logits(provider, name, cfg, tokens):
         assert np.argmax(got) == np.argmax(e16) == np.argmax(GOLD[name + "_logits"][i])
     kv = plan.read_kv(cfg["layers"] - 1, 0, len(tokens))
     k16, v16 = ref16.read_kv(cfg["layers"] - 1, 0, len(tokens), m.kv_dim)
-    assert scaled_error(kv[0], k16) <= 2e-3 and scaled_error(kv[1], v16) <= 2e-3
+    # last layer of a high-gain model: compare on the tensor's scale, as the logits
+    assert logit_error(kv[0], k16) <= 2e-3 and logit_error(kv[1], v16) <= 2e-3, \
+        (logit_error(kv[0], k16), logit_error(kv[1], v16))
     st = plan.stats()
     assert st["graph_captures"] == 1 and st["graph_replays"] == len(tokens)
     assert st["kv_bytes"] == cfg["layers"] * m.kv_dim * len(tokens) * 2 * 2
