@@ -97,6 +97,8 @@ def _load():
     lib.fyb_attention_workspace.argtypes = [C.c_uint] * 5
     lib.fyb_attention_decode.argtypes = [_P, _P, _P, C.c_size_t, _P, C.c_uint, C.c_uint, C.c_uint, C.c_uint,
                                          C.c_uint, C.c_float, _P, C.c_uint, _P, C.c_size_t, _P]
+    lib.fyb_attention_decode_static.argtypes = [_P, _P, _P, C.c_size_t, _P, C.c_uint, C.c_uint, C.c_uint, C.c_uint,
+                                                C.c_uint, C.c_float, _P, C.c_uint, _P]
     lib.fyb_plan_decode_greedy.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t, _P]
     lib.fyb_plan_time_greedy.restype = C.c_double
     lib.fyb_plan_time_greedy.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t]
@@ -116,7 +118,8 @@ lib = _load()
 
 # exported names declared in include/fyodor_b200.h
 EXPORTS = ["nya_cuda_backend", "fyb_version", "fyb_device_count", "fyb_dequantize", "fyb_quant_matmul_workspace",
-           "fyb_quant_matmul", "fyb_attention_workspace", "fyb_attention_decode", "fyb_plan_decode_greedy",
+           "fyb_quant_matmul", "fyb_attention_workspace", "fyb_attention_decode",
+           "fyb_attention_decode_static", "fyb_plan_decode_greedy",
            "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_profile", "fyb_plan_time_projection",
            "fyb_synth_create",
            "fyb_synth_free", "fyb_synth_fill"]

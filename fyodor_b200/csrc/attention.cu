@@ -20,8 +20,10 @@
 // the online softmax, then the lanes switch to 4 output dimensions each and
 // accumulate p * v over the 32 positions.
 #include "common.cuh"
+#include "fyodor_b200.h"
 #include "kernels.h"
 #include <cfloat>
+#include <mutex>
 
 namespace fyb {
 
@@ -266,3 +268,76 @@ int launch_attention(const AttentionLaunch &L, cudaStream_t s)
 }
 
 }  // namespace fyb
+
+// ---------------------------------------------------------------------------
+// fyb_attention_decode_static: the same kernel with its scratch (split
+// partials + per-(sequence, KV head) counters) in a fixed device array of
+// this module instead of a caller workspace. It is for callers that cannot
+// allocate device memory at the point of the call: a host hook that runs
+// under a device-memory budget it has already spent (the engine caps the
+// provider with NYA_CUDA_MEMORY_MIB), or a caller on a latency-critical path
+// that must not pay the implicit device synchronization of cudaFree. The
+// entry point itself allocates nothing: no cudaMalloc, no cudaFree, no
+// library allocator.
+//
+// Set-up: the first call on a device (with that device current) looks up the
+// array's device address with cudaGetSymbolAddress and keeps it; that first
+// call should therefore come before any stream capture on the device. Every
+// call clears the counters it will use (the only part that must start at
+// zero) with cudaMemsetAsync on the caller's stream, then launches.
+// Problems whose scratch exceeds FYB_ATTENTION_STATIC_SCRATCH_BYTES are
+// rejected with -3 before anything is launched. There is one array per
+// device, so calls that overlap in time on the same device (other streams or
+// threads) race on it; callers must serialize them.
+namespace {
+
+constexpr size_t kStaticScratchBytes = 4u << 20;
+static_assert(kStaticScratchBytes == FYB_ATTENTION_STATIC_SCRATCH_BYTES, "header and module disagree");
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_attention_scratch[kStaticScratchBytes];
+
+std::mutex g_scratch_mutex;
+void *g_scratch_ptr[kMaxDevices];
+
+// Device address of this device's array, looked up once per device.
+void *static_scratch(int device)
+{
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_ptr[device]) {
+        void *ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_attention_scratch) != cudaSuccess || !ptr) return nullptr;
+        g_scratch_ptr[device] = ptr;
+    }
+    return g_scratch_ptr[device];
+}
+
+}  // namespace
+
+extern "C" int fyb_attention_decode_static(const float *q, const void *k, const void *v, size_t seq_stride,
+    const unsigned *lengths, unsigned nseq, unsigned heads, unsigned kv_heads, unsigned head_dim, unsigned capacity,
+    float scale, float *out, unsigned splits, void *stream)
+{
+    using namespace fyb;
+    AttentionLaunch L;
+    L.q = q; L.k = (const __half *)k; L.v = (const __half *)v;
+    L.seq_stride = seq_stride; L.lengths = lengths;
+    L.nseq = nseq; L.heads = heads; L.kv_heads = kv_heads; L.head_dim = head_dim; L.capacity = capacity;
+    L.scale = scale; L.out = out; L.splits = splits ? splits : 8;
+    if (!lengths || !kv_heads || !nseq || heads % kv_heads) return -1;
+    const size_t need = attention_workspace_bytes(L);
+    if (need > kStaticScratchBytes) return -3;
+    int device = -1;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return -2;
+    unsigned char *scratch = (unsigned char *)static_scratch(device);
+    if (!scratch) return -2;
+    // counters follow the 256-byte-rounded partials (attention_workspace_bytes' layout)
+    const unsigned G = heads / kv_heads;
+    const size_t pairs = (size_t)nseq * kv_heads;
+    const size_t counters = (pairs * L.splits * G * (head_dim + 2) * sizeof(float) + 255) / 256 * 256;
+    if (cudaMemsetAsync(scratch + counters, 0, pairs * sizeof(unsigned), (cudaStream_t)stream) != cudaSuccess)
+        return -2;
+    L.workspace = scratch;
+    L.workspace_bytes = need;
+    return launch_attention(L, (cudaStream_t)stream);
+}

@@ -69,6 +69,25 @@ int fyb_attention_decode(const float *q, const void *k_cache, const void *v_cach
     unsigned capacity, float scale, float *out, unsigned splits, void *workspace, size_t workspace_bytes,
     void *stream);
 
+/* fyb_attention_decode without a workspace argument and without allocating
+   anything (no counterpart in the reference). Same arguments and results as
+   fyb_attention_decode; the scratch is a fixed array of
+   FYB_ATTENTION_STATIC_SCRATCH_BYTES per device inside the library. Meant
+   for callers that cannot allocate device memory where they call: a hook
+   that runs under a device-memory budget it has already used up
+   (NYA_CUDA_MEMORY_MIB), or a latency path that must not take cudaFree's
+   implicit device synchronization.
+   - The first call on a device (that device current) looks up the array's
+     address; make that first call before any stream capture on the device.
+   - Returns -3, launching nothing, when the problem needs more scratch than
+     the array holds (fyb_attention_workspace() gives the need).
+   - One array per device: calls that overlap in time on one device (other
+     streams or threads) race on it and must be serialized by the caller. */
+#define FYB_ATTENTION_STATIC_SCRATCH_BYTES ((size_t)4 << 20)
+int fyb_attention_decode_static(const float *q, const void *k_cache, const void *v_cache, size_t seq_stride,
+    const unsigned *lengths, unsigned nseq, unsigned heads, unsigned kv_heads, unsigned head_dim,
+    unsigned capacity, float scale, float *out, unsigned splits, void *stream);
+
 /* ---- resident plans ---------------------------------------------------- */
 
 /* Greedy decode entirely on the device: starting from `token` at `position`,
