@@ -171,13 +171,13 @@ def run_provider(args):
         raise SystemExit("prefill failed")
     first = int(np.argmax(plan.logits))
     setup_s = time.perf_counter() - t_setup
-    launches = int(plan.launches_per_token()) + 1 - 1  # graph nodes per greedy step (advance replaces request)
 
     for _ in range(args.warmup):
         if plan.time_greedy(first, PROMPT, DECODE) < 0:
             raise SystemExit("warm-up failed")
     barrier(dist)
     torch.cuda.synchronize()
+    launches_before = plan.stats()["kernel_launches"]
     with ClockSampler(local) as clocks:
         total_ms = 0.0
         for _ in range(args.steps):
@@ -186,6 +186,7 @@ def run_provider(args):
                 raise SystemExit("timed step failed")
             total_ms += ms
     torch.cuda.synchronize()
+    launches = plan.stats()["kernel_launches"] - launches_before  # counted by the plan, graph nodes included
     barrier(dist)
     total_ms = max_over_ranks(dist, total_ms)
     tokens = args.steps * DECODE
@@ -266,7 +267,7 @@ def run_provider(args):
                     "step_ms_by_class": None if breakdown is None else
                     {"matrix": round(float(breakdown[0]), 4), "attention": round(float(breakdown[1]), 4),
                      "other": round(float(breakdown[2]), 4)}},
-        "gpu_launches": int(args.steps * DECODE * (launches)),
+        "gpu_launches": int(launches),
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
         "setup_s": round(setup_s, 1),
@@ -354,11 +355,57 @@ def run_steps_mode(args):
     print(json.dumps({"eager_steps": args.eager_steps, "kernel_launches": plan.stats()["kernel_launches"]}))
 
 
+def run_trace_mode(args):
+    """Where one persistent decode step spends its time: the 8B model after a
+    PROMPT-token prefill, one step traced per CTA (globaltimer), reported per
+    phase kind as the CTA-median time spent waiting for the phase's input,
+    preparing it, and working (GEMV units or attention items), summed over
+    layers, in microseconds."""
+    import fyodor_b200 as F
+    from tests.patterns import bench_tokens
+    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **CFG8B)
+    plan = F.Provider().plan(model, PROMPT + 8)
+    if plan is None or plan.prefill(bench_tokens(PROMPT, model.vocabulary), 0) != 0:
+        raise SystemExit("8B plan or prefill failed")
+    tr = None
+    for i in range(args.trace_step):  # the last traced step is reported (earlier ones warm up)
+        res = plan.trace(17 + i, PROMPT + i, warps=bool(args.trace_raw))
+        if res is None:
+            raise SystemExit("trace failed (persistent kernel not in use?)")
+        tr = res[0] if args.trace_raw else res
+    if args.trace_raw:
+        np.save(args.trace_raw, tr)
+        np.save(args.trace_raw.replace(".npy", "") + "_warps.npy", res[1])
+    t = tr.astype(np.int64) - int(tr[0].min())
+    L = model.config.layers
+    kinds = ["qkv", "attention", "o", "gateup", "down"]
+    out = {k: {"wait": 0.0, "prep": 0.0, "work": 0.0} for k in kinds + ["logits"]}
+    for l in range(L):
+        base = 1 + 15 * l
+        # layout per layer: qkv A B C | att A B C | o A B C | gu A B C | down A B C
+        for k in range(5):
+            a, b, c = t[base + 3 * k], t[base + 3 * k + 1], t[base + 3 * k + 2]
+            nxt = t[base + 3 * k + 3]  # the next phase's idle point (or logits / exit)
+            out[kinds[k]]["wait"] += float(np.median(b - a)) / 1e3
+            out[kinds[k]]["prep"] += float(np.median(c - b)) / 1e3 if k != 1 else 0.0
+            out[kinds[k]]["work"] += float(np.median(nxt - c if k != 1 else c - b)) / 1e3
+    lb = 1 + 15 * L
+    out["logits"]["wait"] = float(np.median(t[lb + 1] - t[lb])) / 1e3
+    out["logits"]["prep"] = float(np.median(t[lb + 2] - t[lb + 1])) / 1e3
+    out["logits"]["work"] = float(np.median(t[lb + 3] - t[lb + 2])) / 1e3
+    total = float(t[-1].max()) / 1e3
+    print(json.dumps({"trace_us": {k: {x: round(v, 1) for x, v in d.items()} for k, d in out.items()},
+                      "step_us": round(total, 1), "grid": int(tr.shape[1]), "points": int(tr.shape[0])}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", choices=sorted(KERNELS), help="time one fused kernel of an 8B layer")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--eager-steps", type=int, default=0, help="run N eager 8B decode steps (profiling)")
+    ap.add_argument("--trace-step", type=int, default=0,
+                    help="trace N persistent 8B decode steps per CTA and report the last (profiling)")
+    ap.add_argument("--trace-raw", default="", help="with --trace-step: also save the raw trace (.npy)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -371,6 +418,8 @@ def main():
         run_kernel_mode(args)
     elif args.eager_steps:
         run_steps_mode(args)
+    elif args.trace_step:
+        run_trace_mode(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 
 #define FYB_DEV __device__ __forceinline__
+#define FYB_HOST_DEV __host__ __device__ __forceinline__
 
 namespace fyb {
 
@@ -54,6 +55,11 @@ FYB_DEV unsigned ldg_stream_u1(const void *p)
     return r;
 }
 FYB_DEV void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2::evict_last [%0];" :: "l"(p)); }
+// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, bytes a multiple of 16).
+FYB_DEV void bulk_prefetch_l2(const void *p, unsigned bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
+}
 
 // ---- mbarrier + bulk (TMA, non-tensor) copies into shared memory ----------
 FYB_DEV void mbar_init(uint64_t *bar, unsigned count)

@@ -98,4 +98,62 @@ struct AttentionLaunch {
 size_t attention_workspace_bytes(const AttentionLaunch &L);
 int launch_attention(const AttentionLaunch &L, cudaStream_t s);
 
+// ---------------------------------------------------------------- decode.cu
+// One decode step of a dense LLaMA model as one persistent kernel.
+struct DecodeLayer {
+    QWeights qkv, o, gateup, down;  // repacked as for the stand-alone GEMV
+    const float *attn_norm = nullptr, *ffn_norm = nullptr;
+    __half *kcache = nullptr, *vcache = nullptr;  // [kv_heads][capacity][hd]
+};
+struct DecodeGeometry {
+    unsigned nl = 0, d = 0, H = 0, Hkv = 0, hd = 0, ffn = 0, V = 0, capacity = 0;
+};
+// Device-side synchronization words of a plan (all zero at creation; the
+// kernel keeps them consistent from step to step).
+struct DecodeSync {
+    unsigned *qkv_done = nullptr;   // [nl][kv_heads]
+    unsigned *attn_done = nullptr;  // [nl]
+    unsigned *o_done = nullptr, *gu_done = nullptr, *down_done = nullptr;  // [nl]
+    unsigned *tile_counters = nullptr;  // [max tiles of a phase]
+    unsigned *attn_counters = nullptr;  // [kv_heads]
+    unsigned *exit_count = nullptr, *abort_flag = nullptr;
+    unsigned *logit_tiles = nullptr;
+};
+struct DecodeLaunch {
+    DecodeGeometry g;
+    const DecodeLayer *layers = nullptr;  // device array [nl]
+    QWeights out_head;
+    const float *out_norm = nullptr;
+    const unsigned char *embd = nullptr;
+    size_t embd_row_bytes = 0;
+    unsigned embd_type = 0;
+    float eps = 1e-5f, attn_scale = 0.f;
+    const float *rope_cos = nullptr, *rope_sin = nullptr;
+    unsigned *request = nullptr;  // {token, position, tokens logged, step}
+    float *xa = nullptr, *xm = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
+    double *ss_o = nullptr, *ss_d = nullptr;  // [d/16] per-tile sums of squares
+    DecodeSync sync;
+    float *partials = nullptr;       // decode_partials_bytes()
+    float *attn_partials = nullptr;  // kv_heads * splits * G * (hd + 2) floats
+    unsigned attn_splits = 1;
+    unsigned long long *argmax_key = nullptr;
+    unsigned *argmax_token = nullptr, *tokens_log = nullptr;
+    unsigned *error = nullptr;
+    int logits_mode = 1;  // 0 none, 1 logits + argmax, 2 logits + greedy advance
+    int grid = 0;
+    unsigned long long *trace = nullptr;  // profiling: [decode_trace_points()][grid] globaltimer ns
+    unsigned trace_slots = 0;
+    unsigned long long *wtrace = nullptr;  // profiling: [layers*5 + 1][grid*16][4] per-warp GEMV points
+    unsigned ring_bytes = 0;  // per-warp weight ring (0: as much as shared memory allows)
+    int l2_prefetch = 1;      // prefetch each next phase's weights into L2
+};
+// Trace points per CTA of one step: start, per layer 5 x (idle, ready) + 4
+// preparations + attention end, logits (idle, ready, prepared), exit (idle, ready).
+inline unsigned decode_trace_points(unsigned layers) { return 1 + 15 * layers + 3 + 2; }
+int decode_supported(const DecodeGeometry &g, unsigned type_out);
+size_t decode_partials_bytes(const DecodeGeometry &g, int grid);
+unsigned decode_max_tiles(const DecodeGeometry &g);
+int decode_grid(int sms, const DecodeGeometry &g);
+int launch_decode(const DecodeLaunch &L, cudaStream_t s);
+
 }  // namespace fyb

@@ -331,6 +331,16 @@ struct Plan {
     std::vector<uint16_t> kv_stage;
     // profiling: when set, an event is recorded after every launch
     std::vector<std::pair<cudaEvent_t, int>> *marks = nullptr;
+    // persistent decode kernel (decode.cu); dec_grid == 0: per-kernel launches
+    int dec_grid = 0;
+    DecodeLayer *dec_layers = nullptr;
+    DecodeSync dec_sync;
+    float *dec_xm = nullptr, *dec_partials = nullptr, *dec_attn = nullptr;
+    double *dec_ss = nullptr;  // [2][d/16]: per-tile sums of squares after O and after down
+    unsigned dec_splits = 1;
+    size_t dec_bytes = 0;
+    unsigned dec_ring_bytes = 6720;  // per-warp weight ring; NYA_CUDA_RING_BYTES (0 = largest)
+    int dec_l2_prefetch = 0;         // NYA_CUDA_L2_PREFETCH=1 prefetches each next phase into L2
 };
 
 static void *plan_alloc(Plan *p, size_t bytes)
@@ -489,8 +499,40 @@ static AttentionLaunch attention_launch(const Plan *p, unsigned l)
 // Enqueue one decode step reading {token, position} from p->request.
 // Residual stream: x[cur] holds the stream, `delta` the last branch output
 // not yet added; the kernel that adds it writes the sum to x[cur ^ 1].
+static DecodeLaunch persistent_launch(const Plan *p, StepMode mode)
+{
+    DecodeLaunch L;
+    L.g.nl = p->nl; L.g.d = p->d; L.g.H = p->H; L.g.Hkv = p->Hkv; L.g.hd = p->hd; L.g.ffn = p->ffn; L.g.V = p->V;
+    L.g.capacity = (unsigned)p->capacity;
+    L.layers = p->dec_layers;
+    L.out_head = p->out_head; L.out_norm = p->out_norm;
+    L.embd = (const unsigned char *)p->embd; L.embd_row_bytes = p->embd_row_bytes; L.embd_type = p->embd_type;
+    L.eps = p->eps; L.attn_scale = 1.0f / std::sqrt((float)p->hd);
+    L.rope_cos = p->rope_cos; L.rope_sin = p->rope_sin;
+    L.request = p->request;
+    L.xa = p->x[0]; L.xm = p->dec_xm; L.q = p->q; L.attn = p->attn; L.h = p->h; L.logits = p->logits;
+    L.ss_o = p->dec_ss; L.ss_d = p->dec_ss + p->d / 16;
+    L.sync = p->dec_sync;
+    L.partials = p->dec_partials;
+    L.attn_partials = p->dec_attn; L.attn_splits = p->dec_splits;
+    L.argmax_key = p->argmax_key; L.argmax_token = p->argmax_token; L.tokens_log = p->tokens_log;
+    L.error = p->err_dev;
+    L.logits_mode = mode == STEP_NO_LOGITS ? 0 : mode == STEP_GREEDY ? 2 : 1;
+    L.grid = p->dec_grid;
+    L.ring_bytes = p->dec_ring_bytes;
+    L.l2_prefetch = p->dec_l2_prefetch;
+    return L;
+}
+
+static int enqueue_persistent(Plan *p, StepMode mode)
+{
+    p->launches = 1;
+    return launch_decode(persistent_launch(p, mode), p->ctx->stream);
+}
+
 static int enqueue_step(Plan *p, StepMode mode)
 {
+    if (p->dec_grid && !p->marks) return enqueue_persistent(p, mode);
     cudaStream_t s = p->ctx->stream;
     const bool pdl = true;
     p->launches = 0;
@@ -613,6 +655,66 @@ static int upload_fused(Plan *p, const nya_llm_tensor *const *t, int n, int mode
     if (r) return -1;
     out->units = units; out->type = type; out->cols = (unsigned)cols; out->tiles = (unsigned)total;
     return 0;
+}
+
+// Buffers of the persistent decode kernel. Returns false only on an
+// allocation or copy failure; an unsupported geometry leaves dec_grid 0 and
+// the plan runs the per-kernel step.
+static bool setup_persistent(Plan *p)
+{
+    const char *env = std::getenv("NYA_CUDA_PERSISTENT");
+    if (env && !std::strcmp(env, "0")) return true;
+    size_t v;
+    if (env_size("NYA_CUDA_RING_BYTES", &v)) p->dec_ring_bytes = (unsigned)std::min<size_t>(v, 1u << 20);
+    const char *pf = std::getenv("NYA_CUDA_L2_PREFETCH");
+    p->dec_l2_prefetch = pf && !std::strcmp(pf, "1");
+    DecodeGeometry g;
+    g.nl = p->nl; g.d = p->d; g.H = p->H; g.Hkv = p->Hkv; g.hd = p->hd; g.ffn = p->ffn; g.V = p->V;
+    g.capacity = (unsigned)p->capacity;
+    if (!decode_supported(g, p->out_head.type)) return true;
+    const int grid = decode_grid(p->ctx->sms, g);
+    if (grid <= 0) return true;
+    cudaStream_t s = p->ctx->stream;
+    bool ok = true;
+    auto A = [&](size_t bytes) -> void * {
+        void *x = ok ? plan_alloc(p, bytes) : nullptr;
+        if (!x) ok = false;
+        p->dec_bytes += bytes;
+        return x;
+    };
+    const unsigned G = p->H / p->Hkv, dt = p->d / 16;
+    const size_t words = (size_t)p->nl * p->Hkv + 4 * (size_t)p->nl + decode_max_tiles(g) + p->Hkv + 3;
+    unsigned *w = (unsigned *)A(words * 4);
+    std::vector<DecodeLayer> layers(p->nl);
+    for (unsigned l = 0; l < p->nl; ++l) {
+        DecodeLayer &L = layers[l];
+        L.qkv = p->layers[l].qkv; L.o = p->layers[l].o; L.gateup = p->layers[l].gateup; L.down = p->layers[l].down;
+        L.attn_norm = p->layers[l].attn_norm; L.ffn_norm = p->layers[l].ffn_norm;
+        L.kcache = p->kcache + (size_t)l * p->Hkv * p->capacity * p->hd;
+        L.vcache = p->vcache + (size_t)l * p->Hkv * p->capacity * p->hd;
+    }
+    p->dec_layers = (DecodeLayer *)A(layers.size() * sizeof(DecodeLayer));
+    p->dec_xm = (float *)A((size_t)p->d * 4);
+    p->dec_ss = (double *)A((size_t)2 * dt * 8);
+    p->dec_partials = (float *)A(decode_partials_bytes(g, grid));
+    p->dec_splits = (unsigned)std::max(1, std::min(32, grid / (int)p->Hkv));
+    p->dec_attn = (float *)A((size_t)p->Hkv * p->dec_splits * G * (p->hd + 2) * 4);
+    if (!ok) return false;
+    DecodeSync &y = p->dec_sync;
+    y.qkv_done = w; w += (size_t)p->nl * p->Hkv;
+    y.attn_done = w; w += p->nl;
+    y.o_done = w; w += p->nl;
+    y.gu_done = w; w += p->nl;
+    y.down_done = w; w += p->nl;
+    y.tile_counters = w; w += decode_max_tiles(g);
+    y.attn_counters = w; w += p->Hkv;
+    y.exit_count = w++; y.abort_flag = w++; y.logit_tiles = w++;
+    if (cudaMemsetAsync(y.qkv_done, 0, words * 4, s) != cudaSuccess ||
+        !upload(p->dec_layers, layers.data(), layers.size() * sizeof(DecodeLayer), s) ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return false;
+    p->dec_grid = grid;
+    return true;
 }
 
 static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity)
@@ -755,6 +857,7 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
         if (ok) ok = cudaMemsetAsync(p->counters, 0, tiles * 4, c->stream) == cudaSuccess &&
                      cudaMemsetAsync(p->attn_ws, 0, p->attn_ws_bytes, c->stream) == cudaSuccess;
     }
+    if (ok) ok = setup_persistent(p);
     if (ok) ok = cudaStreamSynchronize(c->stream) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
     if (!ok) {
         debug("resident plan setup failed; rolling back", cudaGetLastError());
@@ -763,7 +866,7 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
     }
     p->stats.weights_bytes = weights;
     p->stats.kv_bytes = kv_bytes;
-    p->stats.scratch_bytes = act + p->counters_capacity * 4 + p->partials_bytes + p->attn_ws_bytes;
+    p->stats.scratch_bytes = act + p->counters_capacity * 4 + p->partials_bytes + p->attn_ws_bytes + p->dec_bytes;
     p->stats.prefill_batch = 1;
     return p;
 }
@@ -1027,8 +1130,41 @@ extern "C" unsigned long long fyb_plan_launches_per_token(const void *opaque)
 {
     const Plan *p = (const Plan *)opaque;
     if (!p) return 0;
+    if (p->dec_grid) return 2;  // request + the persistent decode kernel
     // request (1) + gather (1) + 5 per layer + logits (1)
     return 3ull + 5ull * p->nl;
+}
+
+extern "C" long fyb_plan_trace(void *opaque, uint32_t token, size_t position, unsigned long long *out,
+    size_t out_count, unsigned *grid_out, unsigned long long *warp_out, size_t warp_count)
+{
+    Plan *p = (Plan *)opaque;
+    if (!p || p->failed || !p->dec_grid || token >= p->V || position >= p->capacity || position > p->valid || !out)
+        return -1;
+    const unsigned points = decode_trace_points(p->nl);
+    const size_t n = (size_t)points * p->dec_grid;
+    if (out_count < n) return -1;
+    DeviceScope scope(p->ctx->device);
+    cudaStream_t s = p->ctx->stream;
+    const size_t wn = ((size_t)p->nl * 5 + 1) * p->dec_grid * 16 * 4;
+    if (warp_out && warp_count < wn) return -1;
+    unsigned long long *buf = nullptr, *wbuf = nullptr;
+    if (cudaMalloc(&buf, n * 8) != cudaSuccess) { cudaGetLastError(); return -1; }
+    if (warp_out && cudaMalloc(&wbuf, wn * 8) != cudaSuccess) { cudaGetLastError(); cudaFree(buf); return -1; }
+    DecodeLaunch L = persistent_launch(p, STEP_LOGITS);
+    L.trace = buf; L.trace_slots = points; L.wtrace = wbuf;
+    int r = cudaMemsetAsync(buf, 0, n * 8, s) == cudaSuccess &&
+            (!wbuf || cudaMemsetAsync(wbuf, 0, wn * 8, s) == cudaSuccess) &&
+            set_request(p, token, (unsigned)position) == 0 &&
+            launch_decode(L, s) == 0 && cudaMemcpyAsync(out, buf, n * 8, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+            (!wbuf || cudaMemcpyAsync(warp_out, wbuf, wn * 8, cudaMemcpyDeviceToHost, s) == cudaSuccess) &&
+            cudaStreamSynchronize(s) == cudaSuccess && !*(volatile unsigned *)p->err_host ? 0 : -1;
+    cudaFree(buf);
+    if (wbuf) cudaFree(wbuf);
+    if (r) return plan_fail(p, position);
+    p->valid = std::max(p->valid, position + 1);
+    if (grid_out) *grid_out = (unsigned)p->dec_grid;
+    return points;
 }
 
 extern "C" int fyb_plan_profile(void *opaque, uint32_t token, size_t position, size_t steps, double *out)

@@ -236,12 +236,13 @@ FYB_DEV void prepare_x(const QgParams &p, signed char *xl, unsigned xstride, int
 }
 
 // ------------------------------------------------------------ tile completion
+template <int NV>
 FYB_DEV void finish_tile(const QgParams &p, unsigned tile, unsigned tile_units, const RowPair &rp, float accA,
     float accB, unsigned long long NW, unsigned long long gw, unsigned lane)
 {
     const unsigned nblk = p.nblk, gid = lane >> 2, tig = lane & 3, v = tig >> 1;
-    float yA = accA + __shfl_xor_sync(0xffffffffu, accA, 1);  // the two limb halves
-    float yB = accB + __shfl_xor_sync(0xffffffffu, accB, 1);
+    float yA = lane_total<NV>(accA);  // the limb halves (and the split minimum term)
+    float yB = lane_total<NV>(accB);
     if (tile_units != nblk) {
         const unsigned long long U = p.total_units;
         const unsigned long long t0 = (unsigned long long)tile * nblk;
@@ -261,23 +262,23 @@ FYB_DEV void finish_tile(const QgParams &p, unsigned tile, unsigned tile_units, 
         old = __shfl_sync(0xffffffffu, old, 0);
         if (old + tile_units != nblk) return;
         __threadfence();
-        yA = 0.f; yB = 0.f;
-        // sum, in column order, the slots of the warps whose unit ranges
-        // intersect this tile (warps without units own no slot)
-        for (unsigned s = 0; s < nslots; ++s) {
+        // the slots of the warps whose unit ranges intersect this tile (warps
+        // without units own no slot); lanes tig and tig ^ 1 split them
+        auto has_units = [&](unsigned s) {
             const unsigned long long g = owner0 + s;
             const unsigned long long ub = g * U / NW, ue = (g + 1) * U / NW;
-            if (ue <= ub || ub >= t0 + nblk || ue <= t0) continue;
-            yA += __ldcg(base + s * 32 + gid * 2 + v);
-            yB += __ldcg(base + s * 32 + (gid + 8) * 2 + v);
-        }
+            return !(ue <= ub || ub >= t0 + nblk || ue <= t0);
+        };
+        sum_slots(base, 32, gid * 2 + v, (gid + 8) * 2 + v, nslots, tig & 1, 2, has_units, yA, yB);
+        yA += __shfl_xor_sync(0xffffffffu, yA, 1);
+        yB += __shfl_xor_sync(0xffffffffu, yB, 1);
         if (lane == 0) p.counters[tile] = 0;
     }
     epilogue(p, rp, yA, yB, lane);
 }
 
 // ------------------------------------------------------------ the kernel
-template <unsigned TYPE>
+template <unsigned TYPE, int NV>
 __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QgParams p)
 {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -322,9 +323,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QgParams p)
     prepare_x(p, xl, xstride, exps, gsums, red);
     __syncthreads();
 
-    const bool brow_ok = (lane >> 2) < (unsigned)(4 * p.nvec);
     float accA = 0.f, accB = 0.f;
     unsigned tile = (unsigned)(u0 / nblk), tile_units = 0;
+    unsigned blk = (unsigned)(u0 - (unsigned long long)tile * nblk);  // advanced per unit, no division
     RowPair rp = tile_rows(p, tile, lane >> 2);
     for (unsigned i = 0; i < n; ++i) {
         const unsigned long long u = u0 + i;
@@ -333,9 +334,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QgParams p)
             if (p.error) *(volatile unsigned *)p.error = ERR_TIMEOUT;
             return;
         }
-        const unsigned blk = (unsigned)(u % nblk);
-        compute_unit<TYPE>(stages + s * UB, blk, xl, xstride, brow_ok, exps, nblk, gsums, K / 32, p.nvec, lane,
-                           accA, accB);
+        compute_unit<TYPE, NV>(stages + s * UB, blk, xl, xstride, exps, nblk, gsums, K / 32, lane, accA, accB);
         __syncwarp();
         if (lane == 0 && i + QG_STAGES < n) {
             fence_proxy_async();
@@ -344,14 +343,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(const QgParams p)
         }
         ++tile_units;
         if (blk + 1 == nblk || i + 1 == n) {
-            finish_tile(p, tile, tile_units, rp, accA, accB, NW, gw, lane);
+            finish_tile<NV>(p, tile, tile_units, rp, accA, accB, NW, gw, lane);
             accA = 0.f; accB = 0.f;
             tile_units = 0;
             if (i + 1 < n) {
-                tile = (unsigned)((u + 1) / nblk);
+                ++tile;
                 rp = tile_rows(p, tile, lane >> 2);
             }
         }
+        blk = blk + 1 == nblk ? 0 : blk + 1;
     }
 }
 
@@ -539,7 +539,8 @@ int launch_qgemv(const QgemvLaunch &L, cudaStream_t s)
     p.partials = L.partials;
     p.counters = L.counters;
     const size_t smem = qgemv_smem(w.type, p.K, p.nvec);
-    auto kern = w.type == T_Q4_K ? qgemv_kernel<T_Q4_K> : qgemv_kernel<T_Q6_K>;
+    auto kern = w.type == T_Q4_K ? (p.nvec == 1 ? qgemv_kernel<T_Q4_K, 1> : qgemv_kernel<T_Q4_K, 2>)
+                                 : (p.nvec == 1 ? qgemv_kernel<T_Q6_K, 1> : qgemv_kernel<T_Q6_K, 2>);
     // The max-shared carveout lets the next kernel's CTAs (programmatic
     // dependent launch) sit next to this one and start their weight streams.
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||

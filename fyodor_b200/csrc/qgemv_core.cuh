@@ -17,7 +17,7 @@ namespace fyb {
 constexpr int QG_WARPS = FYB_QG_WARPS;   // warps per CTA, one CTA per SM
 constexpr int QG_THREADS = QG_WARPS * 32;
 constexpr int QG_STAGES = FYB_QG_STAGES; // bulk-copy stages per warp
-constexpr int QG_XPAD = 16;  // limb-row stride = 16 (mod 128) bytes: conflict-free B fragments
+constexpr int QG_XPAD = 64;  // limb-row stride = 64 (mod 128) bytes: conflict-free B fragments
 
 constexpr unsigned Q4_UNIT = 2304;  // qs [p4][h2][r16][16] | hdr [r16][16]
 constexpr unsigned Q6_UNIT = 3360;  // ql [c4][h2][r16][16] | qh [c2][h2][r16][16] | sc [r16][16] | d [r16] f16
@@ -53,75 +53,96 @@ FYB_DEV void load_frag(unsigned (&r)[4], const unsigned char *base, unsigned lan
 }
 
 // ------------------------------------------------------------ per-unit math
+// x limbs in shared memory: four rows per vector (limb 0..3), row stride
+// K + QG_XPAD bytes. Within every 64-byte chunk the 4-byte words are stored
+// lane-major: word 4j + t of the natural order sits at position 4t + j, so
+// the B fragments a lane needs from one chunk (natural words t, 4+t, 8+t,
+// 12+t for lane t) are one 16-byte load, and the Q6_K pairs one 8-byte load.
+// A row stride of 64 (mod 128) bytes keeps those loads free of bank conflicts.
+FYB_HOST_DEV unsigned limb_pos(unsigned byte)  // natural byte offset -> stored offset
+{
+    const unsigned chunk = byte & ~63u, w = (byte & 63u) >> 2;
+    return chunk + ((w & 3u) * 4u + (w >> 2)) * 4u + (byte & 3u);
+}
+
 // Accumulates one unit (16 rows x 256 columns, from shared memory) into
-// accA (row gid) / accB (row gid+8). Lane (gid, tig) holds matrix columns
-// 2*tig and 2*tig+1 = vector tig/2, limbs 2*(tig&1) and 2*(tig&1)+1.
-template <unsigned TYPE>
+// accA (row gid) / accB (row gid+8) of lane (gid, tig). The MMA result
+// columns of a lane are limbs 2*(tig&1), 2*(tig&1)+1 of vector tig>>1; with
+// NV == 1, lanes tig 2 and 3 see zero B columns. The Q4_K minimum term is
+// split over the lanes that share a vector (all four with NV == 1, two with
+// NV == 2), so a tile's value is the sum of accA over those lanes.
+template <unsigned TYPE, int NV>
 FYB_DEV void compute_unit(const unsigned char *u, unsigned blk, const signed char *xl, unsigned xstride,
-    bool brow_ok, const int *exps, unsigned nblk, const float *gsums, unsigned ngroups, int nvec,
-    unsigned lane, float &accA, float &accB)
+    const int *exps, unsigned nblk, const float *gsums, unsigned ngroups, unsigned lane, float &accA, float &accB)
 {
     const unsigned gid = lane >> 2, tig = lane & 3, vec = tig >> 1;
+    const bool brow_ok = gid < 4u * NV;
     const int l0 = 2 * (tig & 1);
-    const signed char *xrow = xl + (size_t)(brow_ok ? gid : 0) * xstride + blk * 256u;
+    const signed char *xrow = xl + (size_t)(brow_ok ? gid : 0) * xstride + blk * 256u + tig * 16u;
     int T0 = 0, T1 = 0, T2 = 0, T3 = 0;
     if constexpr (TYPE == T_Q4_K) {
         const uint4 hA = *reinterpret_cast<const uint4 *>(u + 2048 + gid * 16);
         const uint4 hB = *reinterpret_cast<const uint4 *>(u + 2048 + (gid + 8) * 16);
-        // the 8 six-bit scales of both rows, unpacked once (llm_quant.c:249)
+        // six-bit scales (llm_quant.c:249): groups 0-3 in .y, 4-7 in .w/.y
         const unsigned scA0 = hA.y & 0x3F3F3F3Fu, scA1 = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
         const unsigned scB0 = hB.y & 0x3F3F3F3Fu, scB1 = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
-        int sA[8], sB[8];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            sA[g] = ubyte(scA0, g); sA[g + 4] = ubyte(scA1, g);
-            sB[g] = ubyte(scB0, g); sB[g + 4] = ubyte(scB1, g);
-        }
+        int U0 = 0, U1 = 0, U2 = 0, U3 = 0;  // high-nibble groups, 16x (the nibbles stay in place)
 #pragma unroll
         for (int pr = 0; pr < 4; ++pr) {
             unsigned q[4];
             load_frag(q, u + pr * 512, lane);
-            unsigned blo0 = 0, blo1 = 0, bhi0 = 0, bhi1 = 0;
-            if (brow_ok) {
-                const signed char *g0 = xrow + 64 * pr, *g1 = g0 + 32;
-                blo0 = *reinterpret_cast<const unsigned *>(g0 + 4 * tig);
-                blo1 = *reinterpret_cast<const unsigned *>(g0 + 16 + 4 * tig);
-                bhi0 = *reinterpret_cast<const unsigned *>(g1 + 4 * tig);
-                bhi1 = *reinterpret_cast<const unsigned *>(g1 + 16 + 4 * tig);
-            }
+            uint4 bw = make_uint4(0u, 0u, 0u, 0u);
+            if (brow_ok) bw = *reinterpret_cast<const uint4 *>(xrow + 64 * pr);
             const unsigned alo[4] = {q[0] & 0x0F0F0F0Fu, q[1] & 0x0F0F0F0Fu, q[2] & 0x0F0F0F0Fu, q[3] & 0x0F0F0F0Fu};
-            const unsigned ahi[4] = {(q[0] >> 4) & 0x0F0F0F0Fu, (q[1] >> 4) & 0x0F0F0F0Fu,
-                                     (q[2] >> 4) & 0x0F0F0F0Fu, (q[3] >> 4) & 0x0F0F0F0Fu};
+            const unsigned ahi[4] = {q[0] & 0xF0F0F0F0u, q[1] & 0xF0F0F0F0u, q[2] & 0xF0F0F0F0u, q[3] & 0xF0F0F0F0u};
             int dlo[4] = {0, 0, 0, 0}, dhi[4] = {0, 0, 0, 0};
-            mma_u8s8_k32(dlo, alo, blo0, blo1);
-            mma_u8s8_k32(dhi, ahi, bhi0, bhi1);
-            T0 += sA[2 * pr] * dlo[0] + sA[2 * pr + 1] * dhi[0];
-            T1 += sA[2 * pr] * dlo[1] + sA[2 * pr + 1] * dhi[1];
-            T2 += sB[2 * pr] * dlo[2] + sB[2 * pr + 1] * dhi[2];
-            T3 += sB[2 * pr] * dlo[3] + sB[2 * pr + 1] * dhi[3];
+            mma_u8s8_k32(dlo, alo, bw.x, bw.y);
+            mma_u8s8_k32(dhi, ahi, bw.z, bw.w);
+            const unsigned wA = pr < 2 ? scA0 : scA1, wB = pr < 2 ? scB0 : scB1;
+            const int b0 = (2 * pr) & 3, b1 = b0 + 1;
+            const int sAl = (int)__byte_perm(wA, 0u, 0x4440 + b0), sAh = (int)__byte_perm(wA, 0u, 0x4440 + b1);
+            const int sBl = (int)__byte_perm(wB, 0u, 0x4440 + b0), sBh = (int)__byte_perm(wB, 0u, 0x4440 + b1);
+            T0 += sAl * dlo[0]; U0 += sAh * dhi[0];
+            T1 += sAl * dlo[1]; U1 += sAh * dhi[1];
+            T2 += sBl * dlo[2]; U2 += sBh * dhi[2];
+            T3 += sBl * dlo[3]; U3 += sBh * dhi[3];
         }
+        T0 += U0 >> 4; T1 += U1 >> 4; T2 += U2 >> 4; T3 += U3 >> 4;  // exact: U is a multiple of 16
         const float dA = half_bits_to_float((unsigned short)(hA.x & 0xffffu));
         const float dB = half_bits_to_float((unsigned short)(hB.x & 0xffffu));
-        const int E = vec < (unsigned)nvec ? exps[vec * nblk + blk] : 0;
+        const int E = vec < (unsigned)NV ? exps[vec * nblk + blk] : 0;
         const float f0 = pow2f(E - 6 - 7 * l0), f1 = pow2f(E - 6 - 7 * (l0 + 1));
         accA = fmaf(dA, fmaf((float)T0, f0, (float)T1 * f1), accA);
         accB = fmaf(dB, fmaf((float)T2, f0, (float)T3 * f1), accB);
-        // minimum term -dmin * sum_g m_g * sum(x_g): lane tig&1 == 0 adds it for
-        // row A, its neighbour for row B (the pair is summed when the tile ends)
-        if (vec < (unsigned)nvec) {
-            const uint4 h = (tig & 1) ? hB : hA;
-            const unsigned mn0 = h.z & 0x3F3F3F3Fu, mn1 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-            const float *gs = gsums + (size_t)vec * ngroups + blk * 8;  // this block's 8 group sums
-            const float4 s0 = *reinterpret_cast<const float4 *>(gs);
-            const float4 s1 = *reinterpret_cast<const float4 *>(gs + 4);
-            float b = (float)ubyte(mn0, 0) * s0.x;
-            b = fmaf((float)ubyte(mn0, 1), s0.y, b); b = fmaf((float)ubyte(mn0, 2), s0.z, b);
-            b = fmaf((float)ubyte(mn0, 3), s0.w, b); b = fmaf((float)ubyte(mn1, 0), s1.x, b);
-            b = fmaf((float)ubyte(mn1, 1), s1.y, b); b = fmaf((float)ubyte(mn1, 2), s1.z, b);
-            b = fmaf((float)ubyte(mn1, 3), s1.w, b);
-            const float dmin = half_bits_to_float((unsigned short)(h.x >> 16));
-            if (tig & 1) accB = fmaf(-dmin, b, accB);
-            else accA = fmaf(-dmin, b, accA);
+        // minimum term -dmin * sum_g m_g * sum(x_g) of both rows; with NV == 1
+        // lane tig takes groups 2tig, 2tig+1, with NV == 2 groups 4(tig&1)..+3
+        if (NV == 1 || vec < (unsigned)NV) {  // with one vector all four lanes take a share
+            const unsigned mA0 = hA.z & 0x3F3F3F3Fu, mA1 = ((hA.w >> 4) & 0x0F0F0F0Fu) | ((hA.z >> 2) & 0x30303030u);
+            const unsigned mB0 = hB.z & 0x3F3F3F3Fu, mB1 = ((hB.w >> 4) & 0x0F0F0F0Fu) | ((hB.z >> 2) & 0x30303030u);
+            const float *gs = gsums + (size_t)(NV == 1 ? 0u : vec) * ngroups + blk * 8;  // the block's 8 group sums
+            const float dmA = half_bits_to_float((unsigned short)(hA.x >> 16));
+            const float dmB = half_bits_to_float((unsigned short)(hB.x >> 16));
+            float bA = 0.f, bB = 0.f;
+            if constexpr (NV == 1) {
+                const float2 g2 = *reinterpret_cast<const float2 *>(gs + 2 * tig);
+                const unsigned wA = tig < 2 ? mA0 : mA1, wB = tig < 2 ? mB0 : mB1;
+                const unsigned o = (2 * tig) & 3;
+                bA = fmaf((float)__byte_perm(wA, 0u, 0x4440 + o + 1), g2.y, (float)__byte_perm(wA, 0u, 0x4440 + o) * g2.x);
+                bB = fmaf((float)__byte_perm(wB, 0u, 0x4440 + o + 1), g2.y, (float)__byte_perm(wB, 0u, 0x4440 + o) * g2.x);
+            } else {
+                const float4 g4 = *reinterpret_cast<const float4 *>(gs + 4 * (tig & 1));
+                const unsigned wA = (tig & 1) ? mA1 : mA0, wB = (tig & 1) ? mB1 : mB0;
+                bA = (float)__byte_perm(wA, 0u, 0x4440) * g4.x;
+                bA = fmaf((float)__byte_perm(wA, 0u, 0x4441), g4.y, bA);
+                bA = fmaf((float)__byte_perm(wA, 0u, 0x4442), g4.z, bA);
+                bA = fmaf((float)__byte_perm(wA, 0u, 0x4443), g4.w, bA);
+                bB = (float)__byte_perm(wB, 0u, 0x4440) * g4.x;
+                bB = fmaf((float)__byte_perm(wB, 0u, 0x4441), g4.y, bB);
+                bB = fmaf((float)__byte_perm(wB, 0u, 0x4442), g4.z, bB);
+                bB = fmaf((float)__byte_perm(wB, 0u, 0x4443), g4.w, bB);
+            }
+            accA = fmaf(-dmA, bA, accA);
+            accB = fmaf(-dmB, bB, accB);
         }
     } else {
         const uint4 sA = *reinterpret_cast<const uint4 *>(u + 3072 + gid * 16);
@@ -143,18 +164,15 @@ FYB_DEV void compute_unit(const unsigned char *u, unsigned blk, const signed cha
 #define FYB_Q6(QQ) for (int i = 0; i < 4; ++i) a[i] = q6_signed<QQ>(ql[i], qh[i]);
                     if (Q == 0) { FYB_Q6(0) } else if (Q == 1) { FYB_Q6(1) } else if (Q == 2) { FYB_Q6(2) } else { FYB_Q6(3) }
 #undef FYB_Q6
-                    unsigned b1 = 0, b2 = 0;
-                    if (brow_ok) {
-                        b1 = *reinterpret_cast<const unsigned *>(xrow + h * 128 + Q * 32 + 4 * tig);
-                        b2 = *reinterpret_cast<const unsigned *>(xrow + h * 128 + Q * 32 + 16 + 4 * tig);
-                    }
+                    uint2 bw = make_uint2(0u, 0u);
+                    if (brow_ok) bw = *reinterpret_cast<const uint2 *>(xrow + (2 * h + (Q >> 1)) * 64 + 8 * (Q & 1));
                     int d1[4] = {0, 0, 0, 0}, d2[4] = {0, 0, 0, 0};
                     asm volatile(
                         "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
-                        : "+r"(d1[0]), "+r"(d1[1]), "+r"(d1[2]), "+r"(d1[3]) : "r"(a[0]), "r"(a[1]), "r"(b1));
+                        : "+r"(d1[0]), "+r"(d1[1]), "+r"(d1[2]), "+r"(d1[3]) : "r"(a[0]), "r"(a[1]), "r"(bw.x));
                     asm volatile(
                         "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
-                        : "+r"(d2[0]), "+r"(d2[1]), "+r"(d2[2]), "+r"(d2[3]) : "r"(a[2]), "r"(a[3]), "r"(b2));
+                        : "+r"(d2[0]), "+r"(d2[1]), "+r"(d2[2]), "+r"(d2[3]) : "r"(a[2]), "r"(a[3]), "r"(bw.y));
                     const int g = h * 8 + Q * 2;  // first of the two 16-value scale groups
                     const unsigned wA = (&sA.x)[g >> 2], wB = (&sB.x)[g >> 2];
                     const int s1A = sbyte(wA, g & 3), s2A = sbyte(wA, (g & 3) + 1);
@@ -166,12 +184,21 @@ FYB_DEV void compute_unit(const unsigned char *u, unsigned blk, const signed cha
                 }
             }
         }
-        const int E = vec < (unsigned)nvec ? exps[vec * nblk + blk] : 0;
+        const int E = vec < (unsigned)NV ? exps[vec * nblk + blk] : 0;
         const float f0 = pow2f(E - 6 - 7 * l0), f1 = pow2f(E - 6 - 7 * (l0 + 1));
         accA = fmaf(dA, fmaf((float)T0, f0, (float)T1 * f1), accA);
         accB = fmaf(dB, fmaf((float)T2, f0, (float)T3 * f1), accB);
         (void)gsums; (void)ngroups;
     }
+}
+
+// Sum of a lane's tile accumulator over the lanes that share its vector.
+template <int NV>
+FYB_DEV float lane_total(float acc)
+{
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    if constexpr (NV == 1) acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    return acc;
 }
 
 FYB_DEV double block_sum_double(double v, double *red)
@@ -185,6 +212,32 @@ FYB_DEV double block_sum_double(double v, double *red)
     double t = 0;
     for (int w = 0; w < QG_WARPS; ++w) t += red[w];
     return t;
+}
+
+// Sum of the partial slots of the warps that share a stream-K tile. The
+// `ways` lanes that need the same values split the slots (slot s goes to the
+// lane with part == s % ways) and keep four slots' loads in flight at once;
+// has_units(s) tells whether the warp of slot s wrote it. The caller adds the
+// `ways` partial sums with shuffles, so the order is fixed by the geometry.
+template <class HasUnits>
+FYB_DEV void sum_slots(const float *base, unsigned slot_floats, unsigned offA, unsigned offB, unsigned nslots,
+    unsigned part, unsigned ways, HasUnits has_units, float &yA, float &yB)
+{
+    float a = 0.f, b = 0.f;
+    for (unsigned s0 = part; s0 < nslots; s0 += 4 * ways) {
+        float va[4], vb[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const unsigned s = s0 + j * ways;
+            const bool ok = s < nslots && has_units(s);
+            va[j] = ok ? __ldcg(base + (size_t)s * slot_floats + offA) : 0.f;
+            vb[j] = ok ? __ldcg(base + (size_t)s * slot_floats + offB) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { a += va[j]; b += vb[j]; }
+    }
+    yA = a;
+    yB = b;
 }
 
 FYB_DEV void load16(const float *src, float (&v)[16])
@@ -243,10 +296,14 @@ FYB_DEV void prep_slot(float (&x)[16], bool ok, unsigned v, unsigned sl, unsigne
             }
         }
         if (ok) {
+            // slot sl = natural words 4a..4a+3 of its chunk (a = sl % 4): stored at 4t + a
+            const unsigned chunk = (sl >> 2) * 64u, a4 = (sl & 3u) * 4u;
 #pragma unroll
-            for (int l = 0; l < 4; ++l)
-                *reinterpret_cast<uint4 *>(xl + (size_t)(v * 4 + l) * xstride + 16 * sl) =
-                    make_uint4(words[l][0], words[l][1], words[l][2], words[l][3]);
+            for (int l = 0; l < 4; ++l) {
+                signed char *row = xl + (size_t)(v * 4 + l) * xstride + chunk + a4;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) *reinterpret_cast<unsigned *>(row + 16 * t) = words[l][t];
+            }
         }
 }
 

@@ -102,13 +102,32 @@ int fyb_plan_decode_greedy(void *plan, uint32_t token, size_t position, size_t s
    a negative value on failure. */
 double fyb_plan_time_greedy(void *plan, uint32_t token, size_t position, size_t steps);
 
-/* Kernel launches issued per decode step by the plan (graph nodes). */
+/* Kernel launches of one plan_token step: the request update plus the
+   persistent decode kernel (2), or 3 + 5 per layer when the plan runs
+   one kernel per operation. */
 unsigned long long fyb_plan_launches_per_token(const void *plan);
 
 /* Average duration (ms) of each kernel class of one decode step measured
    with CUDA events around eager launches: out[0] matrix kernels, out[1]
    attention, out[2] other. Returns 0 on success. */
 int fyb_plan_profile(void *plan, uint32_t token, size_t position, size_t steps, double *out);
+
+/* Profiling of the persistent decode kernel (no reference counterpart): runs
+   one decode step of `token` at `position` with per-CTA trace points and
+   copies them to out[point * grid + cta] (globaltimer nanoseconds). Points
+   per CTA: start; per layer, for the QKV, attention, O, gate/up and down
+   phases, (CTA idle, dependency met) pairs, with a point after each input
+   preparation and after the CTA's attention items; logits (idle, met,
+   prepared); exit (idle, met). Returns the number of points per CTA and
+   stores the grid in *grid_out, or -1 (plan without the persistent kernel,
+   invalid arguments, out_count too small). With warp_out (may be NULL),
+   also per-warp points of every GEMV phase: warp_out[((layer*5 + phase) *
+   warps + warp) * 4 + k] (phase 0 QKV, 1 O, 2 gate/up, 3 down; layers*5 for
+   the logits), k = entry (ns), SM clock cycles spent waiting for weights,
+   units computed (ns), done (ns);
+   warp_count >= (layers*5 + 1) * grid * 16 * 4. */
+long fyb_plan_trace(void *plan, uint32_t token, size_t position, unsigned long long *out, size_t out_count,
+    unsigned *grid_out, unsigned long long *warp_out, size_t warp_count);
 
 /* Average milliseconds of one stand-alone launch of a fused projection
    kernel of `layer` (which: 0 QKV+RoPE+KV append, 1 attention output,

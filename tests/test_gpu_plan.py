@@ -117,6 +117,30 @@ def test_8b_layer_shapes(provider):
         assert np.argmax(plan.logits) == np.argmax(e)
 
 
+@pytest.mark.parametrize("name,cfg,tokens", SMALL_MODELS)
+def test_persistent_matches_per_kernel(provider, name, cfg, tokens):
+    """The persistent decode kernel (default) and the one-kernel-per-operation
+    step (NYA_CUDA_PERSISTENT=0) compute the same logits; they differ only in
+    summation order (sums of squares per tile, split-K partitions)."""
+    m = F.SynthModel(**cfg)
+    plan = provider.plan(m, len(tokens))
+    assert plan.launches_per_token() == 2  # request + one decode kernel
+    os.environ["NYA_CUDA_PERSISTENT"] = "0"
+    try:
+        multi = provider.plan(m, len(tokens))
+    finally:
+        del os.environ["NYA_CUDA_PERSISTENT"]
+    assert multi.launches_per_token() == 3 + 5 * cfg["layers"]
+    for i, t in enumerate(tokens):
+        assert plan.token(t, i) == 0 and multi.token(t, i) == 0
+        assert logit_error(plan.logits, multi.logits) <= 2e-4, (i, logit_error(plan.logits, multi.logits))
+        assert np.argmax(plan.logits) == np.argmax(multi.logits)
+    for layer in range(cfg["layers"]):
+        a, b = plan.read_kv(layer, 0, len(tokens)), multi.read_kv(layer, 0, len(tokens))
+        # fp16 cache: one rounding step at the largest magnitude is ~1e-3 of the scale
+        assert logit_error(a[0], b[0]) <= 1e-3 and logit_error(a[1], b[1]) <= 1e-3
+
+
 def _env_run(code, **env):
     e = dict(os.environ, **{k: str(v) for k, v in env.items()})
     return subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=e, capture_output=True, text=True, timeout=300)
