@@ -18,6 +18,7 @@ LIB = os.path.join(HERE, "libfyodor_b200.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "-I" + os.path.join(ROOT, "include")]
+COMMON += os.environ.get("FYB_NVCC_FLAGS", "").split()  # extra flags for experimental builds
 
 
 def _nvcc():

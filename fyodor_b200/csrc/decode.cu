@@ -146,7 +146,10 @@ FYB_DEV bool cta_wait(const DecodeParams &p, const unsigned *ctr, unsigned targe
             if (aborted(p)) break;
             if (!ctr || reached(ld_acquire(ctr), target)) { ok = 1; break; }
             if (i >= WAIT_LIMIT) { raise_abort(p, ERR_TIMEOUT); break; }
-            __nanosleep(32);
+#ifndef FYB_POLL_NS
+#define FYB_POLL_NS 32
+#endif
+            if (FYB_POLL_NS) __nanosleep(FYB_POLL_NS);
         }
         *flag = ok;
     }
@@ -622,10 +625,14 @@ FYB_HOST_DEV size_t attn_smem_floats(unsigned G, unsigned hd)
 
 // Partitions of the context per KV head for attended length L: one per
 // ATT_CHUNK positions, at most the plan's maximum.
-constexpr unsigned ATT_CHUNK = 32;
+#ifndef FYB_ATT_CHUNK
+#define FYB_ATT_CHUNK 32
+#endif
+constexpr unsigned ATT_CHUNK = FYB_ATT_CHUNK;
+constexpr unsigned ATT_MAX_PARTS = 16;  // partitions per KV head (the plan caps its maximum here)
 FYB_DEV unsigned attn_parts(const DecodeParams &p, unsigned L)
 {
-    return max(1u, min(p.attn_splits, (L + ATT_CHUNK - 1) / ATT_CHUNK));
+    return max(1u, min(min(p.attn_splits, ATT_MAX_PARTS), (L + ATT_CHUNK - 1) / ATT_CHUNK));
 }
 
 // Widen DPL fp16 values (DPL 4: uint2, DPL 2: one word) to float.
@@ -759,20 +766,33 @@ FYB_DEV void attention_item(const DecodeParams &p, unsigned l, unsigned kvh, uns
     __syncthreads();
     if (!*sm.flag) return;
     __threadfence();
+    // merge the S slots: their maxima and sums staged in shared memory (one
+    // round of loads), then every output element loads its S values at once
     const float *all = p.attn_partials + (size_t)kvh * S * SLOT;
+    float *sM = sm.wo, *sD = sm.wo + ATT_MAX_PARTS * G;
+    for (unsigned i = threadIdx.x; i < S * G; i += QG_THREADS) {
+        const unsigned s2 = i / G, g = i % G;
+        sM[i] = __ldcg(all + s2 * SLOT + g * (HD + 2) + HD);
+        sD[i] = __ldcg(all + s2 * SLOT + g * (HD + 2) + HD + 1);
+    }
+    __syncthreads();
     for (unsigned i = threadIdx.x; i < G * HD; i += QG_THREADS) {
         const unsigned g = i / HD, dd = i % HD;
+        float v[ATT_MAX_PARTS];
+#pragma unroll
+        for (unsigned s2 = 0; s2 < ATT_MAX_PARTS; ++s2)
+            v[s2] = s2 < S ? __ldcg(all + s2 * SLOT + g * (HD + 2) + dd) : 0.f;
         float M = -INFINITY;
-#pragma unroll 8
-        for (unsigned s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(all + s2 * SLOT + g * (HD + 2) + HD));
+        for (unsigned s2 = 0; s2 < S; ++s2) M = fmaxf(M, sM[s2 * G + g]);
         float acc = 0.f, den = 0.f;
-#pragma unroll 8
-        for (unsigned s2 = 0; s2 < S; ++s2) {
-            const float *sl = all + s2 * SLOT + g * (HD + 2);
-            const float ms = __ldcg(sl + HD);
-            const float f = ms == -INFINITY ? 0.f : expf(ms - M);
-            acc = fmaf(__ldcg(sl + dd), f, acc);
-            den = fmaf(__ldcg(sl + HD + 1), f, den);
+#pragma unroll
+        for (unsigned s2 = 0; s2 < ATT_MAX_PARTS; ++s2) {
+            if (s2 < S) {
+                const float ms = sM[s2 * G + g];
+                const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+                acc = fmaf(v[s2], f, acc);
+                den = fmaf(sD[s2 * G + g], f, den);
+            }
         }
         p.attn[((size_t)kvh * G + g) * HD + dd] = acc / den;
     }

@@ -697,7 +697,7 @@ static bool setup_persistent(Plan *p)
     p->dec_xm = (float *)A((size_t)p->d * 4);
     p->dec_ss = (double *)A((size_t)2 * dt * 8);
     p->dec_partials = (float *)A(decode_partials_bytes(g, grid));
-    p->dec_splits = (unsigned)std::max(1, std::min(32, grid / (int)p->Hkv));
+    p->dec_splits = (unsigned)std::max(1, std::min(16, grid / (int)p->Hkv));  // decode.cu ATT_MAX_PARTS
     p->dec_attn = (float *)A((size_t)p->Hkv * p->dec_splits * G * (p->hd + 2) * 4);
     if (!ok) return false;
     DecodeSync &y = p->dec_sync;
