@@ -663,7 +663,7 @@ FYB_DEV void load_half_row(const __half *src, float (&out)[DPL])
 template <int HD, int G>
 FYB_DEV void attention_item(const DecodeParams &p, unsigned l, unsigned kvh, unsigned sp, const AttnSmem &sm)
 {
-    constexpr int DPL = HD / 32, PB = G <= 2 ? 4 : 2;
+    constexpr int DPL = HD / 32, PB = G <= 2 ? 4 : G <= 4 ? 2 : 1;
     const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const unsigned L = __ldcg(p.request + 1) + 1;
     const unsigned S = attn_parts(p, L);
@@ -805,19 +805,17 @@ FYB_DEV void attention_item(const DecodeParams &p, unsigned l, unsigned kvh, uns
     }
 }
 
+template <int HD, int G>
 FYB_DEV bool attention_phase(const DecodeParams &p, unsigned l, unsigned step, const AttnSmem &sm)
 {
     const unsigned S = attn_parts(p, __ldcg(p.request + 1) + 1);
-    const unsigned G = p.H / p.Hkv, items = p.Hkv * S;
-    const unsigned per_step = G * p.hd / 16 + 2 * p.hd / 16;
+    const unsigned items = p.Hkv * S;
+    const unsigned per_step = G * HD / 16 + 2 * HD / 16;
     for (unsigned it = blockIdx.x; it < items; it += gridDim.x) {
         const unsigned kvh = it / S, sp = it % S;
         unsigned untraced = ~0u - 4;  // item counts differ between CTAs: not traced
         if (!cta_wait(p, p.sync.qkv_done + l * p.Hkv + kvh, step * per_step, sm.flag, untraced)) return false;
-#define FYB_AI(HDV, GV) if (p.hd == HDV && G == GV) attention_item<HDV, GV>(p, l, kvh, sp, sm);
-        FYB_AI(128, 1) FYB_AI(128, 2) FYB_AI(128, 4) FYB_AI(128, 8)
-        FYB_AI(64, 1) FYB_AI(64, 2) FYB_AI(64, 4) FYB_AI(64, 8)
-#undef FYB_AI
+        attention_item<HD, G>(p, l, kvh, sp, sm);
     }
     return true;
 }
@@ -847,6 +845,9 @@ FYB_HOST_DEV SmemLayout smem_layout(unsigned d, unsigned ffn, unsigned H, unsign
     return s;
 }
 
+// One instantiation per (head dimension, query heads per KV head): a plan
+// runs exactly one, so its registers are sized for that attention variant.
+template <int HD, int G>
 __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParams p)
 {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -869,7 +870,6 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
     unsigned long long *keys = reinterpret_cast<unsigned long long *>(smem + lay.parts + QG_WARPS * 2 * sizeof(PartSlot));
     unsigned *flag = reinterpret_cast<unsigned *>(smem + lay.misc);
     float *scale_smem = reinterpret_cast<float *>(flag + 1);
-    const unsigned G = p.H / p.Hkv;
     AttnSmem as;  // overlays the limb buffer, which is idle during attention
     as.wm = reinterpret_cast<float *>(smem + lay.xbuf);
     as.wl = as.wm + QG_WARPS * G;
@@ -898,7 +898,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
         stamp(p, ts);
         run_gemv(p, cur, ring, xb, lane, parts, keys); advance(p, cur);  // now the O projection
         // attention (its scratch overlays the limb buffer, idle now)
-        ok = cta_wait(p, nullptr, 0, flag, ts) && attention_phase(p, l, step, as);
+        ok = cta_wait(p, nullptr, 0, flag, ts) && attention_phase<HD, G>(p, l, step, as);
         stamp(p, ts);
         if (!ok) break;
         // output projection; residual add in the tile outputs
@@ -999,9 +999,22 @@ size_t decode_partials_bytes(const DecodeGeometry &g, int grid)
     return best;
 }
 
+using DecodeKernel = void (*)(const DecodeParams);
+static DecodeKernel decode_kernel_for(const DecodeGeometry &g)
+{
+    const unsigned G = g.Hkv ? g.H / g.Hkv : 0;
+#define FYB_DK(HDV, GV) if (g.hd == HDV && G == GV) return decode_kernel<HDV, GV>;
+    FYB_DK(128, 1) FYB_DK(128, 2) FYB_DK(128, 4) FYB_DK(128, 8)
+    FYB_DK(64, 1) FYB_DK(64, 2) FYB_DK(64, 4) FYB_DK(64, 8)
+#undef FYB_DK
+    return nullptr;
+}
+
 // One CTA per SM when one fits with the geometry's shared memory, else 0.
 int decode_grid(int sms, const DecodeGeometry &g)
 {
+    const DecodeKernel decode_kernel = decode_kernel_for(g);
+    if (!decode_kernel) return 0;
     const size_t smem = decode_smem_bytes(g);
     int per_sm = 0;
     if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
@@ -1037,6 +1050,8 @@ int launch_decode(const DecodeLaunch &L, cudaStream_t s)
     p.trace = L.trace; p.trace_slots = L.trace_slots;
     p.wtrace = L.wtrace;
     const size_t smem = decode_smem_bytes(L.g, L.ring_bytes);
+    const DecodeKernel decode_kernel = decode_kernel_for(L.g);
+    if (!decode_kernel) return -1;
     if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return -2;
     cudaLaunchConfig_t cfg = {};
