@@ -207,24 +207,26 @@ def run_provider(args):
     e2e_s = max_over_ranks(dist, time.perf_counter() - t0)
     e2e_value = e2e_steps * DECODE * world / e2e_s
 
-    # dominant kernel (fused gate/up GEMV, 66 MB of Q4_K) timed alone
+    # stand-alone GEMV kernels (the matvec/matmul entry points), for reference
     gate_ms, gate_bytes = plan.time_projection(0, 2, 20)
     qkv_ms, qkv_bytes = plan.time_projection(0, 0, 20)
     down_ms, down_bytes = plan.time_projection(0, 3, 20)
     o_ms, o_bytes = plan.time_projection(0, 1, 20)
     lg_ms, lg_bytes = plan.time_projection(0, 4, 10)
-    breakdown = plan.profile(first, PROMPT, 4)
+    phases = trace_summary(plan, first, PROMPT, model.config.layers)
     peaks, peak_kind = measured_peaks()
     hbm = peaks.get("hbm_gbs", 6650.0)
-    achieved = gate_bytes / (gate_ms / 1000.0) / 1e9
+    # the dominant kernel is the persistent decode kernel, one launch per token:
+    # algorithmic bytes per launch = weights + the KV cache read at that step
+    bpt = mean_bytes_per_token()
+    per_launch_ms = total_ms / (args.steps * DECODE)
+    achieved = bpt / (per_launch_ms / 1000.0) / 1e9
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get("qgemv_gateup_8b")
+            traffic = json.load(f).get("decode_kernel_8b")
     except (OSError, ValueError):
         pass
-    bpt = mean_bytes_per_token()
-    step_gbs = bpt * value / world / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -254,19 +256,16 @@ def run_provider(args):
                 "d2h_bytes_per_step": 4 * model.vocabulary * DECODE},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic,
-                     "kernel": "qgemv gate/up+SwiGLU (Q4_K 2x14336x4096), timed alone",
-                     "peak_source": peak_kind},
-        "step_roofline": {"bytes_per_token": int(bpt), "achieved_gbs": round(step_gbs, 1),
-                          "frac": round(step_gbs / hbm, 4), "tok_s_at_peak": round(hbm * 1e9 / bpt, 1)},
+                     "kernel": "decode_kernel (persistent, one launch per token; %d B per launch)" % int(bpt),
+                     "us_per_launch": round(per_launch_ms * 1000, 2), "peak_source": peak_kind,
+                     "tok_s_at_peak": round(hbm * 1e9 / bpt, 1)},
+        "decode_phases_us": phases,
         "kernels": {"qkv": [round(qkv_ms * 1e3, 2), round(qkv_bytes / qkv_ms / 1e6, 1)],
                     "o": [round(o_ms * 1e3, 2), round(o_bytes / o_ms / 1e6, 1)],
-                    "gateup": [round(gate_ms * 1e3, 2), round(achieved, 1)],
+                    "gateup": [round(gate_ms * 1e3, 2), round(gate_bytes / gate_ms / 1e6, 1)],
                     "down": [round(down_ms * 1e3, 2), round(down_bytes / down_ms / 1e6, 1)],
                     "logits": [round(lg_ms * 1e3, 2), round(lg_bytes / lg_ms / 1e6, 1)],
-                    "units": "[us per launch, GB/s]",
-                    "step_ms_by_class": None if breakdown is None else
-                    {"matrix": round(float(breakdown[0]), 4), "attention": round(float(breakdown[1]), 4),
-                     "other": round(float(breakdown[2]), 4)}},
+                    "units": "stand-alone GEMV launches (matvec/matmul path): [us per launch, GB/s]"},
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
@@ -346,13 +345,47 @@ def run_steps_mode(args):
     off) so an ncu launch list shows every kernel of a step."""
     os.environ["NYA_CUDA_GRAPHS"] = "0"
     import fyodor_b200 as F
-    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **dict(CFG8B, context=64))
+    layers = args.layers or CFG8B["layers"]
+    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K,
+                         **dict(CFG8B, context=64, layers=layers))
     provider = F.Provider()
     plan = provider.plan(model, 64)
     for i in range(args.eager_steps):
         if plan.token(17 + i, i) != 0:
             raise SystemExit("decode step failed")
     print(json.dumps({"eager_steps": args.eager_steps, "kernel_launches": plan.stats()["kernel_launches"]}))
+
+
+PHASE_KINDS = ["qkv", "attention", "o", "gateup", "down"]
+
+
+def summarize_trace(tr, layers):
+    """Per phase kind: CTA-median microseconds waiting for the input,
+    preparing it and working, summed over layers (trace of one step)."""
+    t = tr.astype(np.int64) - int(tr[0].min())
+    out = {k: {"wait": 0.0, "prep": 0.0, "work": 0.0} for k in PHASE_KINDS + ["logits"]}
+    for l in range(layers):
+        base = 1 + 15 * l
+        # layout per layer: qkv A B C | att A B C | o A B C | gu A B C | down A B C
+        for k in range(5):
+            a, b, c = t[base + 3 * k], t[base + 3 * k + 1], t[base + 3 * k + 2]
+            nxt = t[base + 3 * k + 3]  # the next phase's idle point (or logits / exit)
+            out[PHASE_KINDS[k]]["wait"] += float(np.median(b - a)) / 1e3
+            out[PHASE_KINDS[k]]["prep"] += float(np.median(c - b)) / 1e3 if k != 1 else 0.0
+            out[PHASE_KINDS[k]]["work"] += float(np.median(nxt - c if k != 1 else c - b)) / 1e3
+    lb = 1 + 15 * layers
+    out["logits"]["wait"] = float(np.median(t[lb + 1] - t[lb])) / 1e3
+    out["logits"]["prep"] = float(np.median(t[lb + 2] - t[lb + 1])) / 1e3
+    out["logits"]["work"] = float(np.median(t[lb + 3] - t[lb + 2])) / 1e3
+    res = {k: {x: round(v, 1) for x, v in d.items()} for k, d in out.items()}
+    res["step_us"] = round(float(t[-1].max()) / 1e3, 1)
+    return res
+
+
+def trace_summary(plan, token, position, layers):
+    """One traced persistent decode step (None when the plan does not use it)."""
+    tr = plan.trace(token, position)
+    return None if tr is None else summarize_trace(tr, layers)
 
 
 def run_trace_mode(args):
@@ -376,26 +409,9 @@ def run_trace_mode(args):
     if args.trace_raw:
         np.save(args.trace_raw, tr)
         np.save(args.trace_raw.replace(".npy", "") + "_warps.npy", res[1])
-    t = tr.astype(np.int64) - int(tr[0].min())
-    L = model.config.layers
-    kinds = ["qkv", "attention", "o", "gateup", "down"]
-    out = {k: {"wait": 0.0, "prep": 0.0, "work": 0.0} for k in kinds + ["logits"]}
-    for l in range(L):
-        base = 1 + 15 * l
-        # layout per layer: qkv A B C | att A B C | o A B C | gu A B C | down A B C
-        for k in range(5):
-            a, b, c = t[base + 3 * k], t[base + 3 * k + 1], t[base + 3 * k + 2]
-            nxt = t[base + 3 * k + 3]  # the next phase's idle point (or logits / exit)
-            out[kinds[k]]["wait"] += float(np.median(b - a)) / 1e3
-            out[kinds[k]]["prep"] += float(np.median(c - b)) / 1e3 if k != 1 else 0.0
-            out[kinds[k]]["work"] += float(np.median(nxt - c if k != 1 else c - b)) / 1e3
-    lb = 1 + 15 * L
-    out["logits"]["wait"] = float(np.median(t[lb + 1] - t[lb])) / 1e3
-    out["logits"]["prep"] = float(np.median(t[lb + 2] - t[lb + 1])) / 1e3
-    out["logits"]["work"] = float(np.median(t[lb + 3] - t[lb + 2])) / 1e3
-    total = float(t[-1].max()) / 1e3
-    print(json.dumps({"trace_us": {k: {x: round(v, 1) for x, v in d.items()} for k, d in out.items()},
-                      "step_us": round(total, 1), "grid": int(tr.shape[1]), "points": int(tr.shape[0])}))
+    res = summarize_trace(tr, model.config.layers)
+    step = res.pop("step_us")
+    print(json.dumps({"trace_us": res, "step_us": step, "grid": int(tr.shape[1]), "points": int(tr.shape[0])}))
 
 
 def main():
@@ -406,6 +422,7 @@ def main():
     ap.add_argument("--trace-step", type=int, default=0,
                     help="trace N persistent 8B decode steps per CTA and report the last (profiling)")
     ap.add_argument("--trace-raw", default="", help="with --trace-step: also save the raw trace (.npy)")
+    ap.add_argument("--layers", type=int, default=0, help="with --eager-steps: layers of the model (small ncu cases)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
