@@ -99,6 +99,9 @@ def _load():
                                          C.c_uint, C.c_float, _P, C.c_uint, _P, C.c_size_t, _P]
     lib.fyb_attention_decode_static.argtypes = [_P, _P, _P, C.c_size_t, _P, C.c_uint, C.c_uint, C.c_uint, C.c_uint,
                                                 C.c_uint, C.c_float, _P, C.c_uint, _P]
+    lib.fyb_plan_tp_info.argtypes = [_P, _P, _P]
+    lib.fyb_plan_tp_handle.argtypes = [_P, _P, C.c_size_t]
+    lib.fyb_plan_tp_connect.argtypes = [_P, _P, C.c_size_t]
     lib.fyb_plan_trace.restype = C.c_long
     lib.fyb_plan_trace.argtypes = [_P, C.c_uint32, C.c_size_t, _P, C.c_size_t, _P, _P, C.c_size_t]
     lib.fyb_plan_decode_greedy.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t, _P]
@@ -122,7 +125,8 @@ lib = _load()
 EXPORTS = ["nya_cuda_backend", "fyb_version", "fyb_device_count", "fyb_dequantize", "fyb_quant_matmul_workspace",
            "fyb_quant_matmul", "fyb_attention_workspace", "fyb_attention_decode",
            "fyb_attention_decode_static", "fyb_plan_decode_greedy",
-           "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_profile", "fyb_plan_trace", "fyb_plan_time_projection",
+           "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_profile", "fyb_plan_trace",
+           "fyb_plan_tp_info", "fyb_plan_tp_handle", "fyb_plan_tp_connect", "fyb_plan_time_projection",
            "fyb_synth_create",
            "fyb_synth_free", "fyb_synth_fill"]
 
@@ -175,6 +179,21 @@ class SynthModel:
 
 
 # ---------------------------------------------------------------- provider
+IPC_HANDLE_BYTES = 64  # FYB_IPC_HANDLE_BYTES
+
+
+def tp_exchange(handle, group=None):
+    """Gather every rank's exchange-region handle in rank order through a
+    torch.distributed group (any backend): the host side of connecting a
+    tensor-parallel plan."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, bytes(handle), group=group)
+    if any(h is None or len(h) != IPC_HANDLE_BYTES for h in out):
+        raise ValueError("a rank has no exchange-region handle")
+    return out
+
+
 class Provider:
     """A provider context: what nya_compute_create_for("cuda") owns.
 
@@ -260,6 +279,24 @@ class Plan:
 
     def launches_per_token(self):
         return lib.fyb_plan_launches_per_token(C.c_void_p(self.ptr))
+
+    def tp_info(self):
+        """(rank, size) of the plan's tensor-parallel shard."""
+        r, n = C.c_uint(0), C.c_uint(0)
+        lib.fyb_plan_tp_info(C.c_void_p(self.ptr), C.byref(r), C.byref(n))
+        return r.value, n.value
+
+    def tp_handle(self):
+        """This rank's exchange-region handle (bytes), or None."""
+        buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+        if lib.fyb_plan_tp_handle(C.c_void_p(self.ptr), buf, IPC_HANDLE_BYTES) != 0:
+            return None
+        return buf.raw
+
+    def tp_connect(self, handles):
+        """Open the other ranks' regions; handles: one bytes object per rank, in rank order."""
+        blob = b"".join(handles)
+        return lib.fyb_plan_tp_connect(C.c_void_p(self.ptr), C.c_char_p(blob), len(handles))
 
     def trace(self, token, position, warps=False):
         """Per-CTA trace points of one persistent decode step: array

@@ -69,6 +69,10 @@ struct DecodeParams {
     unsigned long long *trace;  // optional [stamp][CTA] globaltimer values
     unsigned trace_slots;
     unsigned long long *wtrace;  // optional [layer][phase kind][warp][4] globaltimer values
+    // tensor parallelism (tp > 1): H, Hkv, ffn and V above are this rank's
+    unsigned tp, tp_rank, vocab0;
+    unsigned char *const *peers;  // [tp] exchange regions, this rank's at tp_rank
+    XchgLayout xl;
 };
 
 enum PhaseKind { PH_QKV = 0, PH_O = 1, PH_GATEUP = 2, PH_DOWN = 3, PH_LOGITS = 4 };
@@ -105,12 +109,28 @@ FYB_DEV unsigned ld_acquire(const unsigned *p)
     return v;
 }
 
+FYB_DEV unsigned ld_acquire_sys(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 FYB_DEV bool reached(unsigned value, unsigned target) { return (int)(value - target) >= 0; }
+
+// Exchange counters of rank j (tensor parallelism): o_x[l] at l, d_x[l] at
+// nl + l, argmax keys at 2 nl, the shared abort word at 2 nl + 1.
+FYB_DEV unsigned *xctr(const DecodeParams &p, unsigned j)
+{
+    return reinterpret_cast<unsigned *>(p.peers[j] + p.xl.ctr);
+}
 
 FYB_DEV void raise_abort(const DecodeParams &p, unsigned code)
 {
     if (p.error) atomicCAS(p.error, 0u, code);
     atomicExch(p.sync.abort_flag, 1u);
+    for (unsigned j = 0; p.tp > 1 && j < p.tp; ++j)  // the other ranks leave too
+        if (j != p.tp_rank) atomicExch_system(xctr(p, j) + 2 * p.nl + 1, 1u);
 }
 
 FYB_DEV bool aborted(const DecodeParams &p) { return *(volatile unsigned *)p.sync.abort_flag != 0; }
@@ -136,7 +156,8 @@ FYB_DEV void stamp(const DecodeParams &p, unsigned &ts)
 // Whole-CTA wait until *ctr reached target (ctr null: only the abort check).
 // Thread 0 polls; false (for every thread) on abort or timeout. Trace points:
 // the CTA is idle (all its warps arrived), the wait is over.
-FYB_DEV bool cta_wait(const DecodeParams &p, const unsigned *ctr, unsigned target, unsigned *flag, unsigned &ts)
+FYB_DEV bool cta_wait(const DecodeParams &p, const unsigned *ctr, unsigned target, unsigned *flag, unsigned &ts,
+    bool sys = false)
 {
     __syncthreads();
     stamp(p, ts);
@@ -144,7 +165,7 @@ FYB_DEV bool cta_wait(const DecodeParams &p, const unsigned *ctr, unsigned targe
         unsigned ok = 0;
         for (unsigned i = 0;; ++i) {
             if (aborted(p)) break;
-            if (!ctr || reached(ld_acquire(ctr), target)) { ok = 1; break; }
+            if (!ctr || reached(sys ? ld_acquire_sys(ctr) : ld_acquire(ctr), target)) { ok = 1; break; }
             if (i >= WAIT_LIMIT) { raise_abort(p, ERR_TIMEOUT); break; }
 #ifndef FYB_POLL_NS
 #define FYB_POLL_NS 32
@@ -330,6 +351,55 @@ FYB_DEV void prep_input(const DecodeParams &p, bool embed, const float *buf, con
     __syncthreads();
 }
 
+// Tensor-parallel input of QKV, gate/up and the logits: x = base + the ranks'
+// partial rows in rank order (so every rank computes the same x), or the
+// embedding row; x is written back in shares (slot s by CTA s % grid) when
+// `share` is set, its sum of squares reduced over the CTA, and x * scale * w
+// split into limbs. One slot per thread (d <= 16 * threads).
+FYB_DEV void prep_tp(const DecodeParams &p, bool embed, const float *base, const float *parts, float *share,
+    const float *norm_w, const XBuf &xb, double *red)
+{
+    const unsigned tid = threadIdx.x, K = p.d, nslot = K / 16, nblk = K / 256;
+    const bool ok = tid < nslot;
+    const unsigned sl = ok ? tid : 0;
+    float x[16], w[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) { x[j] = 0.f; w[j] = 0.f; }
+    if (ok) {
+        load16(norm_w + 16 * sl, w);
+        if (embed) {
+            const unsigned char *erow = p.embd + (unsigned long long)__ldcg(p.request) * p.embd_row_bytes;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) x[j] = dequant_any(erow, 16ull * sl + j, p.embd_type);
+        } else {
+            load16(base + 16 * sl, x);
+#pragma unroll 8
+            for (unsigned r = 0; r < 8; ++r) {
+                if (r < p.tp) {
+                    float y[16];
+                    load16(parts + (size_t)r * K + 16 * sl, y);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) x[j] = __fadd_rn(x[j], y[j]);
+                }
+            }
+        }
+        if (share && sl % gridDim.x == blockIdx.x) {
+            float4 *o4 = reinterpret_cast<float4 *>(share + 16 * sl);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o4[i] = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+        }
+    }
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) ss += (double)x[j] * (double)x[j];
+    ss = block_sum_double(ss, red);
+    const float scale = (float)(1.0 / sqrt(ss / (double)K + (double)p.eps));
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = __fmul_rn(__fmul_rn(x[j], scale), w[j]);
+    prep_slot(x, ok, 0, sl, K, nblk, xb.xl, xb.xstride, xb.exps, xb.gsums, p.error);
+    __syncthreads();
+}
+
 // ------------------------------------------------------------ tile outputs
 FYB_DEV float residual_in(const DecodeParams &p, unsigned layer, unsigned r)
 {
@@ -380,6 +450,19 @@ FYB_DEV void tile_output(const DecodeParams &p, const Phase &ph, unsigned tile, 
         }
         return;
     }
+    if ((ph.kind == PH_O || ph.kind == PH_DOWN) && p.tp > 1) {
+        // this rank's partial rows go to every rank's exchange region; the
+        // residual add and the sum of squares follow the exchange
+        if (mine) {
+            const size_t off = (ph.kind == PH_O ? p.xl.xo : p.xl.xd) + ((size_t)p.tp_rank * p.d + tile * 16 + gid) * 4;
+            for (unsigned j = 0; j < p.tp; ++j) {
+                float *dst = reinterpret_cast<float *>(p.peers[j] + off);
+                dst[0] = yA;
+                dst[8] = yB;
+            }
+        }
+        return;
+    }
     if (ph.kind == PH_O || ph.kind == PH_DOWN) {
         const unsigned rA = tile * 16 + gid, rB = rA + 8;
         double sq = 0.0;
@@ -410,15 +493,24 @@ FYB_DEV void tile_output(const DecodeParams &p, const Phase &ph, unsigned tile, 
     }
     // PH_LOGITS: store; argmax key = (order key, ~index) so ties go to the
     // lowest index (llm_cpu.c:896-905)
-    const unsigned rA = tile * 16 + gid, rB = rA + 8;
+    const unsigned rA = tile * 16 + gid, rB = rA + 8;  // this rank's rows; p.vocab0 + row is the token
     unsigned long long k = 0ull;
     if (mine) {
         const bool okA = rA < p.V, okB = rB < p.V;
-        if (okA) p.logits[rA] = yA;
-        if (okB) p.logits[rB] = yB;
+        if (p.tp == 1) {
+            if (okA) p.logits[rA] = yA;
+            if (okB) p.logits[rB] = yB;
+        } else if (p.logits_mode == 1) {  // every rank gathers the whole vocabulary
+            for (unsigned j = 0; j < p.tp; ++j) {
+                float *lg = reinterpret_cast<float *>(p.peers[j] + p.xl.logits) + p.vocab0;
+                if (okA) lg[rA] = yA;
+                if (okB) lg[rB] = yB;
+            }
+        }
         if (((okA && !isfinite(yA)) || (okB && !isfinite(yB))) && p.error) atomicCAS(p.error, 0u, ERR_NONFINITE);
-        const unsigned long long kA = okA ? ((unsigned long long)float_order_key(yA) << 32) | (0xffffffffu - rA) : 0ull;
-        const unsigned long long kB = okB ? ((unsigned long long)float_order_key(yB) << 32) | (0xffffffffu - rB) : 0ull;
+        const unsigned gA = p.vocab0 + rA, gB = p.vocab0 + rB;
+        const unsigned long long kA = okA ? ((unsigned long long)float_order_key(yA) << 32) | (0xffffffffu - gA) : 0ull;
+        const unsigned long long kB = okB ? ((unsigned long long)float_order_key(yB) << 32) | (0xffffffffu - gB) : 0ull;
         k = kA > kB ? kA : kB;
     }
 #pragma unroll
@@ -576,7 +668,8 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, Ring &r, const X
         tile_output(p, ph, t, yA, yB, lane, key);
     }
     if (ph.kind == PH_LOGITS && lane == 0) keys[warp] = key;
-    __threadfence();  // this thread's outputs, before the CTA's counter update
+    if (p.tp > 1) __threadfence_system();  // outputs reach other GPUs before their counters move
+    else __threadfence();                  // this thread's outputs, before the CTA's counter update
     __syncthreads();
     unsigned tb, te;
     cta_tiles(ph, tb, te);
@@ -589,13 +682,24 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, Ring &r, const X
             for (unsigned w = 0; w < QG_WARPS; ++w) best = keys[w] > best ? keys[w] : best;
             atomicMax(p.argmax_key, best);
             __threadfence();
-            // the CTA that completes the last tile publishes the token
+            // the CTA that completes the last tile publishes the token (with
+            // tensor parallelism: this rank's best key, to every rank)
             if (atomicAdd(p.sync.logit_tiles, te - tb) + (te - tb) == ph.w.tiles) {
                 __threadfence();
                 const unsigned long long k = atomicExch(p.argmax_key, 0ull);
-                *p.argmax_token = 0xffffffffu - (unsigned)(k & 0xffffffffu);
                 atomicExch(p.sync.logit_tiles, 0u);
+                if (p.tp == 1) {
+                    *p.argmax_token = 0xffffffffu - (unsigned)(k & 0xffffffffu);
+                } else {
+                    for (unsigned j = 0; j < p.tp; ++j)
+                        reinterpret_cast<unsigned long long *>(p.peers[j] + p.xl.keys)[p.tp_rank] = k;
+                    __threadfence_system();
+                    for (unsigned j = 0; j < p.tp; ++j) atomicAdd_system(xctr(p, j) + 2 * p.nl, 1u);
+                }
             }
+        } else if (p.tp > 1 && (ph.kind == PH_O || ph.kind == PH_DOWN)) {
+            const unsigned idx = (ph.kind == PH_O ? 0 : p.nl) + ph.layer;
+            for (unsigned j = 0; j < p.tp; ++j) atomicAdd_system(xctr(p, j) + idx, te - tb);
         } else {
             signal_tiles(p, ph, tb, te - tb);
         }
@@ -886,15 +990,24 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
     const unsigned dt = p.d / 16;
     bool ok = true;
     unsigned ts = 0;
+    const bool tp = p.tp > 1;
+    // this rank's exchange region as floats (the partial rows all ranks wrote)
+    const float *xparts = tp ? reinterpret_cast<const float *>(p.peers[p.tp_rank]) : nullptr;
     stamp(p, ts);
     Phase cur = make_phase(p, PH_QKV, 0), nx0;
     ring_begin(cur, ring, lane, phase_after(p, PH_QKV, 0, nx0) ? &nx0 : nullptr, p.l2_prefetch != 0);
     for (unsigned l = 0; l < p.nl && ok; ++l) {
         // Q/K/V + RoPE + KV append
-        ok = cta_wait(p, l ? p.sync.down_done + (l - 1) : nullptr, step * dt, flag, ts);
-        if (!ok) break;
-        if (l == 0) prep_input(p, true, nullptr, nullptr, 0, p.layers[0].attn_norm, p.d, xb, red, scale_smem);
-        else prep_input(p, false, p.xa, p.ss_d, dt, p.layers[l].attn_norm, p.d, xb, red, scale_smem);
+        if (tp) {  // x = x_mid + the ranks' down rows (or the embedding row); written to xa
+            ok = cta_wait(p, l ? xctr(p, p.tp_rank) + p.nl + l - 1 : nullptr, step * p.tp * dt, flag, ts, true);
+            if (!ok) break;
+            prep_tp(p, l == 0, p.xm, xparts + p.xl.xd / 4, p.xa, p.layers[l].attn_norm, xb, red);
+        } else {
+            ok = cta_wait(p, l ? p.sync.down_done + (l - 1) : nullptr, step * dt, flag, ts);
+            if (!ok) break;
+            if (l == 0) prep_input(p, true, nullptr, nullptr, 0, p.layers[0].attn_norm, p.d, xb, red, scale_smem);
+            else prep_input(p, false, p.xa, p.ss_d, dt, p.layers[l].attn_norm, p.d, xb, red, scale_smem);
+        }
         stamp(p, ts);
         run_gemv(p, cur, ring, xb, lane, parts, keys); advance(p, cur);  // now the O projection
         // attention (its scratch overlays the limb buffer, idle now)
@@ -908,9 +1021,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
         stamp(p, ts);
         run_gemv(p, cur, ring, xb, lane, parts, keys); advance(p, cur);  // gate/up
         // gate/up + SwiGLU
-        ok = cta_wait(p, p.sync.o_done + l, step * dt, flag, ts);
-        if (!ok) break;
-        prep_input(p, false, p.xm, p.ss_o, dt, p.layers[l].ffn_norm, p.d, xb, red, scale_smem);
+        if (tp) {  // x_mid = x + the ranks' O rows; written to xm
+            ok = cta_wait(p, xctr(p, p.tp_rank) + l, step * p.tp * dt, flag, ts, true);
+            if (!ok) break;
+            prep_tp(p, false, p.xa, xparts + p.xl.xo / 4, p.xm, p.layers[l].ffn_norm, xb, red);
+        } else {
+            ok = cta_wait(p, p.sync.o_done + l, step * dt, flag, ts);
+            if (!ok) break;
+            prep_input(p, false, p.xm, p.ss_o, dt, p.layers[l].ffn_norm, p.d, xb, red, scale_smem);
+        }
         stamp(p, ts);
         run_gemv(p, cur, ring, xb, lane, parts, keys); advance(p, cur);  // down
         // down; residual add in the tile outputs
@@ -921,9 +1040,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
         run_gemv(p, cur, ring, xb, lane, parts, keys); advance(p, cur);  // the next layer's QKV, or the logits
     }
     if (ok && p.logits_mode) {
-        ok = cta_wait(p, p.sync.down_done + (p.nl - 1), step * dt, flag, ts);
+        if (tp) ok = cta_wait(p, xctr(p, p.tp_rank) + 2 * p.nl - 1, step * p.tp * dt, flag, ts, true);
+        else ok = cta_wait(p, p.sync.down_done + (p.nl - 1), step * dt, flag, ts);
         if (ok) {
-            prep_input(p, false, p.xa, p.ss_d, dt, p.out_norm, p.d, xb, red, scale_smem);
+            if (tp) prep_tp(p, false, p.xm, xparts + p.xl.xd / 4, nullptr, p.out_norm, xb, red);
+            else prep_input(p, false, p.xa, p.ss_d, dt, p.out_norm, p.d, xb, red, scale_smem);
             stamp(p, ts);
             run_gemv(p, cur, ring, xb, lane, parts, keys);
         }
@@ -937,6 +1058,24 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
         if (atomicAdd(p.sync.exit_count, 1u) == gridDim.x - 1) {
             __threadfence();
             p.sync.exit_count[0] = 0;
+            if (tp && p.logits_mode) {  // the token: the best of the ranks' keys
+                // keys move once per step with logits: request[4] counts those steps
+                const unsigned *kc = xctr(p, p.tp_rank) + 2 * p.nl;
+                const unsigned lstep = p.request[4] + 1;
+                bool got = false;
+                for (unsigned i = 0; i < WAIT_LIMIT && !aborted(p); ++i) {
+                    if (reached(ld_acquire_sys(kc), lstep * p.tp)) { got = true; break; }
+                    __nanosleep(32);
+                }
+                if (!got) { raise_abort(p, ERR_TIMEOUT); return; }
+                const unsigned long long *kk = reinterpret_cast<const unsigned long long *>(p.peers[p.tp_rank] + p.xl.keys);
+                unsigned long long best = 0ull;
+                for (unsigned j = 0; j < p.tp; ++j) {
+                    const unsigned long long v = __ldcg(kk + j);
+                    best = v > best ? v : best;
+                }
+                *p.argmax_token = 0xffffffffu - (unsigned)(best & 0xffffffffu);
+            }
             if (p.logits_mode == 2) {
                 const unsigned t = __ldcg(p.argmax_token);
                 p.tokens_log[p.request[2]] = t;
@@ -945,6 +1084,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
                 p.request[2] += 1;
             }
             p.request[3] += 1;
+            if (p.logits_mode) p.request[4] += 1;
         }
     }
 }
@@ -1028,6 +1168,7 @@ int decode_grid(int sms, const DecodeGeometry &g)
 int launch_decode(const DecodeLaunch &L, cudaStream_t s)
 {
     if (!decode_supported(L.g, L.out_head.type) || L.grid <= 0 || !L.layers) return -1;
+    if (L.tp > 1 && (!L.peers || L.g.d > 16u * QG_THREADS)) return -1;  // prep_tp: one slot per thread
     DecodeParams p = {};
     p.layers = L.layers;
     p.nl = L.g.nl; p.d = L.g.d; p.H = L.g.H; p.Hkv = L.g.Hkv; p.hd = L.g.hd; p.ffn = L.g.ffn; p.V = L.g.V;
@@ -1049,6 +1190,7 @@ int launch_decode(const DecodeLaunch &L, cudaStream_t s)
     p.l2_prefetch = L.l2_prefetch;
     p.trace = L.trace; p.trace_slots = L.trace_slots;
     p.wtrace = L.wtrace;
+    p.tp = L.tp; p.tp_rank = L.tp_rank; p.vocab0 = L.vocab0; p.peers = L.peers; p.xl = L.xl;
     const size_t smem = decode_smem_bytes(L.g, L.ring_bytes);
     const DecodeKernel decode_kernel = decode_kernel_for(L.g);
     if (!decode_kernel) return -1;

@@ -99,6 +99,28 @@ size_t attention_workspace_bytes(const AttentionLaunch &L);
 int launch_attention(const AttentionLaunch &L, cudaStream_t s);
 
 // ---------------------------------------------------------------- decode.cu
+// Tensor-parallel exchange region of a plan (byte offsets). Every rank has
+// one; rank j writes its partial O and down rows into [xo|xd] + j*d floats of
+// every rank's region, its vocabulary slice of the logits into `logits`, its
+// best argmax key into keys[j], and bumps the counters: o_x[l] (index l),
+// d_x[l] (nl + l), keys (2 nl); 2 nl + 1 is the shared abort word.
+struct XchgLayout {
+    size_t xo = 0, xd = 0, logits = 0, keys = 0, ctr = 0, bytes = 0;
+};
+inline XchgLayout xchg_layout(unsigned tp, unsigned d, unsigned V, unsigned nl)
+{
+    auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+    XchgLayout x;
+    size_t o = 0;
+    x.xo = o; o += up((size_t)tp * d * 4);
+    x.xd = o; o += up((size_t)tp * d * 4);
+    x.logits = o; o += up((size_t)V * 4);
+    x.keys = o; o += up((size_t)tp * 8);
+    x.ctr = o; o += up(((size_t)2 * nl + 4) * 4);
+    x.bytes = o;
+    return x;
+}
+
 // One decode step of a dense LLaMA model as one persistent kernel.
 struct DecodeLayer {
     QWeights qkv, o, gateup, down;  // repacked as for the stand-alone GEMV
@@ -129,7 +151,7 @@ struct DecodeLaunch {
     unsigned embd_type = 0;
     float eps = 1e-5f, attn_scale = 0.f;
     const float *rope_cos = nullptr, *rope_sin = nullptr;
-    unsigned *request = nullptr;  // {token, position, tokens logged, step}
+    unsigned *request = nullptr;  // {token, position, tokens logged, steps, steps with logits}
     float *xa = nullptr, *xm = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
     double *ss_o = nullptr, *ss_d = nullptr;  // [d/16] per-tile sums of squares
     DecodeSync sync;
@@ -146,6 +168,11 @@ struct DecodeLaunch {
     unsigned long long *wtrace = nullptr;  // profiling: [layers*5 + 1][grid*16][4] per-warp GEMV points
     unsigned ring_bytes = 0;  // per-warp weight ring (0: as much as shared memory allows)
     int l2_prefetch = 1;      // prefetch each next phase's weights into L2
+    // tensor parallelism (tp > 1): g holds this rank's heads, FFN rows and
+    // vocabulary rows (g.V), the d-row phases exchange partial sums
+    unsigned tp = 1, tp_rank = 0, vocab0 = 0;
+    unsigned char *const *peers = nullptr;  // device array [tp] of exchange regions
+    XchgLayout xl;
 };
 // Trace points per CTA of one step: start, per layer 5 x (idle, ready) + 4
 // preparations + attention end, logits (idle, ready, prepared), exit (idle, ready).

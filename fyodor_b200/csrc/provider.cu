@@ -341,6 +341,15 @@ struct Plan {
     size_t dec_bytes = 0;
     unsigned dec_ring_bytes = 6720;  // per-warp weight ring; NYA_CUDA_RING_BYTES (0 = largest)
     int dec_l2_prefetch = 0;         // NYA_CUDA_L2_PREFETCH=1 prefetches each next phase into L2
+    // tensor parallelism: this plan holds rank tp_rank's shard of tp_size
+    // (H, Hkv and ffn above are this rank's; V is the whole vocabulary)
+    unsigned tp_size = 1, tp_rank = 0, vocab_rows = 0, vocab0 = 0;
+    unsigned char *xchg = nullptr;     // exchange region peers write into (tp_size > 1)
+    size_t xchg_bytes = 0;
+    XchgLayout xl;
+    unsigned char **peers_dev = nullptr;  // [tp_size] device pointers to every rank's region
+    std::vector<unsigned char *> peers;   // host copy; peers opened through IPC are closed on free
+    bool connected = false;
 };
 
 static void *plan_alloc(Plan *p, size_t bytes)
@@ -365,6 +374,8 @@ static void plan_free(void *opaque)
         DeviceScope scope(p->ctx->device);
         cudaStreamSynchronize(p->ctx->stream);
         for (auto &g : p->graphs) if (g) cudaGraphExecDestroy(g);
+        for (unsigned j = 0; j < p->peers.size(); ++j)
+            if (j != p->tp_rank && p->peers[j]) cudaIpcCloseMemHandle(p->peers[j]);
         for (void *a : p->allocations) cudaFree(a);
         if (p->err_host) cudaFreeHost(p->err_host);
     }
@@ -473,7 +484,7 @@ static QgemvLaunch logits_launch(const Plan *p)
     QgemvLaunch L = gemv_base(p);
     L.epilogue = EPI_LOGITS;
     L.w = p->out_head;
-    L.seg_rows[0] = p->V;
+    L.seg_rows[0] = p->vocab_rows;
     L.out[0] = p->logits;
     L.norm_w = p->out_norm;
     L.argmax_key = p->argmax_key; L.argmax_token = p->argmax_token; L.tiles_done = p->tiles_done;
@@ -502,7 +513,8 @@ static AttentionLaunch attention_launch(const Plan *p, unsigned l)
 static DecodeLaunch persistent_launch(const Plan *p, StepMode mode)
 {
     DecodeLaunch L;
-    L.g.nl = p->nl; L.g.d = p->d; L.g.H = p->H; L.g.Hkv = p->Hkv; L.g.hd = p->hd; L.g.ffn = p->ffn; L.g.V = p->V;
+    L.g.nl = p->nl; L.g.d = p->d; L.g.H = p->H; L.g.Hkv = p->Hkv; L.g.hd = p->hd; L.g.ffn = p->ffn;
+    L.g.V = p->vocab_rows;
     L.g.capacity = (unsigned)p->capacity;
     L.layers = p->dec_layers;
     L.out_head = p->out_head; L.out_norm = p->out_norm;
@@ -521,6 +533,12 @@ static DecodeLaunch persistent_launch(const Plan *p, StepMode mode)
     L.grid = p->dec_grid;
     L.ring_bytes = p->dec_ring_bytes;
     L.l2_prefetch = p->dec_l2_prefetch;
+    if (p->tp_size > 1) {  // partial sums and logits go through the ranks' exchange regions
+        L.tp = p->tp_size; L.tp_rank = p->tp_rank; L.vocab0 = p->vocab0;
+        L.peers = p->peers_dev; L.xl = p->xl;
+        L.logits = nullptr;
+        L.sync.abort_flag = reinterpret_cast<unsigned *>(p->xchg + p->xl.ctr) + 2 * p->nl + 1;
+    }
     return L;
 }
 
@@ -626,27 +644,43 @@ static bool supported_matrix(const nya_llm_tensor *t, size_t cols, size_t rows)
 
 // Upload the raw GGUF bytes of up to three tensors and repack them, tile
 // after tile, into one fused unit array.
-static int upload_fused(Plan *p, const nya_llm_tensor *const *t, int n, int mode, QWeights *out)
+// A rank's part of a weight matrix: rows [r0, r0 + nr) and column blocks
+// [cb0, cb0 + ncb) (256-value K-quant blocks); null slice = all of it.
+struct Slice {
+    size_t r0, nr, cb0, ncb;
+};
+
+static int upload_fused(Plan *p, const nya_llm_tensor *const *t, int n, int mode, QWeights *out,
+    const Slice *slices = nullptr)
 {
     const unsigned type = t[0]->type;
-    const size_t cols = (size_t)t[0]->dimensions[0];
+    size_t block = 256, bb = 0;
+    type_geometry(type, &block, &bb);
+    const size_t full_cols = (size_t)t[0]->dimensions[0], full_row = full_cols / block * bb;
+    Slice sl[3];
+    for (int i = 0; i < n; ++i)
+        sl[i] = slices ? slices[i] : Slice{0, (size_t)t[i]->dimensions[1], 0, full_cols / block};
+    const size_t cols = sl[0].ncb * block, row_bytes = sl[0].ncb * bb;
     size_t tiles[3] = {0, 0, 0}, total = 0;
-    if (mode == REPACK_GATEUP) { tiles[0] = ((size_t)t[0]->dimensions[1] + 7) / 8; total = tiles[0]; }
-    else for (int i = 0; i < n; ++i) { tiles[i] = ((size_t)t[i]->dimensions[1] + 15) / 16; total += tiles[i]; }
+    if (mode == REPACK_GATEUP) { tiles[0] = (sl[0].nr + 7) / 8; total = tiles[0]; }
+    else for (int i = 0; i < n; ++i) { tiles[i] = (sl[i].nr + 15) / 16; total += tiles[i]; }
     unsigned char *units = (unsigned char *)plan_alloc(p, qunits_bytes(type, total, cols));
     if (!units) return -1;
     void *raw[3] = {nullptr, nullptr, nullptr};
     int r = 0;
     for (int i = 0; i < n && !r; ++i) {
-        if (cudaMalloc(&raw[i], t[i]->data_size) != cudaSuccess ||
-            !upload(raw[i], t[i]->data, t[i]->data_size, p->ctx->stream)) r = -1;
+        const unsigned char *src = (const unsigned char *)t[i]->data + sl[i].r0 * full_row + sl[i].cb0 * bb;
+        if (cudaMalloc(&raw[i], sl[i].nr * row_bytes) != cudaSuccess) { r = -1; break; }
+        if (row_bytes == full_row) r = upload(raw[i], src, sl[i].nr * row_bytes, p->ctx->stream) ? 0 : -1;
+        else r = cudaMemcpy2DAsync(raw[i], row_bytes, src, full_row, row_bytes, sl[i].nr, cudaMemcpyHostToDevice,
+                                   p->ctx->stream) == cudaSuccess ? 0 : -1;
     }
     size_t at = 0;
     if (!r && mode == REPACK_GATEUP)
-        r = repack_units(raw[0], raw[1], (size_t)t[0]->dimensions[1], cols, type, mode, units, total, p->ctx->stream);
+        r = repack_units(raw[0], raw[1], sl[0].nr, cols, type, mode, units, total, p->ctx->stream);
     for (int i = 0; !r && mode != REPACK_GATEUP && i < n; ++i) {
-        r = repack_units(raw[i], nullptr, (size_t)t[i]->dimensions[1], cols, type, mode,
-                         units + qunits_bytes(type, at, cols), tiles[i], p->ctx->stream);
+        r = repack_units(raw[i], nullptr, sl[i].nr, cols, type, mode, units + qunits_bytes(type, at, cols), tiles[i],
+                         p->ctx->stream);
         at += tiles[i];
     }
     if (cudaStreamSynchronize(p->ctx->stream) != cudaSuccess) r = -1;  // raw buffers are read until here
@@ -669,7 +703,7 @@ static bool setup_persistent(Plan *p)
     const char *pf = std::getenv("NYA_CUDA_L2_PREFETCH");
     p->dec_l2_prefetch = pf && !std::strcmp(pf, "1");
     DecodeGeometry g;
-    g.nl = p->nl; g.d = p->d; g.H = p->H; g.Hkv = p->Hkv; g.hd = p->hd; g.ffn = p->ffn; g.V = p->V;
+    g.nl = p->nl; g.d = p->d; g.H = p->H; g.Hkv = p->Hkv; g.hd = p->hd; g.ffn = p->ffn; g.V = p->vocab_rows;
     g.capacity = (unsigned)p->capacity;
     if (!decode_supported(g, p->out_head.type)) return true;
     const int grid = decode_grid(p->ctx->sms, g);
@@ -753,17 +787,31 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
     size_t eblock, ebytes;
     if (!type_geometry(m->token_embedding->type, &eblock, &ebytes) || d % eblock) return plan_decline("embedding type");
 
+    // tensor parallelism: this process holds rank tp_rank of tp_size shards
+    size_t tp = 1, tp_rank = 0;
+    env_size("NYA_CUDA_TP_SIZE", &tp);
+    env_size("NYA_CUDA_TP_RANK", &tp_rank);
+    if (tp == 0 || tp > 8 || tp_rank >= tp) return plan_decline("NYA_CUDA_TP_SIZE / NYA_CUDA_TP_RANK");
+    if (tp > 1 && (H % tp || Hkv % tp || (H * hd / tp) % 256 || (ffn / tp) % 256 || ffn % tp || V % tp))
+        return plan_decline("model does not shard evenly over NYA_CUDA_TP_SIZE ranks");
+    if (tp > 1 && d > 8192) return plan_decline("tensor parallelism supports d <= 8192");
+    const unsigned Hs = H / (unsigned)tp, Hkvs = Hkv / (unsigned)tp, ffns = ffn / (unsigned)tp;
+    const unsigned Vs = V / (unsigned)tp, r = (unsigned)tp_rank;
+
     // admission: weights + KV + scratch against the budget (resident.inc:155-168)
     size_t weights = 0;
     for (size_t i = 0; i < m->tensor_count; ++i) weights += m->tensors[i].data_size;
     if (m->output == m->token_embedding) weights += m->output->data_size;  // gather copy + units
-    const size_t kv_bytes = (size_t)nl * Hkv * capacity * hd * sizeof(__half) * 2;
+    weights = weights / tp + (tp > 1 ? m->token_embedding->data_size : 0);  // shards + the replicated embedding
+    const size_t kv_bytes = (size_t)nl * Hkvs * capacity * hd * sizeof(__half) * 2;
     const size_t act = ((size_t)d * 3 + (size_t)H * hd * 2 + ffn + V) * sizeof(float) + 2 * capacity * (hd / 2) * sizeof(float);
     if (weights + kv_bytes + act > c->cache_limit) return plan_decline("weights plus KV/scratch exceed the memory budget");
 
     Plan *p = new Plan();
     p->ctx = c; p->m = m; p->capacity = capacity;
-    p->d = d; p->H = H; p->Hkv = Hkv; p->hd = hd; p->ffn = ffn; p->V = V; p->nl = nl;
+    p->d = d; p->H = Hs; p->Hkv = Hkvs; p->hd = hd; p->ffn = ffns; p->V = V; p->nl = nl;
+    p->tp_size = (unsigned)tp; p->tp_rank = r; p->vocab_rows = Vs; p->vocab0 = r * Vs;
+    p->connected = tp == 1;
     p->eps = m->norm_epsilon;
     std::memset(&p->stats, 0, sizeof(p->stats));
     const char *graphs = std::getenv("NYA_CUDA_GRAPHS");
@@ -802,8 +850,17 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
         const nya_llm_tensor *o[1] = {w.attention_output};
         const nya_llm_tensor *gu[2] = {w.feed_forward_gate, w.feed_forward_up};
         const nya_llm_tensor *dn[1] = {w.feed_forward_down};
-        ok = upload_fused(p, qkv, 3, REPACK_QKV, &L.qkv) == 0 && upload_fused(p, o, 1, REPACK_PLAIN, &L.o) == 0 &&
-             upload_fused(p, gu, 2, REPACK_GATEUP, &L.gateup) == 0 && upload_fused(p, dn, 1, REPACK_PLAIN, &L.down) == 0;
+        // this rank's heads (rows of q/k/v, columns of O) and FFN rows (gate/up
+        // rows, down columns); the whole matrices when tp == 1
+        const Slice s_qkv[3] = {{(size_t)r * Hs * hd, (size_t)Hs * hd, 0, d / 256},
+                                {(size_t)r * Hkvs * hd, (size_t)Hkvs * hd, 0, d / 256},
+                                {(size_t)r * Hkvs * hd, (size_t)Hkvs * hd, 0, d / 256}};
+        const Slice s_o[1] = {{0, d, (size_t)r * Hs * hd / 256, (size_t)Hs * hd / 256}};
+        const Slice s_gu[2] = {{(size_t)r * ffns, ffns, 0, d / 256}, {(size_t)r * ffns, ffns, 0, d / 256}};
+        const Slice s_dn[1] = {{0, d, (size_t)r * ffns / 256, ffns / 256}};
+        ok = upload_fused(p, qkv, 3, REPACK_QKV, &L.qkv, s_qkv) == 0 && upload_fused(p, o, 1, REPACK_PLAIN, &L.o, s_o) == 0 &&
+             upload_fused(p, gu, 2, REPACK_GATEUP, &L.gateup, s_gu) == 0 &&
+             upload_fused(p, dn, 1, REPACK_PLAIN, &L.down, s_dn) == 0;
         if (!ok) break;
         float *an = (float *)A(d * 4), *fn = (float *)A(d * 4);
         ok = ok && upload(an, w.attention_norm->data, d * 4, c->stream) && upload(fn, w.feed_forward_norm->data, d * 4, c->stream);
@@ -811,7 +868,8 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
     }
     if (ok) {
         const nya_llm_tensor *out[1] = {m->output};
-        ok = upload_fused(p, out, 1, REPACK_PLAIN, &p->out_head) == 0;
+        const Slice s_out[1] = {{(size_t)p->vocab0, Vs, 0, d / 256}};  // this rank's vocabulary rows
+        ok = upload_fused(p, out, 1, REPACK_PLAIN, &p->out_head, s_out) == 0;
     }
     if (ok) {
         void *e = A(m->token_embedding->data_size);
@@ -858,6 +916,18 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
                      cudaMemsetAsync(p->attn_ws, 0, p->attn_ws_bytes, c->stream) == cudaSuccess;
     }
     if (ok) ok = setup_persistent(p);
+    if (ok && p->tp_size > 1) {
+        if (!p->dec_grid) {  // only the persistent kernel exchanges partial sums
+            debug("tensor parallelism needs the persistent decode kernel", cudaSuccess);
+            plan_free(p);
+            return plan_decline("tensor parallelism needs the persistent decode kernel");
+        }
+        p->xl = xchg_layout(p->tp_size, d, V, nl);
+        p->xchg_bytes = p->xl.bytes;
+        p->xchg = (unsigned char *)A(p->xchg_bytes);
+        p->peers_dev = (unsigned char **)A(p->tp_size * sizeof(void *));
+        if (ok) ok = cudaMemsetAsync(p->xchg, 0, p->xchg_bytes, c->stream) == cudaSuccess;
+    }
     if (ok) ok = cudaStreamSynchronize(c->stream) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
     if (!ok) {
         debug("resident plan setup failed; rolling back", cudaGetLastError());
@@ -884,7 +954,8 @@ static int finish_logits(Plan *p, float *out)
 {
     cudaStream_t s = p->ctx->stream;
     ++p->stats.downloads;
-    if (cudaMemcpyAsync(out, p->logits, (size_t)p->V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess) return -2;
+    const void *src = p->tp_size > 1 ? (const void *)(p->xchg + p->xl.logits) : (const void *)p->logits;
+    if (cudaMemcpyAsync(out, src, (size_t)p->V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess) return -2;
     ++p->stats.synchronizations;
     if (cudaStreamSynchronize(s) != cudaSuccess) return -2;
     if (*(volatile unsigned *)p->err_host) return -2;
@@ -897,8 +968,8 @@ static int finish_logits(Plan *p, float *out)
 static int plan_token(void *opaque, uint32_t token, size_t position, int logits, float *out)
 {
     Plan *p = (Plan *)opaque;
-    if (!p || p->failed || position >= p->capacity || (position != 0 && position > p->valid) || (logits && !out) ||
-        token >= p->V)
+    if (!p || p->failed || !p->connected || position >= p->capacity || (position != 0 && position > p->valid) ||
+        (logits && !out) || token >= p->V)
         return -1;
     if (position >= p->fail_after) { p->failed = true; return -1; }
     DeviceScope scope(p->ctx->device);
@@ -913,7 +984,7 @@ static int plan_prefill(void *opaque, const uint32_t *tokens, size_t count, size
 {
     Plan *p = (Plan *)opaque;
     if (!p || !tokens || count == 0 || position > p->capacity || count > p->capacity - position) return -1;
-    if (p->failed || (position != 0 && position > p->valid) || !out) return -1;
+    if (p->failed || !p->connected || (position != 0 && position > p->valid) || !out) return -1;
     for (size_t i = 0; i < count; ++i) if (tokens[i] >= p->V) return -1;
     if (position + count > p->fail_after) { p->failed = true; return -1; }
     DeviceScope scope(p->ctx->device);
@@ -938,9 +1009,9 @@ static int plan_read_kv(void *opaque, size_t layer, size_t position, size_t coun
     size_t elements)
 {
     Plan *p = (Plan *)opaque;
-    if (!p || p->failed || !keys || !values || !count || layer >= p->nl || position > p->valid ||
+    if (!p || p->failed || p->tp_size > 1 || !keys || !values || !count || layer >= p->nl || position > p->valid ||
         count > p->valid - position)
-        return -1;
+        return -1;  // a tensor-parallel rank holds only its own KV heads
     const size_t width = (size_t)p->hd * p->Hkv;
     if (count > SIZE_MAX / width || elements != count * width) return -1;
     DeviceScope scope(p->ctx->device);
@@ -1091,7 +1162,7 @@ extern "C" int fyb_attention_decode(const float *q, const void *k, const void *v
 extern "C" int fyb_plan_decode_greedy(void *opaque, uint32_t token, size_t position, size_t steps, uint32_t *tokens_out)
 {
     Plan *p = (Plan *)opaque;
-    if (!p || p->failed || !tokens_out || token >= p->V || position > p->valid || steps == 0 ||
+    if (!p || p->failed || !p->connected || !tokens_out || token >= p->V || position > p->valid || steps == 0 ||
         steps > p->capacity - position)
         return -1;
     DeviceScope scope(p->ctx->device);
@@ -1108,7 +1179,8 @@ extern "C" int fyb_plan_decode_greedy(void *opaque, uint32_t token, size_t posit
 extern "C" double fyb_plan_time_greedy(void *opaque, uint32_t token, size_t position, size_t steps)
 {
     Plan *p = (Plan *)opaque;
-    if (!p || p->failed || token >= p->V || position > p->valid || steps == 0 || steps > p->capacity - position)
+    if (!p || p->failed || !p->connected || token >= p->V || position > p->valid || steps == 0 ||
+        steps > p->capacity - position)
         return -1.0;
     DeviceScope scope(p->ctx->device);
     cudaEvent_t a, b;
@@ -1135,11 +1207,58 @@ extern "C" unsigned long long fyb_plan_launches_per_token(const void *opaque)
     return 3ull + 5ull * p->nl;
 }
 
+extern "C" int fyb_plan_tp_info(const void *opaque, unsigned *rank, unsigned *size)
+{
+    const Plan *p = (const Plan *)opaque;
+    if (!p) return -1;
+    if (rank) *rank = p->tp_rank;
+    if (size) *size = p->tp_size;
+    return 0;
+}
+
+extern "C" int fyb_plan_tp_handle(void *opaque, void *handle, size_t bytes)
+{
+    Plan *p = (Plan *)opaque;
+    if (!p || p->tp_size < 2 || !handle || bytes < sizeof(cudaIpcMemHandle_t)) return -1;
+    DeviceScope scope(p->ctx->device);
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, p->xchg) != cudaSuccess) { cudaGetLastError(); return -2; }
+    std::memcpy(handle, &h, sizeof(h));
+    return 0;
+}
+
+extern "C" int fyb_plan_tp_connect(void *opaque, const void *handles, size_t count)
+{
+    Plan *p = (Plan *)opaque;
+    if (!p || p->tp_size < 2 || p->connected || !handles || count != p->tp_size) return -1;
+    DeviceScope scope(p->ctx->device);
+    p->peers.assign(p->tp_size, nullptr);
+    p->peers[p->tp_rank] = p->xchg;
+    for (unsigned j = 0; j < p->tp_size; ++j) {
+        if (j == p->tp_rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, (const unsigned char *)handles + (size_t)j * sizeof(h), sizeof(h));
+        void *ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            debug("opening a peer's exchange region", cudaErrorInvalidValue);
+            return -2;
+        }
+        p->peers[j] = (unsigned char *)ptr;
+    }
+    if (!upload(p->peers_dev, p->peers.data(), p->tp_size * sizeof(void *), p->ctx->stream) ||
+        cudaStreamSynchronize(p->ctx->stream) != cudaSuccess)
+        return -2;
+    p->connected = true;
+    return 0;
+}
+
 extern "C" long fyb_plan_trace(void *opaque, uint32_t token, size_t position, unsigned long long *out,
     size_t out_count, unsigned *grid_out, unsigned long long *warp_out, size_t warp_count)
 {
     Plan *p = (Plan *)opaque;
-    if (!p || p->failed || !p->dec_grid || token >= p->V || position >= p->capacity || position > p->valid || !out)
+    if (!p || p->failed || !p->connected || !p->dec_grid || token >= p->V || position >= p->capacity ||
+        position > p->valid || !out)
         return -1;
     const unsigned points = decode_trace_points(p->nl);
     const size_t n = (size_t)points * p->dec_grid;
@@ -1170,7 +1289,8 @@ extern "C" long fyb_plan_trace(void *opaque, uint32_t token, size_t position, un
 extern "C" int fyb_plan_profile(void *opaque, uint32_t token, size_t position, size_t steps, double *out)
 {
     Plan *p = (Plan *)opaque;
-    if (!p || p->failed || !out || token >= p->V || position > p->valid || steps == 0 || steps > p->capacity - position)
+    if (!p || p->failed || p->tp_size > 1 || !out || token >= p->V || position > p->valid || steps == 0 ||
+        steps > p->capacity - position)
         return -1;
     DeviceScope scope(p->ctx->device);
     out[0] = out[1] = out[2] = 0.0;

@@ -138,6 +138,29 @@ long fyb_plan_trace(void *plan, uint32_t token, size_t position, unsigned long l
    launches read different weights (more bytes than L2 holds). */
 double fyb_plan_time_projection(void *plan, unsigned layer, unsigned which, unsigned reps, size_t *bytes);
 
+/* ---- tensor parallelism across processes (no reference counterpart) -----
+   A process whose environment holds NYA_CUDA_TP_SIZE=N (2..8) and
+   NYA_CUDA_TP_RANK=r (and NYA_CUDA_DEVICE for its GPU) creates plans that hold
+   rank r's shard of the model: its H/N query and Hkv/N KV heads (rows of
+   q/k/v, columns of the attention output), its FFN/N rows of gate/up and
+   columns of down, and its V/N rows of the output head. The persistent decode
+   kernel adds the ranks' partial attention-output and down rows over NVLink
+   in every rank's exchange region (one exchange per attention block and one
+   per MLP block), every rank gets the whole logits vector and the same greedy
+   token. Before the first step each rank exports its exchange region with
+   fyb_plan_tp_handle, the handles of all ranks are gathered (in rank order)
+   by the caller, and every rank passes them to fyb_plan_tp_connect. The ranks
+   must then run the same steps (plan_token, plan_prefill, greedy decoding)
+   together; a rank that stops makes the others fail their next step after a
+   bounded wait. plan_read_kv declines (a rank holds only its KV heads). */
+#define FYB_IPC_HANDLE_BYTES 64
+/* rank and size of the plan's shard (size 1 without tensor parallelism). */
+int fyb_plan_tp_info(const void *plan, unsigned *rank, unsigned *size);
+/* this rank's exchange region handle (FYB_IPC_HANDLE_BYTES bytes). */
+int fyb_plan_tp_handle(void *plan, void *handle, size_t bytes);
+/* opens the other ranks' regions; handles = count (= size) handles in rank order. */
+int fyb_plan_tp_connect(void *plan, const void *handles, size_t count);
+
 /* ---- synthetic GGUF-layout models (no reference counterpart) -------------
    Builds an in-memory model in the engine's own binding layout
    (backend/core/llm_gguf.c:1013-1118): LLaMA tensors, block formats as
