@@ -27,25 +27,43 @@ def _nvcc():
     return path if os.path.exists(path) else (shutil.which("nvcc") or "nvcc")
 
 
+# Sources compiled once per variant (object suffix, extra flags): each
+# instantiation of the persistent decode kernel is its own compilation, so
+# they run in parallel.
+VARIANTS = {
+    "decode_inst.cu": [("%d_%d_%d" % (df, hd, g), ["-DFYB_DK_DF=%d" % df, "-DFYB_DK_HD=%d" % hd, "-DFYB_DK_G=%d" % g])
+                       for df in (0, 1) for hd in (128, 64) for g in (1, 2, 4, 8)],
+}
+
+
 def sources():
     return sorted(f for f in os.listdir(CSRC) if f.endswith((".cu", ".cpp")))
 
 
-def _compile(src, verbose):
-    obj = os.path.join(OBJ, src + ".o")
+def units():
+    """(source, object suffix, extra flags) of every compilation."""
+    out = []
+    for src in sources():
+        out += [(src, suffix, flags) for suffix, flags in VARIANTS.get(src, [("", [])])]
+    return out
+
+
+def _compile(unit, verbose):
+    src, suffix, flags = unit
+    obj = os.path.join(OBJ, src + ("." + suffix if suffix else "") + ".o")
     path = os.path.join(CSRC, src)
     deps = [path] + [os.path.join(CSRC, h) for h in os.listdir(CSRC) if h.endswith((".cuh", ".h"))]
     deps += [os.path.join(ROOT, "include", h) for h in os.listdir(os.path.join(ROOT, "include"))]
     if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(d) for d in deps):
         return obj
-    cmd = [_nvcc()] + ARCH + COMMON + ["-c", path, "-o", obj]
+    cmd = [_nvcc()] + ARCH + COMMON + flags + ["-c", path, "-o", obj]
     if src.endswith(".cpp"):
-        cmd = [_nvcc(), "-x", "cu"] + ARCH + COMMON + ["-c", path, "-o", obj]
+        cmd = [_nvcc(), "-x", "cu"] + ARCH + COMMON + flags + ["-c", path, "-o", obj]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError("nvcc failed for %s:\n%s\n%s" % (src, r.stdout, r.stderr))
+        raise RuntimeError("nvcc failed for %s %s:\n%s\n%s" % (src, suffix, r.stdout, r.stderr))
     if verbose and r.stderr:
         sys.stderr.write(r.stderr)
     return obj
@@ -53,9 +71,11 @@ def _compile(src, verbose):
 
 def build(verbose=False):
     os.makedirs(OBJ, exist_ok=True)
-    srcs = sources()
-    with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
+    todo = units()
+    # the longest compilations first
+    todo.sort(key=lambda u: u[0] != "decode_inst.cu")
+    with concurrent.futures.ThreadPoolExecutor(max_workers=min(os.cpu_count() or 8, len(todo))) as ex:
+        objs = list(ex.map(lambda u: _compile(u, verbose), todo))
     newest = max(os.path.getmtime(o) for o in objs)
     if os.path.exists(LIB) and os.path.getmtime(LIB) >= newest:
         return LIB

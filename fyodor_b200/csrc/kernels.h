@@ -141,6 +141,18 @@ struct DecodeSync {
     unsigned *exit_count = nullptr, *abort_flag = nullptr;
     unsigned *logit_tiles = nullptr;
 };
+// Readiness counters of the dataflow decode kernel (zero at plan creation,
+// never reset: each step adds a fixed amount, targets are step multiples).
+struct DecodeDfSync {
+    unsigned *bo = nullptr;       // [nl][d/256] attention-output tiles done per 256-row block (16 per step)
+    unsigned *bgu = nullptr;      // [nl][ffn/256] gate/up tiles done per 256-row block of h (32 per step)
+    unsigned *bdn = nullptr;      // [nl][d/256] down tiles done per 256-row block (16 per step)
+    unsigned *attn_kv = nullptr;  // [nl][kv_heads] attention outputs done per KV head (1 per step)
+};
+inline size_t decode_df_counters(unsigned nl, unsigned d, unsigned ffn, unsigned Hkv)
+{
+    return (size_t)nl * (2 * (d / 256) + ffn / 256 + Hkv);
+}
 struct DecodeLaunch {
     DecodeGeometry g;
     const DecodeLayer *layers = nullptr;  // device array [nl]
@@ -173,6 +185,8 @@ struct DecodeLaunch {
     unsigned tp = 1, tp_rank = 0, vocab0 = 0;
     unsigned char *const *peers = nullptr;  // device array [tp] of exchange regions
     XchgLayout xl;
+    // dataflow kernel (single GPU): set to run it instead of the barrier form
+    DecodeDfSync df;
 };
 // Trace points per CTA of one step: start, per layer 5 x (idle, ready) + 4
 // preparations + attention end, logits (idle, ready, prepared), exit (idle, ready).
@@ -181,6 +195,8 @@ int decode_supported(const DecodeGeometry &g, unsigned type_out);
 size_t decode_partials_bytes(const DecodeGeometry &g, int grid);
 unsigned decode_max_tiles(const DecodeGeometry &g);
 int decode_grid(int sms, const DecodeGeometry &g);
+// Whether the dataflow form runs this geometry on `grid` CTAs (single GPU).
+int decode_df_supported(const DecodeGeometry &g, unsigned type_out, int grid);
 int launch_decode(const DecodeLaunch &L, cudaStream_t s);
 
 }  // namespace fyb

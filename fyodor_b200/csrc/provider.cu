@@ -341,6 +341,7 @@ struct Plan {
     size_t dec_bytes = 0;
     unsigned dec_ring_bytes = 6720;  // per-warp weight ring; NYA_CUDA_RING_BYTES (0 = largest)
     int dec_l2_prefetch = 0;         // NYA_CUDA_L2_PREFETCH=1 prefetches each next phase into L2
+    DecodeDfSync dec_df;             // NYA_CUDA_DATAFLOW=1: the dataflow form of the kernel
     // tensor parallelism: this plan holds rank tp_rank's shard of tp_size
     // (H, Hkv and ffn above are this rank's; V is the whole vocabulary)
     unsigned tp_size = 1, tp_rank = 0, vocab_rows = 0, vocab0 = 0;
@@ -533,6 +534,7 @@ static DecodeLaunch persistent_launch(const Plan *p, StepMode mode)
     L.grid = p->dec_grid;
     L.ring_bytes = p->dec_ring_bytes;
     L.l2_prefetch = p->dec_l2_prefetch;
+    L.df = p->dec_df;
     if (p->tp_size > 1) {  // partial sums and logits go through the ranks' exchange regions
         L.tp = p->tp_size; L.tp_rank = p->tp_rank; L.vocab0 = p->vocab0;
         L.peers = p->peers_dev; L.xl = p->xl;
@@ -743,6 +745,17 @@ static bool setup_persistent(Plan *p)
     y.tile_counters = w; w += decode_max_tiles(g);
     y.attn_counters = w; w += p->Hkv;
     y.exit_count = w++; y.abort_flag = w++; y.logit_tiles = w++;
+    const char *dfe = std::getenv("NYA_CUDA_DATAFLOW");
+    if (dfe && !std::strcmp(dfe, "1") && p->tp_size == 1 && decode_df_supported(g, p->out_head.type, grid)) {
+        const size_t n = decode_df_counters(p->nl, p->d, p->ffn, p->Hkv);
+        unsigned *c = (unsigned *)A(n * 4);
+        if (!ok || cudaMemsetAsync(c, 0, n * 4, s) != cudaSuccess) return false;
+        DecodeDfSync &f = p->dec_df;
+        f.bo = c; c += (size_t)p->nl * (p->d / 256);
+        f.bdn = c; c += (size_t)p->nl * (p->d / 256);
+        f.bgu = c; c += (size_t)p->nl * (p->ffn / 256);
+        f.attn_kv = c;
+    }
     if (cudaMemsetAsync(y.qkv_done, 0, words * 4, s) != cudaSuccess ||
         !upload(p->dec_layers, layers.data(), layers.size() * sizeof(DecodeLayer), s) ||
         cudaStreamSynchronize(s) != cudaSuccess)
