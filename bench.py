@@ -392,7 +392,10 @@ def summarize_trace(tr, layers):
 
 
 def trace_summary(plan, token, position, layers):
-    """One traced persistent decode step (None when the plan does not use it)."""
+    """One traced persistent decode step (None when the plan does not use the
+    barrier form of the kernel, whose CTA trace points this summary reads)."""
+    if plan.decode_form() != 1:
+        return None
     tr = plan.trace(token, position)
     return None if tr is None else summarize_trace(tr, layers)
 
@@ -418,6 +421,9 @@ def run_trace_mode(args):
     if args.trace_raw:
         np.save(args.trace_raw, tr)
         np.save(args.trace_raw.replace(".npy", "") + "_warps.npy", res[1])
+    if plan.decode_form() != 1:  # the dataflow form: only the raw per-warp records mean anything
+        print(json.dumps({"decode_form": plan.decode_form(), "grid": int(tr.shape[1])}))
+        return
     res = summarize_trace(tr, model.config.layers)
     step = res.pop("step_us")
     print(json.dumps({"trace_us": res, "step_us": step, "grid": int(tr.shape[1]), "points": int(tr.shape[0])}))

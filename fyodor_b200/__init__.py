@@ -109,6 +109,8 @@ def _load():
     lib.fyb_plan_time_greedy.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t]
     lib.fyb_plan_launches_per_token.restype = C.c_ulonglong
     lib.fyb_plan_launches_per_token.argtypes = [_P]
+    lib.fyb_plan_decode_form.restype = C.c_int
+    lib.fyb_plan_decode_form.argtypes = [_P]
     lib.fyb_plan_profile.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t, _P]
     lib.fyb_plan_time_projection.restype = C.c_double
     lib.fyb_plan_time_projection.argtypes = [_P, C.c_uint, C.c_uint, C.c_uint, C.POINTER(C.c_size_t)]
@@ -125,7 +127,7 @@ lib = _load()
 EXPORTS = ["nya_cuda_backend", "fyb_version", "fyb_device_count", "fyb_dequantize", "fyb_quant_matmul_workspace",
            "fyb_quant_matmul", "fyb_attention_workspace", "fyb_attention_decode",
            "fyb_attention_decode_static", "fyb_plan_decode_greedy",
-           "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_profile", "fyb_plan_trace",
+           "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_decode_form", "fyb_plan_profile", "fyb_plan_trace",
            "fyb_plan_tp_info", "fyb_plan_tp_handle", "fyb_plan_tp_connect", "fyb_plan_time_projection",
            "fyb_synth_create",
            "fyb_synth_free", "fyb_synth_fill"]
@@ -280,6 +282,10 @@ class Plan:
     def launches_per_token(self):
         return lib.fyb_plan_launches_per_token(C.c_void_p(self.ptr))
 
+    def decode_form(self):
+        """0 per-operation kernels, 1 persistent kernel, 2 its dataflow form."""
+        return lib.fyb_plan_decode_form(C.c_void_p(self.ptr))
+
     def tp_info(self):
         """(rank, size) of the plan's tensor-parallel shard."""
         r, n = C.c_uint(0), C.c_uint(0)
@@ -301,12 +307,12 @@ class Plan:
     def trace(self, token, position, warps=False):
         """Per-CTA trace points of one persistent decode step: array
         [points][grid] of globaltimer nanoseconds, or None. With warps=True,
-        a pair (that array, per-warp GEMV points [layers*5 + 1][warps][4])."""
+        a pair (that array, per-warp GEMV records [layers*5 + 1][warps][8])."""
         grid = C.c_uint(0)
         L = self.model.config.layers
         n = (1 + 15 * L + 5) * 1024
         out = np.zeros(n, np.uint64)
-        wn = (L * 5 + 1) * 1024 * 16 * 4
+        wn = (L * 5 + 1) * 1024 * 16 * 8
         wout = np.zeros(wn, np.uint64) if warps else None
         r = lib.fyb_plan_trace(C.c_void_p(self.ptr), token, position, _ptr(out), n, C.byref(grid),
                                _ptr(wout) if warps else None, wn if warps else 0)
@@ -316,7 +322,7 @@ class Plan:
         if not warps:
             return cta
         nw = grid.value * 16
-        return cta, wout[: (L * 5 + 1) * nw * 4].reshape(L * 5 + 1, nw, 4)
+        return cta, wout[: (L * 5 + 1) * nw * 8].reshape(L * 5 + 1, nw, 8)
 
     def profile(self, token, position, steps):
         """Per-class milliseconds of one decode step: matrix, attention, other."""

@@ -18,16 +18,21 @@ FYB_DK_DECL(1, 64, 1) FYB_DK_DECL(1, 64, 2) FYB_DK_DECL(1, 64, 4) FYB_DK_DECL(1,
 // ------------------------------------------------------------ host side
 constexpr size_t SMEM_LIMIT = 227 * 1024;
 
-// Ring bytes per warp: what the rest of the layout leaves (or `want`, when
-// smaller), at most RING_BARS Q6_K units; 0 when fewer than two Q6_K units fit.
-static unsigned ring_bytes_for(const DecodeGeometry &g, unsigned want = 0)
+// Ring bytes per warp for the rest of the layout taking `other` bytes: what
+// is left (or `want`, when smaller but at least two Q6_K units), at most
+// RING_BARS Q6_K units; 0 when fewer than two Q6_K units fit.
+static unsigned ring_bytes_left(size_t other, unsigned want)
 {
-    const size_t other = smem_layout(g.d, g.ffn, g.H, g.Hkv, g.hd, 0).total;
     if (other >= SMEM_LIMIT) return 0;
     size_t rb = (SMEM_LIMIT - other) / QG_WARPS / 16 * 16;
     rb = std::min<size_t>(rb, (size_t)RING_BARS * Q6_UNIT);
-    if (want) rb = std::min<size_t>(rb, want / 16 * 16);
+    if (want) rb = std::min<size_t>(rb, std::max<size_t>(want / 16 * 16, 2 * Q6_UNIT));
     return rb >= 2 * Q6_UNIT ? (unsigned)rb : 0;
+}
+
+static unsigned ring_bytes_for(const DecodeGeometry &g, unsigned want = 0)
+{
+    return ring_bytes_left(smem_layout(g.d, g.ffn, g.H, g.Hkv, g.hd, 0).total, want);
 }
 
 static size_t decode_smem_bytes(const DecodeGeometry &g, unsigned want = 0)
@@ -76,15 +81,10 @@ static DecodeKernel decode_kernel_for(const DecodeGeometry &g, bool df = false)
     return nullptr;
 }
 
-// Ring bytes per warp of the dataflow form (as ring_bytes_for).
+// Ring bytes per warp of the dataflow form.
 static unsigned df_ring_bytes_for(const DecodeGeometry &g, unsigned want = 0)
 {
-    const size_t other = df_layout(g.d, g.ffn, g.H, g.Hkv, g.hd, 0).total;
-    if (other >= SMEM_LIMIT) return 0;
-    size_t rb = (SMEM_LIMIT - other) / QG_WARPS / 16 * 16;
-    rb = std::min<size_t>(rb, (size_t)RING_BARS * Q6_UNIT);
-    if (want) rb = std::min<size_t>(rb, want / 16 * 16);
-    return rb >= 2 * Q6_UNIT ? (unsigned)rb : 0;
+    return ring_bytes_left(df_layout(g.d, g.ffn, g.H, g.Hkv, g.hd, 0).total, want);
 }
 
 static size_t df_smem_bytes(const DecodeGeometry &g, unsigned want = 0)
@@ -156,6 +156,7 @@ int launch_decode(const DecodeLaunch &L, cudaStream_t s)
     if (df && (L.tp > 1 || !L.df.bgu || !L.df.bdn || !L.df.attn_kv)) return -1;
     p.df = L.df;
     if (df) p.ring_bytes = df_ring_bytes_for(L.g, L.ring_bytes);
+    if (p.ring_bytes < 2 * Q6_UNIT) return -1;  // every unit size needs two ring slots
     const size_t smem = df ? df_smem_bytes(L.g, L.ring_bytes) : decode_smem_bytes(L.g, L.ring_bytes);
     const DecodeKernel decode_kernel = decode_kernel_for(L.g, df);
     if (!decode_kernel) return -1;

@@ -296,7 +296,7 @@ FYB_DEV void df_output(const DecodeParams &p, const DfSync &ds, const Phase &ph,
                     __halves2half2(__float2half_rn(a), __float2half_rn(b));
             }
         }
-        __threadfence();
+        if (mine) __threadfence();  // the lanes that wrote, before the counter
         __syncwarp();
         if (lane == 0) atomicAdd(p.sync.qkv_done + l * p.Hkv + qkv_kvh(p, tile), 1u);
         return;
@@ -317,7 +317,7 @@ FYB_DEV void df_output(const DecodeParams &p, const DfSync &ds, const Phase &ph,
             dst[rA] = __fadd_rn(rsA, yA);
             dst[rB] = __fadd_rn(rsB, yB);
         }
-        __threadfence();
+        if (mine) __threadfence();  // the lanes that wrote, before the counter
         __syncwarp();
         if (lane == 0) atomicAdd((ph.kind == PH_O ? ds.bo : ds.bdn) + l * (p.d / 256) + tile / 16, 1u);
         return;
@@ -327,7 +327,7 @@ FYB_DEV void df_output(const DecodeParams &p, const DfSync &ds, const Phase &ph,
             const float g = __fdiv_rn(yA, __fadd_rn(1.0f, expf(-yA)));
             p.h[tile * 8 + gid] = __fmul_rn(g, yB);
         }
-        __threadfence();
+        if (mine) __threadfence();  // the lanes that wrote, before the counter
         __syncwarp();
         if (lane == 0) atomicAdd(ds.bgu + l * (p.ffn / 256) + tile / 32, 1u);
         return;
@@ -370,6 +370,7 @@ FYB_DEV bool df_gemv(const DecodeParams &p, const DfSync &ds, const DfShared &sh
     if (lane == 0) ok = spin_smem_geq(p, sh.exits + par, QG_WARPS * use);
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     if (ok) ok = df_eager_blocks(p, ds, ph, bf, seq, step, lane);
+    wstamp(p, ph, 4, lane);
     unsigned tb, te;
     cta_tiles(ph, tb, te);
     // tiles this warp touches (it may produce any of them: a shared tile's
@@ -383,9 +384,11 @@ FYB_DEV bool df_gemv(const DecodeParams &p, const DfSync &ds, const DfShared &sh
     unsigned tile = ta, tile_units = 0;
     unsigned blk = (unsigned)(r.u0 - (unsigned long long)tile * nblk);
     unsigned long long key = 0ull;
-    long long wait_cycles = 0;
+    long long wait_cycles = 0, block_cycles = 0, out_cycles = 0;
     for (unsigned i = 0; i < n && ok; ++i) {
+        const long long b0 = p.wtrace ? clock64() : 0;
         ok = df_ensure_block(p, ds, ph, bf, blk, seq, step, lane);
+        if (p.wtrace) block_cycles += clock64() - b0;
         if (!ok) break;
         if (i == 0 && fetch_resid) df_fetch_resid(p, ph, ta, tz, lane, in);
         const long long c0 = p.wtrace ? clock64() : 0;
@@ -399,6 +402,7 @@ FYB_DEV bool df_gemv(const DecodeParams &p, const DfSync &ds, const DfShared &sh
         const bool tile_end = blk + 1 == nblk;
         blk = tile_end ? 0 : blk + 1;
         if (tile_end || i + 1 == n) {
+            const long long o0 = p.wtrace ? clock64() : 0;
             const float yA = lane_total<1>(accA), yB = lane_total<1>(accB);
             if (tile_units == nblk) {
                 df_output(p, ds, ph, bf, tile, yA, yB, lane, key, in, ta, scale);
@@ -433,9 +437,12 @@ FYB_DEV bool df_gemv(const DecodeParams &p, const DfSync &ds, const DfShared &sh
             accA = 0.f; accB = 0.f;
             tile_units = 0;
             if (tile_end) ++tile;
+            if (p.wtrace) out_cycles += clock64() - o0;
         }
     }
-    wstamp(p, ph, 1, lane, (unsigned long long)wait_cycles);
+    wrecord(p, ph, 1, lane, (unsigned long long)wait_cycles);
+    wrecord(p, ph, 5, lane, (unsigned long long)block_cycles);
+    wrecord(p, ph, 6, lane, (unsigned long long)out_cycles);
     wstamp(p, ph, 2, lane);
     // the ring is empty: the next phase's weights start now
     if (ok && !warp_aborted(p)) ring_next(p, ph, r, lane);
@@ -571,7 +578,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_df_kernel(const DecodePa
     bool ok = true;
     stamp(p, ts);
     Phase cur = make_phase(p, PH_QKV, 0), nx0;
-    ring_begin(cur, ring, lane, phase_after(p, PH_QKV, 0, nx0) ? &nx0 : nullptr, p.l2_prefetch != 0);
+    ring_begin(cur, ring, lane, phase_after(p, PH_QKV, 0, nx0) ? &nx0 : nullptr, p.l2_prefetch);
     // A failed phase raises the abort word, so the CTA-wide wait before the
     // next attention phase fails for every warp: the CTA barriers stay in step.
     for (unsigned l = 0; l < p.nl; ++l) {

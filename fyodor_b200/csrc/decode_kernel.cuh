@@ -66,10 +66,10 @@ struct DecodeParams {
     unsigned *error;
     int logits_mode;
     unsigned ring_bytes;        // per warp, a multiple of 16
-    int l2_prefetch;            // prefetch the next phase's weights into L2
+    int l2_prefetch;            // L2 prefetch of weights: 0 none, 1 the phase after next, 2 the rest of the next phase
     unsigned long long *trace;  // optional [stamp][CTA] globaltimer values
     unsigned trace_slots;
-    unsigned long long *wtrace;  // optional [layer][phase kind][warp][4] globaltimer values
+    unsigned long long *wtrace;  // optional [layer][phase kind][warp][WTRACE_POINTS] records
     // tensor parallelism (tp > 1): H, Hkv, ffn and V above are this rank's
     unsigned tp, tp_rank, vocab0;
     unsigned char *const *peers;  // [tp] exchange regions, this rank's at tp_rank
@@ -213,10 +213,11 @@ FYB_DEV void ring_issue(Ring &r, unsigned lane)
 }
 
 // Start a phase on an empty ring: this warp's range, and its first units.
-// With `next`, the warp's units of the phase after this one are prefetched
-// into L2 (one bulk prefetch), so HBM streams them while this phase and the
-// barrier after it run.
-FYB_DEV void ring_begin(const Phase &ph, Ring &r, unsigned lane, const Phase *next, bool l2_prefetch)
+// L2 prefetch (one bulk prefetch per warp) mode 2: the warp's units of this
+// phase beyond the ring's first S, so HBM streams the whole phase into L2
+// while the CTAs still wait for its input; mode 1 (with `next`): the warp's
+// units of the phase after this one.
+FYB_DEV void ring_begin(const Phase &ph, Ring &r, unsigned lane, const Phase *next, int l2_prefetch)
 {
     warp_range(ph, r.u0, r.n);
     r.ub = unit_bytes(ph.w.type);
@@ -224,7 +225,9 @@ FYB_DEV void ring_begin(const Phase &ph, Ring &r, unsigned lane, const Phase *ne
     r.src = ph.w.units;
     r.issued = r.consumed = 0;
     while (r.issued < r.n && r.issued < r.S) ring_issue(r, lane);
-    if (next && l2_prefetch && lane == 0) {
+    if (l2_prefetch == 2 && r.n > r.S && lane == 0)
+        bulk_prefetch_l2(r.src + (r.u0 + r.S) * r.ub, (r.n - r.S) * r.ub);
+    if (next && l2_prefetch == 1 && lane == 0) {
         unsigned long long v0;
         unsigned nn;
         warp_range(*next, v0, nn);
@@ -583,20 +586,28 @@ FYB_DEV void ring_next(const DecodeParams &p, const Phase &ph, Ring &r, unsigned
     Phase nx, nx2;
     if (!phase_after(p, ph.kind, ph.layer, nx)) return;
     const bool has2 = phase_after(p, nx.kind, nx.layer, nx2);
-    ring_begin(nx, r, lane, has2 ? &nx2 : nullptr, p.l2_prefetch != 0);
+    ring_begin(nx, r, lane, has2 ? &nx2 : nullptr, p.l2_prefetch);
 }
 
 // ------------------------------------------------------------ GEMV phase
-// Profiling: per-warp points of a GEMV phase (entry, SM clock cycles spent
-// waiting for weights, all units computed, outputs done).
-FYB_DEV void wstamp(const DecodeParams &p, const Phase &ph, unsigned point, unsigned lane,
-    unsigned long long value = 0)
+// Profiling: per-warp records of a GEMV phase, WTRACE_POINTS words each:
+// 0 entry (ns), 1 SM clock cycles spent waiting for weights, 2 all units
+// computed (ns), 3 outputs done (ns); then in the barrier form the times
+// (ns) after 4 the CTA barrier following the units, 5 the shared tiles'
+// outputs, 6 the fence, 7 the second CTA barrier; in the dataflow form
+// 4 its input preparation at phase entry done (ns), 5 cycles waiting for
+// input blocks between units, 6 cycles spent in tile outputs.
+FYB_DEV void wrecord(const DecodeParams &p, const Phase &ph, unsigned point, unsigned lane, unsigned long long value)
 {
     if (!p.wtrace || lane) return;
     const unsigned long long NW = (unsigned long long)gridDim.x * QG_WARPS;
     const unsigned long long gw = (unsigned long long)blockIdx.x * QG_WARPS + (threadIdx.x >> 5);
     const unsigned slot = ph.kind == PH_LOGITS ? p.nl * 5 : ph.layer * 5 + ph.kind;
-    p.wtrace[((size_t)slot * NW + gw) * 4 + point] = point == 1 ? value : globaltimer();
+    p.wtrace[((size_t)slot * NW + gw) * WTRACE_POINTS + point] = value;
+}
+FYB_DEV void wstamp(const DecodeParams &p, const Phase &ph, unsigned point, unsigned lane)
+{
+    if (p.wtrace) wrecord(p, ph, point, lane, globaltimer());
 }
 
 // A warp's partial result for a tile it shares with other warps of its CTA.
@@ -653,11 +664,12 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, Ring &r, const X
         tile_units = 0;
         if (tile_end) ++tile;
     }
-    wstamp(p, ph, 1, lane, (unsigned long long)wait_cycles);
+    wrecord(p, ph, 1, lane, (unsigned long long)wait_cycles);
     wstamp(p, ph, 2, lane);
     // the ring is empty: the next phase's weights start now
     if (ok && !warp_aborted(p)) ring_next(p, ph, r, lane);
     __syncthreads();
+    wstamp(p, ph, 4, lane);
     // shared tiles: the warp with the tile's last unit sums every warp's part
     for (unsigned k = 0; k < 2; ++k) {
         const unsigned t = mine[k].tile;
@@ -670,9 +682,15 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, Ring &r, const X
         tile_output(p, ph, t, yA, yB, lane, key);
     }
     if (ph.kind == PH_LOGITS && lane == 0) keys[warp] = key;
-    if (p.tp > 1) __threadfence_system();  // outputs reach other GPUs before their counters move
-    else __threadfence();                  // this thread's outputs, before the CTA's counter update
+    wstamp(p, ph, 5, lane);
+    // the lanes that wrote outputs (tig 0) order them before the CTA's counter update
+    if ((lane & 3) == 0 || p.tp > 1) {  // (prep_tp's shares are written by any thread)
+        if (p.tp > 1) __threadfence_system();  // outputs reach other GPUs before their counters move
+        else __threadfence();
+    }
+    wstamp(p, ph, 6, lane);
     __syncthreads();
+    wstamp(p, ph, 7, lane);
     unsigned tb, te;
     cta_tiles(ph, tb, te);
     if (ph.kind == PH_QKV) {
@@ -1042,7 +1060,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
     const float *xparts = tp ? reinterpret_cast<const float *>(p.peers[p.tp_rank]) : nullptr;
     stamp(p, ts);
     Phase cur = make_phase(p, PH_QKV, 0), nx0;
-    ring_begin(cur, ring, lane, phase_after(p, PH_QKV, 0, nx0) ? &nx0 : nullptr, p.l2_prefetch != 0);
+    ring_begin(cur, ring, lane, phase_after(p, PH_QKV, 0, nx0) ? &nx0 : nullptr, p.l2_prefetch);
     for (unsigned l = 0; l < p.nl && ok; ++l) {
         // Q/K/V + RoPE + KV append
         if (tp) {  // x = x_mid + the ranks' down rows (or the embedding row); written to xa

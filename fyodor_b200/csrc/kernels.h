@@ -177,9 +177,9 @@ struct DecodeLaunch {
     int grid = 0;
     unsigned long long *trace = nullptr;  // profiling: [decode_trace_points()][grid] globaltimer ns
     unsigned trace_slots = 0;
-    unsigned long long *wtrace = nullptr;  // profiling: [layers*5 + 1][grid*16][4] per-warp GEMV points
+    unsigned long long *wtrace = nullptr;  // profiling: [layers*5 + 1][grid*16][WTRACE_POINTS] per-warp GEMV records
     unsigned ring_bytes = 0;  // per-warp weight ring (0: as much as shared memory allows)
-    int l2_prefetch = 1;      // prefetch each next phase's weights into L2
+    int l2_prefetch = 1;      // L2 prefetch of weights: 0 none, 1 the phase after next, 2 the rest of the next phase
     // tensor parallelism (tp > 1): g holds this rank's heads, FFN rows and
     // vocabulary rows (g.V), the d-row phases exchange partial sums
     unsigned tp = 1, tp_rank = 0, vocab0 = 0;
@@ -190,6 +190,7 @@ struct DecodeLaunch {
 };
 // Trace points per CTA of one step: start, per layer 5 x (idle, ready) + 4
 // preparations + attention end, logits (idle, ready, prepared), exit (idle, ready).
+constexpr unsigned WTRACE_POINTS = 8;  // words per warp and GEMV phase of the warp trace
 inline unsigned decode_trace_points(unsigned layers) { return 1 + 15 * layers + 3 + 2; }
 int decode_supported(const DecodeGeometry &g, unsigned type_out);
 size_t decode_partials_bytes(const DecodeGeometry &g, int grid);

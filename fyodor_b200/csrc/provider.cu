@@ -340,7 +340,7 @@ struct Plan {
     unsigned dec_splits = 1;
     size_t dec_bytes = 0;
     unsigned dec_ring_bytes = 6720;  // per-warp weight ring; NYA_CUDA_RING_BYTES (0 = largest)
-    int dec_l2_prefetch = 0;         // NYA_CUDA_L2_PREFETCH=1 prefetches each next phase into L2
+    int dec_l2_prefetch = 0;         // NYA_CUDA_L2_PREFETCH: 1 the phase after next into L2, 2 the rest of the next
     DecodeDfSync dec_df;             // NYA_CUDA_DATAFLOW=1: the dataflow form of the kernel
     // tensor parallelism: this plan holds rank tp_rank's shard of tp_size
     // (H, Hkv and ffn above are this rank's; V is the whole vocabulary)
@@ -703,7 +703,7 @@ static bool setup_persistent(Plan *p)
     size_t v;
     if (env_size("NYA_CUDA_RING_BYTES", &v)) p->dec_ring_bytes = (unsigned)std::min<size_t>(v, 1u << 20);
     const char *pf = std::getenv("NYA_CUDA_L2_PREFETCH");
-    p->dec_l2_prefetch = pf && !std::strcmp(pf, "1");
+    if (pf && (!std::strcmp(pf, "1") || !std::strcmp(pf, "2"))) p->dec_l2_prefetch = pf[0] - '0';
     DecodeGeometry g;
     g.nl = p->nl; g.d = p->d; g.H = p->H; g.Hkv = p->Hkv; g.hd = p->hd; g.ffn = p->ffn; g.V = p->vocab_rows;
     g.capacity = (unsigned)p->capacity;
@@ -1220,6 +1220,13 @@ extern "C" unsigned long long fyb_plan_launches_per_token(const void *opaque)
     return 3ull + 5ull * p->nl;
 }
 
+extern "C" int fyb_plan_decode_form(const void *opaque)
+{
+    const Plan *p = (const Plan *)opaque;
+    if (!p) return -1;
+    return !p->dec_grid ? 0 : p->dec_df.bo ? 2 : 1;
+}
+
 extern "C" int fyb_plan_tp_info(const void *opaque, unsigned *rank, unsigned *size)
 {
     const Plan *p = (const Plan *)opaque;
@@ -1278,7 +1285,7 @@ extern "C" long fyb_plan_trace(void *opaque, uint32_t token, size_t position, un
     if (out_count < n) return -1;
     DeviceScope scope(p->ctx->device);
     cudaStream_t s = p->ctx->stream;
-    const size_t wn = ((size_t)p->nl * 5 + 1) * p->dec_grid * 16 * 4;
+    const size_t wn = ((size_t)p->nl * 5 + 1) * p->dec_grid * 16 * WTRACE_POINTS;
     if (warp_out && warp_count < wn) return -1;
     unsigned long long *buf = nullptr, *wbuf = nullptr;
     if (cudaMalloc(&buf, n * 8) != cudaSuccess) { cudaGetLastError(); return -1; }

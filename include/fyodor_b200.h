@@ -107,6 +107,14 @@ double fyb_plan_time_greedy(void *plan, uint32_t token, size_t position, size_t 
    one kernel per operation. */
 unsigned long long fyb_plan_launches_per_token(const void *plan);
 
+/* Which decode step the plan runs: 0 one kernel per operation
+   (NYA_CUDA_PERSISTENT=0 or an unsupported geometry), 1 the persistent
+   kernel with CTA barriers between phases (default), 2 its dataflow form
+   (NYA_CUDA_DATAFLOW=1: phases start per 256-column input block as its
+   producers finish, no CTA barrier inside matrix phases; single GPU). -1 for
+   a null plan. */
+int fyb_plan_decode_form(const void *plan);
+
 /* Average duration (ms) of each kernel class of one decode step measured
    with CUDA events around eager launches: out[0] matrix kernels, out[1]
    attention, out[2] other. Returns 0 on success. */
@@ -121,11 +129,18 @@ int fyb_plan_profile(void *plan, uint32_t token, size_t position, size_t steps, 
    prepared); exit (idle, met). Returns the number of points per CTA and
    stores the grid in *grid_out, or -1 (plan without the persistent kernel,
    invalid arguments, out_count too small). With warp_out (may be NULL),
-   also per-warp points of every GEMV phase: warp_out[((layer*5 + phase) *
-   warps + warp) * 4 + k] (phase 0 QKV, 1 O, 2 gate/up, 3 down; layers*5 for
-   the logits), k = entry (ns), SM clock cycles spent waiting for weights,
-   units computed (ns), done (ns);
-   warp_count >= (layers*5 + 1) * grid * 16 * 4. */
+   also per-warp records of every GEMV phase: warp_out[((layer*5 + phase) *
+   warps + warp) * 8 + k] (phase 0 QKV, 1 O, 2 gate/up, 3 down; layers*5 for
+   the logits), k = 0 entry (ns), 1 SM clock cycles spent waiting for
+   weights, 2 units computed (ns), 3 done (ns); then the default form's
+   times (ns) after 4 the CTA barrier that follows the units, 5 the outputs
+   of tiles shared between warps, 6 the fence, 7 the second CTA barrier; the
+   dataflow form's 4 input preparation at phase entry done (ns), 5 cycles
+   waiting for input blocks between units, 6 cycles in tile outputs;
+   warp_count >= (layers*5 + 1) * grid * 16 * 8. The dataflow form has
+   fewer CTA points (start; per layer the CTA idle and ready points before
+   attention and the end of attention; exit idle and ready) and leaves the
+   rest 0. */
 long fyb_plan_trace(void *plan, uint32_t token, size_t position, unsigned long long *out, size_t out_count,
     unsigned *grid_out, unsigned long long *warp_out, size_t warp_count);
 

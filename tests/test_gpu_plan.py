@@ -179,3 +179,29 @@ def test_graphs_disabled_matches():
     assert _env_run(code, NYA_CUDA_GRAPHS=0).returncode == 0
     a, b = np.load("/tmp/fyb_graphs.npy"), np.load("/tmp/fyb_eager.npy")
     assert (a == b).all()
+
+
+@pytest.mark.parametrize("ring", ["4608", "0", "13440"])
+def test_ring_sizes_match(ring):
+    """NYA_CUDA_RING_BYTES changes only how many weight units each warp keeps
+    in flight: a request below two Q6_K units is raised to two, 0 takes what
+    shared memory leaves. Logits must equal the default ring's bitwise."""
+    code = ("import fyodor_b200 as F, numpy as np, sys\n"
+            "m=F.SynthModel(layers=2,embedding=512,heads=4,kv_heads=2,feed_forward=1024,vocabulary=1024,context=8,"
+            "matrix_type=F.Q4_K,embed_type=F.Q6_K,output_type=F.Q6_K,seed=6,norm_mode=2)\n"
+            "p=F.Provider().plan(m,8)\n"
+            "assert p.decode_form()==1\n"
+            "out=[]\n"
+            "for i in range(4):\n"
+            "    assert p.token(9+i,i)==0; out.append(p.logits.copy())\n"
+            "np.save(sys.argv[1] if len(sys.argv)>1 else '/tmp/x.npy', np.stack(out))\n")
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        a, b = os.path.join(d, "a.npy"), os.path.join(d, "b.npy")
+        run = lambda path, **env: subprocess.run([sys.executable, "-c", code, path], cwd=ROOT, capture_output=True,
+                                                 text=True, timeout=300, env=dict(os.environ, **env))
+        r1 = run(a)
+        assert r1.returncode == 0, r1.stderr
+        r2 = run(b, NYA_CUDA_RING_BYTES=ring)
+        assert r2.returncode == 0, r2.stderr
+        assert (np.load(a) == np.load(b)).all()
