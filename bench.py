@@ -242,6 +242,7 @@ def run_provider(args):
         cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "reference",
                "sample": "%d decode tokens of the same 8B model through the Fyodor engine's CPU provider "
                          "(nya_llm_session_run, NYA_CPU_THREADS=%d) from an empty cache; prompt not prefilled" % (n, threads)}
+    attn_c4 = attention_c4() if rank == 0 and world == 1 else None
     line = {
         "metric": "8B Q4_K decode tok/s (bs1)",
         "value": round(value, 2),
@@ -275,6 +276,7 @@ def run_provider(args):
                     "down": [round(down_ms * 1e3, 2), round(down_bytes / down_ms / 1e6, 1)],
                     "logits": [round(lg_ms * 1e3, 2), round(lg_bytes / lg_ms / 1e6, 1)],
                     "units": "stand-alone GEMV launches (matvec/matmul path): [us per launch, GB/s]"},
+        "attention_c4": attn_c4,
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
@@ -329,6 +331,52 @@ def run_reference(args):
                                        "cpu provider, positions 1..%d" % (per_step, pos)},
             "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def attention_c4(reps=20, warmup=3, splits_decode=32, splits_verify=8):
+    """The ragged-batch attention configuration: 32 sequences with context
+    lengths uniform in [128, 32768] (seeded), 32 query / 8 KV heads, head_dim
+    128, fp16 K/V; decode (one query per sequence) and speculative
+    verification (8 draft queries per sequence, causal within the draft).
+    [us per launch, GB/s] with GB/s = unique K/V bytes (4096 B per position
+    and KV-head group) plus q and out, over CUDA-event time."""
+    import ctypes as C
+    import torch
+    import fyodor_b200 as F
+    nseq, heads, kvh, hd, cap = 32, 32, 8, 128, 32768
+    rng = np.random.default_rng(1234)
+    lengths = rng.integers(128, cap + 1, size=nseq).astype(np.int32)
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    k = torch.randn((nseq, kvh, cap, hd), generator=g, device="cuda", dtype=torch.float16)
+    v = torch.randn((nseq, kvh, cap, hd), generator=g, device="cuda", dtype=torch.float16)
+    dl = torch.from_numpy(lengths).cuda()
+    P = lambda t: C.c_void_p(t.data_ptr())
+    kv_bytes = int(lengths.sum()) * kvh * hd * 2 * 2
+    res = {}
+    for name, queries, splits in (("decode", 1, splits_decode), ("verify8", 8, splits_verify)):
+        q = torch.randn((nseq, queries, heads, hd), generator=g, device="cuda")
+        out = torch.empty_like(q)
+        wsb = F.lib.fyb_attention_workspace(nseq * queries, heads, kvh, hd, splits)
+        ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+        call = lambda: F.lib.fyb_attention_verify(P(q), P(k), P(v), kvh * cap * hd, P(dl), nseq, queries, heads,
+                                                  kvh, hd, cap, C.c_float(1 / np.sqrt(hd)), P(out), splits, P(ws),
+                                                  wsb, C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        for _ in range(warmup):
+            assert call() == 0
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            call()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        nbytes = kv_bytes + 2 * q.numel() * 4
+        res[name] = [round(ms * 1e3, 1), round(nbytes / ms / 1e6, 1)]
+    del k, v
+    torch.cuda.empty_cache()
+    res["units"] = "[us per launch, GB/s of unique K/V + q + out]; 32 sequences, lengths U[128, 32768]"
+    return res
 
 
 # ----------------------------------------------------------------------------- profiling modes

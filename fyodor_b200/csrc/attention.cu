@@ -36,6 +36,7 @@ struct AtParams {
     unsigned long long seq_stride;
     const unsigned *lengths, *request;
     unsigned length, heads, kv_heads, capacity, splits;
+    unsigned queries;  // query rows per KV sequence (speculative verification: the draft tokens)
     float scale;
     float *out;
     float *partials;
@@ -57,14 +58,19 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
 
     pdl_launch_dependents();
     pdl_wait();
+    // row `seq` is query j = seq % queries of KV sequence seq / queries; with
+    // several queries, query j sits queries-1-j positions before the last one
+    // and attends only up to itself (causal within the draft)
+    const unsigned kvs = seq / p.queries, j = seq - kvs * p.queries;
     unsigned L = p.length;
-    if (p.lengths) L = p.lengths[seq];
+    if (p.lengths) L = p.lengths[kvs];
     else if (p.request) L = p.request[1] + 1;
+    if (p.queries > 1) L = L > p.queries - 1 - j ? L - (p.queries - 1 - j) : 1u;
     const unsigned chunk = (L + p.splits - 1) / p.splits;
     const unsigned c0 = min(L, sp * chunk), c1 = min(L, c0 + chunk);
 
-    const __half *K = p.k + seq * p.seq_stride + (size_t)kh * p.capacity * HD;
-    const __half *V = p.v + seq * p.seq_stride + (size_t)kh * p.capacity * HD;
+    const __half *K = p.k + kvs * p.seq_stride + (size_t)kh * p.capacity * HD;
+    const __half *V = p.v + kvs * p.seq_stride + (size_t)kh * p.capacity * HD;
     const float *qg = p.q + ((size_t)seq * p.heads + (size_t)kh * G) * HD;
     for (unsigned i = threadIdx.x; i < G * HD; i += AT_THREADS) qs[i / HD][i % HD] = qg[i];
     __syncthreads();
@@ -217,7 +223,7 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
 size_t attention_workspace_bytes(const AttentionLaunch &L)
 {
     const unsigned G = L.heads / L.kv_heads;
-    size_t pairs = (size_t)L.nseq * L.kv_heads;
+    size_t pairs = (size_t)L.nseq * L.queries * L.kv_heads;
     size_t partial = pairs * L.splits * G * (L.head_dim + 2) * sizeof(float);
     return (partial + 255) / 256 * 256 + (pairs * sizeof(unsigned) + 255) / 256 * 256;
 }
@@ -242,7 +248,8 @@ static cudaError_t launch_at(const AtParams &p, dim3 grid, cudaStream_t s, bool 
 int launch_attention(const AttentionLaunch &L, cudaStream_t s)
 {
     if (!L.q || !L.k || !L.v || !L.out || L.kv_heads == 0 || L.heads % L.kv_heads || L.splits == 0 ||
-        L.capacity == 0 || L.nseq == 0)
+        L.capacity == 0 || L.nseq == 0 || L.queries == 0 || L.queries > L.capacity ||
+        (size_t)L.nseq * L.queries > 65535)
         return -1;
     const unsigned G = L.heads / L.kv_heads;
     if (!L.workspace || L.workspace_bytes < attention_workspace_bytes(L)) return -1;
@@ -251,13 +258,15 @@ int launch_attention(const AttentionLaunch &L, cudaStream_t s)
     p.seq_stride = L.seq_stride;
     p.lengths = L.lengths; p.request = L.request; p.length = L.length;
     p.heads = L.heads; p.kv_heads = L.kv_heads; p.capacity = L.capacity; p.splits = L.splits;
+    p.queries = L.queries;
     p.scale = L.scale;
     p.out = L.out;
-    size_t pairs = (size_t)L.nseq * L.kv_heads;
+    const unsigned rows = L.nseq * L.queries;  // query rows (grid z)
+    size_t pairs = (size_t)rows * L.kv_heads;
     size_t partial = (pairs * L.splits * G * (L.head_dim + 2) * sizeof(float) + 255) / 256 * 256;
     p.partials = (float *)L.workspace;
     p.counters = (unsigned *)((unsigned char *)L.workspace + partial);
-    dim3 grid(L.splits, L.kv_heads, L.nseq);
+    dim3 grid(L.splits, L.kv_heads, rows);
     cudaError_t e = cudaErrorInvalidValue;
 #define FYB_AT(HDV, GV) if (L.head_dim == HDV && G == GV) e = launch_at<HDV, GV>(p, grid, s, L.pdl);
     FYB_AT(128, 1) FYB_AT(128, 2) FYB_AT(128, 4) FYB_AT(128, 8)

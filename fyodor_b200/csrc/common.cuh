@@ -56,6 +56,10 @@ FYB_DEV unsigned ldg_stream_u1(const void *p)
 }
 FYB_DEV void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2::evict_last [%0];" :: "l"(p)); }
 // Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, bytes a multiple of 16).
+// Release/acquire fence at GPU scope: orders this thread's earlier writes
+// before its later ones (the counter update after a tile's outputs).
+FYB_DEV void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 FYB_DEV void bulk_prefetch_l2(const void *p, unsigned bytes)
 {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");

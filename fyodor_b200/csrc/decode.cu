@@ -149,6 +149,8 @@ int launch_decode(const DecodeLaunch &L, cudaStream_t s)
     p.logits_mode = L.logits_mode;
     p.ring_bytes = ring_bytes_for(L.g, L.ring_bytes);
     p.l2_prefetch = L.l2_prefetch;
+    p.ring_pre = L.ring_pre;
+    p.kcache = L.kcache; p.vcache = L.vcache;
     p.trace = L.trace; p.trace_slots = L.trace_slots;
     p.wtrace = L.wtrace;
     p.tp = L.tp; p.tp_rank = L.tp_rank; p.vocab0 = L.vocab0; p.peers = L.peers; p.xl = L.xl;

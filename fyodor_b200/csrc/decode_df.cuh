@@ -214,43 +214,6 @@ FYB_DEV bool df_ensure_block(const DecodeParams &p, const DfSync &ds, const Phas
     return false;
 }
 
-// Inputs the output tiles of a warp need besides the GEMV result (for the
-// first two tiles it touches): RoPE factors (QKV) or residual rows (O, down).
-struct DfTileIn {
-    float a0, a1, b0, b1;
-};
-
-// RoPE factors of the QKV tiles (constant tables: loaded at phase start).
-FYB_DEV void df_fetch_rope(const DecodeParams &p, const Phase &ph, unsigned ta, unsigned tz, unsigned lane,
-    DfTileIn &in)
-{
-    const unsigned gid = lane >> 2;
-    const unsigned tq = p.H * p.hd / 16, tk = p.Hkv * p.hd / 16, hd = p.hd;
-    in.a0 = in.a1 = in.b0 = in.b1 = 0.f;
-    if (ph.kind != PH_QKV || (lane & 3)) return;
-    const unsigned pos = __ldcg(p.request + 1);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const unsigned t = ta + k;
-        if (t >= tz || t >= tq + tk) continue;
-        const unsigned lt = t < tq ? t : t - tq, pair = ((lt * 16 + 2 * gid) % hd) >> 1;
-        const float c = p.rope_cos[(size_t)pos * (hd >> 1) + pair], s = p.rope_sin[(size_t)pos * (hd >> 1) + pair];
-        if (k == 0) { in.a0 = c; in.b0 = s; } else { in.a1 = c; in.b1 = s; }
-    }
-}
-
-// Residual rows of the O (layers after the first) and down tiles: loaded once
-// the warp's first input block is ready, which orders them after their writers.
-FYB_DEV void df_fetch_resid(const DecodeParams &p, const Phase &ph, unsigned ta, unsigned tz, unsigned lane,
-    DfTileIn &in)
-{
-    const unsigned gid = lane >> 2;
-    if (lane & 3) return;
-    const float *src = ph.kind == PH_O ? p.xa : p.xm;
-    if (ta < tz) { in.a0 = __ldcg(src + ta * 16 + gid); in.b0 = __ldcg(src + ta * 16 + gid + 8); }
-    if (ta + 1 < tz) { in.a1 = __ldcg(src + (ta + 1) * 16 + gid); in.b1 = __ldcg(src + (ta + 1) * 16 + gid + 8); }
-}
-
 // The RMSNorm scale from the CTA's per-block sums (all blocks are ready).
 FYB_DEV float df_scale(const DecodeParams &p, const DfBuf &bf, unsigned nblk, unsigned lane)
 {
@@ -263,7 +226,7 @@ FYB_DEV float df_scale(const DecodeParams &p, const DfBuf &bf, unsigned nblk, un
 
 // Output of one complete tile and its counter update.
 FYB_DEV void df_output(const DecodeParams &p, const DfSync &ds, const Phase &ph, const DfBuf &bf, unsigned tile,
-    float yA, float yB, unsigned lane, unsigned long long &key, const DfTileIn &in, unsigned ta, float &scale)
+    float yA, float yB, unsigned lane, unsigned long long &key, const TileIn &in, unsigned ta, float &scale)
 {
     const unsigned gid = lane >> 2, l = ph.layer;
     const bool mine = (lane & 3) == 0;
@@ -291,7 +254,7 @@ FYB_DEV void df_output(const DecodeParams &p, const DfSync &ds, const Phase &ph,
                 *reinterpret_cast<float2 *>(p.q + rowA) = make_float2(a, b);
             } else {
                 const unsigned kvh = rowA / hd, dd = rowA % hd;
-                __half *cache = seg == 1 ? p.layers[l].kcache : p.layers[l].vcache;
+                __half *cache = seg == 1 ? kv_layer(p, l, false) : kv_layer(p, l, true);
                 *reinterpret_cast<__half2 *>(cache + ((size_t)kvh * p.capacity + pos) * hd + dd) =
                     __halves2half2(__float2half_rn(a), __float2half_rn(b));
             }
@@ -364,6 +327,7 @@ FYB_DEV bool df_gemv(const DecodeParams &p, const DfSync &ds, const DfShared &sh
         return false;
     }
     const DfBuf bf = par ? sh.b : sh.a;
+    while (r.issued < n && r.issued < r.S) ring_issue(r, lane);  // the ring may have started shallow
     const unsigned nblk = ph.nblk, gid = lane >> 2, tig = lane & 3;
     // the previous use of this buffer (two phases back) is over for every warp of the CTA
     bool ok = true;
@@ -376,9 +340,9 @@ FYB_DEV bool df_gemv(const DecodeParams &p, const DfSync &ds, const DfShared &sh
     // tiles this warp touches (it may produce any of them: a shared tile's
     // output comes from whichever warp completes it)
     const unsigned ta = (unsigned)(r.u0 / nblk), tz = (unsigned)((r.u0 + n + nblk - 1) / nblk);
-    DfTileIn in;
-    df_fetch_rope(p, ph, ta, tz, lane, in);
-    const bool fetch_resid = ph.kind == PH_DOWN || (ph.kind == PH_O && ph.layer > 0);
+    TileIn in;
+    fetch_rope(p, ph, ta, tz, lane, in);
+    const bool want_resid = ph.kind == PH_DOWN || (ph.kind == PH_O && ph.layer > 0);
     PartSlot *mine = sh.slots + (par * QG_WARPS + warp) * 2;
     float accA = 0.f, accB = 0.f, scale = -1.f;
     unsigned tile = ta, tile_units = 0;
@@ -390,7 +354,7 @@ FYB_DEV bool df_gemv(const DecodeParams &p, const DfSync &ds, const DfShared &sh
         ok = df_ensure_block(p, ds, ph, bf, blk, seq, step, lane);
         if (p.wtrace) block_cycles += clock64() - b0;
         if (!ok) break;
-        if (i == 0 && fetch_resid) df_fetch_resid(p, ph, ta, tz, lane, in);
+        if (i == 0 && want_resid) fetch_resid(p, ph, ta, tz, lane, in);
         const long long c0 = p.wtrace ? clock64() : 0;
         const unsigned char *unit = ring_wait(r);
         if (!unit) { raise_abort(p, ERR_TIMEOUT); ok = false; break; }
@@ -533,6 +497,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_df_kernel(const DecodePa
     ring.base = smem + (size_t)warp * p.ring_bytes;
     ring.bars = reinterpret_cast<uint64_t *>(smem + lay.bars) + warp * RING_BARS;
     ring.bytes = p.ring_bytes;
+    ring.pre = p.ring_pre;
     ring.par = 0;
     ring.issued = ring.consumed = ring.n = 0;
     DfShared sh;

@@ -66,6 +66,7 @@ struct DecodeParams {
     unsigned *error;
     int logits_mode;
     unsigned ring_bytes;        // per warp, a multiple of 16
+    unsigned ring_pre;          // units a warp requests when it starts a phase's ring early (0: all S)
     int l2_prefetch;            // L2 prefetch of weights: 0 none, 1 the phase after next, 2 the rest of the next phase
     unsigned long long *trace;  // optional [stamp][CTA] globaltimer values
     unsigned trace_slots;
@@ -74,6 +75,7 @@ struct DecodeParams {
     unsigned tp, tp_rank, vocab0;
     unsigned char *const *peers;  // [tp] exchange regions, this rank's at tp_rank
     XchgLayout xl;
+    __half *kcache, *vcache;      // all layers' caches in one allocation each (null: use the layer table)
     DecodeDfSync df;  // dataflow form only (df.bo null otherwise)
 };
 
@@ -91,7 +93,7 @@ struct Phase {
 struct Ring {
     unsigned char *base;
     uint64_t *bars;
-    unsigned bytes, par;
+    unsigned bytes, par, pre;
     unsigned S, ub, issued, consumed, n;
     unsigned long long u0;
     const unsigned char *src;
@@ -224,7 +226,8 @@ FYB_DEV void ring_begin(const Phase &ph, Ring &r, unsigned lane, const Phase *ne
     r.S = min(RING_BARS, r.bytes / r.ub);
     r.src = ph.w.units;
     r.issued = r.consumed = 0;
-    while (r.issued < r.n && r.issued < r.S) ring_issue(r, lane);
+    const unsigned pre = r.pre ? min(r.pre, r.S) : r.S;
+    while (r.issued < r.n && r.issued < pre) ring_issue(r, lane);
     if (l2_prefetch == 2 && r.n > r.S && lane == 0)
         bulk_prefetch_l2(r.src + (r.u0 + r.S) * r.ub, (r.n - r.S) * r.ub);
     if (next && l2_prefetch == 1 && lane == 0) {
@@ -420,12 +423,61 @@ FYB_DEV unsigned qkv_kvh(const DecodeParams &p, unsigned tile)
     return ((tile < tq + tk ? tile - tq : tile - tq - tk) * 16) / p.hd;
 }
 
+// Layer l's K (or V) cache: one allocation for all layers when the plan gives
+// its base (no pointer chase through the layer table), else the table.
+FYB_DEV __half *kv_layer(const DecodeParams &p, unsigned l, bool v)
+{
+    if (p.kcache) return (v ? p.vcache : p.kcache) + (size_t)l * p.Hkv * p.capacity * p.hd;
+    return v ? p.layers[l].vcache : p.layers[l].kcache;
+}
+
+// Inputs the output tiles of a warp need besides the GEMV result (for the
+// first two tiles it touches): RoPE factors (QKV) or residual rows (O, down).
+struct TileIn {
+    float a0, a1, b0, b1;
+};
+
+// RoPE factors of the QKV tiles (constant tables: loaded at phase start).
+FYB_DEV void fetch_rope(const DecodeParams &p, const Phase &ph, unsigned ta, unsigned tz, unsigned lane,
+    TileIn &in)
+{
+    const unsigned gid = lane >> 2;
+    const unsigned tq = p.H * p.hd / 16, tk = p.Hkv * p.hd / 16, hd = p.hd;
+    in.a0 = in.a1 = in.b0 = in.b1 = 0.f;
+    if (ph.kind != PH_QKV || (lane & 3)) return;
+    const unsigned pos = __ldcg(p.request + 1);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const unsigned t = ta + k;
+        if (t >= tz || t >= tq + tk) continue;
+        const unsigned lt = t < tq ? t : t - tq, pair = ((lt * 16 + 2 * gid) % hd) >> 1;
+        const float c = p.rope_cos[(size_t)pos * (hd >> 1) + pair], s = p.rope_sin[(size_t)pos * (hd >> 1) + pair];
+        if (k == 0) { in.a0 = c; in.b0 = s; } else { in.a1 = c; in.b1 = s; }
+    }
+}
+
+// Residual rows of the O (layers after the first) and down tiles. The
+// barrier form loads them at phase start (their writers finished phases
+// ago); the dataflow form once the warp's first input block is ready, which
+// orders them after their writers.
+FYB_DEV void fetch_resid(const DecodeParams &p, const Phase &ph, unsigned ta, unsigned tz, unsigned lane,
+    TileIn &in)
+{
+    const unsigned gid = lane >> 2;
+    if (lane & 3) return;
+    const float *src = ph.kind == PH_O ? p.xa : p.xm;
+    if (ta < tz) { in.a0 = __ldcg(src + ta * 16 + gid); in.b0 = __ldcg(src + ta * 16 + gid + 8); }
+    if (ta + 1 < tz) { in.a1 = __ldcg(src + (ta + 1) * 16 + gid); in.b1 = __ldcg(src + (ta + 1) * 16 + gid + 8); }
+}
+
 // Output of one complete tile (no fences, no counters). Lanes with tig == 0
 // hold yA (MMA row gid) and yB (row gid + 8). LOGITS folds the tile's rows
-// into the warp's running argmax key.
+// into the warp's running argmax key. `in` holds the RoPE factors or
+// residual rows of tiles ta and ta + 1 (other tiles load them here).
 FYB_DEV void tile_output(const DecodeParams &p, const Phase &ph, unsigned tile, float yA, float yB, unsigned lane,
-    unsigned long long &key)
+    unsigned long long &key, const TileIn &in, unsigned ta)
 {
+    const int k = tile == ta ? 0 : tile == ta + 1 ? 1 : -1;
     const unsigned gid = lane >> 2;
     const bool mine = (lane & 3) == 0;
     const unsigned l = ph.layer;
@@ -439,8 +491,8 @@ FYB_DEV void tile_output(const DecodeParams &p, const Phase &ph, unsigned tile, 
             const unsigned pos = __ldcg(p.request + 1), pair = (rowA % hd) >> 1;
             float a = yA, b = yB;
             if (seg <= 1) {
-                const float c = p.rope_cos[(size_t)pos * (hd >> 1) + pair];
-                const float s = p.rope_sin[(size_t)pos * (hd >> 1) + pair];
+                const float c = k == 0 ? in.a0 : k == 1 ? in.a1 : p.rope_cos[(size_t)pos * (hd >> 1) + pair];
+                const float s = k == 0 ? in.b0 : k == 1 ? in.b1 : p.rope_sin[(size_t)pos * (hd >> 1) + pair];
                 a = __fsub_rn(__fmul_rn(yA, c), __fmul_rn(yB, s));
                 b = __fadd_rn(__fmul_rn(yA, s), __fmul_rn(yB, c));
             }
@@ -448,7 +500,7 @@ FYB_DEV void tile_output(const DecodeParams &p, const Phase &ph, unsigned tile, 
                 *reinterpret_cast<float2 *>(p.q + rowA) = make_float2(a, b);
             } else {
                 const unsigned kvh = rowA / hd, dd = rowA % hd;
-                __half *cache = seg == 1 ? p.layers[l].kcache : p.layers[l].vcache;
+                __half *cache = kv_layer(p, l, seg == 2);
                 *reinterpret_cast<__half2 *>(cache + ((size_t)kvh * p.capacity + pos) * hd + dd) =
                     __halves2half2(__float2half_rn(a), __float2half_rn(b));
             }
@@ -473,13 +525,14 @@ FYB_DEV void tile_output(const DecodeParams &p, const Phase &ph, unsigned tile, 
         double sq = 0.0;
         if (mine) {
             float xA, xB;
+            const bool pre = k >= 0 && !(ph.kind == PH_O && l == 0);  // prefetched residual rows
             if (ph.kind == PH_O) {
-                xA = __fadd_rn(residual_in(p, l, rA), yA);
-                xB = __fadd_rn(residual_in(p, l, rB), yB);
+                xA = __fadd_rn(pre ? (k ? in.a1 : in.a0) : residual_in(p, l, rA), yA);
+                xB = __fadd_rn(pre ? (k ? in.b1 : in.b0) : residual_in(p, l, rB), yB);
                 p.xm[rA] = xA; p.xm[rB] = xB;
             } else {
-                xA = __fadd_rn(__ldcg(p.xm + rA), yA);
-                xB = __fadd_rn(__ldcg(p.xm + rB), yB);
+                xA = __fadd_rn(pre ? (k ? in.a1 : in.a0) : __ldcg(p.xm + rA), yA);
+                xB = __fadd_rn(pre ? (k ? in.b1 : in.b0) : __ldcg(p.xm + rB), yB);
                 p.xa[rA] = xA; p.xa[rB] = xB;
             }
             sq = (double)xA * (double)xA + (double)xB * (double)xB;
@@ -499,7 +552,7 @@ FYB_DEV void tile_output(const DecodeParams &p, const Phase &ph, unsigned tile, 
     // PH_LOGITS: store; argmax key = (order key, ~index) so ties go to the
     // lowest index (llm_cpu.c:896-905)
     const unsigned rA = tile * 16 + gid, rB = rA + 8;  // this rank's rows; p.vocab0 + row is the token
-    unsigned long long k = 0ull;
+    unsigned long long kk = 0ull;
     if (mine) {
         const bool okA = rA < p.V, okB = rB < p.V;
         if (p.tp == 1) {
@@ -516,14 +569,14 @@ FYB_DEV void tile_output(const DecodeParams &p, const Phase &ph, unsigned tile, 
         const unsigned gA = p.vocab0 + rA, gB = p.vocab0 + rB;
         const unsigned long long kA = okA ? ((unsigned long long)float_order_key(yA) << 32) | (0xffffffffu - gA) : 0ull;
         const unsigned long long kB = okB ? ((unsigned long long)float_order_key(yB) << 32) | (0xffffffffu - gB) : 0ull;
-        k = kA > kB ? kA : kB;
+        kk = kA > kB ? kA : kB;
     }
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
-        k = other > k ? other : k;
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, kk, o);
+        kk = other > kk ? other : kk;
     }
-    key = k > key ? k : key;
+    key = kk > key ? kk : key;
 }
 
 // Counter updates for `count` complete tiles starting at `first` (lane 0,
@@ -632,6 +685,12 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, Ring &r, const X
     wstamp(p, ph, 0, lane);
     const unsigned warp = threadIdx.x >> 5, n = r.n;
     const unsigned nblk = ph.nblk, gid = lane >> 2, tig = lane & 3;
+    while (r.issued < n && r.issued < r.S) ring_issue(r, lane);  // the ring may have started shallow
+    // side inputs of the first two tiles this warp touches, loaded while the units run
+    const unsigned ta = (unsigned)(r.u0 / nblk), tz = (unsigned)((r.u0 + n + nblk - 1) / nblk);
+    TileIn in;
+    fetch_rope(p, ph, ta, tz, lane, in);
+    if (p.tp == 1 && (ph.kind == PH_DOWN || (ph.kind == PH_O && ph.layer > 0))) fetch_resid(p, ph, ta, tz, lane, in);
     PartSlot *mine = parts + warp * 2;
     if (lane < 2) mine[lane].tile = ~0u;
     float accA = 0.f, accB = 0.f;
@@ -654,7 +713,7 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, Ring &r, const X
         if (!tile_end && i + 1 != n) continue;
         const float yA = lane_total<1>(accA), yB = lane_total<1>(accB);
         if (tile_units == nblk) {
-            tile_output(p, ph, tile, yA, yB, lane, key);
+            tile_output(p, ph, tile, yA, yB, lane, key, in, ta);
         } else if (np < 2) {  // only the first and the last tile can be shared
             if (tig == 0) { mine[np].v[gid] = yA; mine[np].v[gid + 8] = yB; }
             if (lane == 0) { mine[np].tile = tile; mine[np].last = tile_end ? 1u : 0u; }
@@ -679,14 +738,14 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, Ring &r, const X
 #pragma unroll
             for (unsigned j = 0; j < 2; ++j)
                 if (parts[w * 2 + j].tile == t) { yA += parts[w * 2 + j].v[gid]; yB += parts[w * 2 + j].v[gid + 8]; }
-        tile_output(p, ph, t, yA, yB, lane, key);
+        tile_output(p, ph, t, yA, yB, lane, key, in, ta);
     }
     if (ph.kind == PH_LOGITS && lane == 0) keys[warp] = key;
     wstamp(p, ph, 5, lane);
     // the lanes that wrote outputs (tig 0) order them before the CTA's counter update
     if ((lane & 3) == 0 || p.tp > 1) {  // (prep_tp's shares are written by any thread)
         if (p.tp > 1) __threadfence_system();  // outputs reach other GPUs before their counters move
-        else __threadfence();
+        else fence_acq_rel_gpu();
     }
     wstamp(p, ph, 6, lane);
     __syncthreads();
@@ -793,8 +852,8 @@ FYB_DEV void attention_item(const DecodeParams &p, unsigned l, unsigned kvh, uns
     const unsigned S = attn_parts(p, L);
     const unsigned chunk = (L + S - 1) / S;
     const unsigned c0 = min(L, sp * chunk), c1 = min(L, c0 + chunk);
-    const __half *K = p.layers[l].kcache + (size_t)kvh * p.capacity * HD + DPL * lane;
-    const __half *V = p.layers[l].vcache + (size_t)kvh * p.capacity * HD + DPL * lane;
+    const __half *K = kv_layer(p, l, false) + (size_t)kvh * p.capacity * HD + DPL * lane;
+    const __half *V = kv_layer(p, l, true) + (size_t)kvh * p.capacity * HD + DPL * lane;
     float qr[G][DPL];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -1026,6 +1085,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
     ring.base = smem + lay.rings + (size_t)warp * p.ring_bytes;
     ring.bars = reinterpret_cast<uint64_t *>(smem + lay.bars) + warp * RING_BARS;
     ring.bytes = p.ring_bytes;
+    ring.pre = p.ring_pre;
     ring.par = 0;
     ring.issued = ring.consumed = ring.n = 0;
     XBuf xb;

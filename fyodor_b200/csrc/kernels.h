@@ -88,6 +88,7 @@ struct AttentionLaunch {
     const unsigned *request = nullptr;  // device {token, position}: length = position + 1
     unsigned length = 0;            // host length when both pointers are null
     unsigned nseq = 1, heads = 32, kv_heads = 8, head_dim = 128, capacity = 0;
+    unsigned queries = 1;           // query rows per sequence; q and out then [nseq][queries][heads][hd]
     float scale = 0.f;
     float *out = nullptr;           // [nseq][heads][hd]
     unsigned splits = 0;            // partitions of the context per (seq, kv head)
@@ -180,6 +181,7 @@ struct DecodeLaunch {
     unsigned long long *wtrace = nullptr;  // profiling: [layers*5 + 1][grid*16][WTRACE_POINTS] per-warp GEMV records
     unsigned ring_bytes = 0;  // per-warp weight ring (0: as much as shared memory allows)
     int l2_prefetch = 1;      // L2 prefetch of weights: 0 none, 1 the phase after next, 2 the rest of the next phase
+    unsigned ring_pre = 0;    // units requested when a phase's ring starts (0: the whole ring)
     // tensor parallelism (tp > 1): g holds this rank's heads, FFN rows and
     // vocabulary rows (g.V), the d-row phases exchange partial sums
     unsigned tp = 1, tp_rank = 0, vocab0 = 0;
@@ -187,6 +189,8 @@ struct DecodeLaunch {
     XchgLayout xl;
     // dataflow kernel (single GPU): set to run it instead of the barrier form
     DecodeDfSync df;
+    // K and V caches of all layers, layer l at l*kv_heads*capacity*head_dim (optional)
+    __half *kcache = nullptr, *vcache = nullptr;
 };
 // Trace points per CTA of one step: start, per layer 5 x (idle, ready) + 4
 // preparations + attention end, logits (idle, ready, prepared), exit (idle, ready).

@@ -342,6 +342,7 @@ struct Plan {
     unsigned dec_ring_bytes = 6720;  // per-warp weight ring; NYA_CUDA_RING_BYTES (0 = largest)
     int dec_l2_prefetch = 0;         // NYA_CUDA_L2_PREFETCH: 1 the phase after next into L2, 2 the rest of the next
     DecodeDfSync dec_df;             // NYA_CUDA_DATAFLOW=1: the dataflow form of the kernel
+    unsigned dec_ring_pre = 0;       // NYA_CUDA_RING_PRE: units requested early per warp (0: whole ring)
     // tensor parallelism: this plan holds rank tp_rank's shard of tp_size
     // (H, Hkv and ffn above are this rank's; V is the whole vocabulary)
     unsigned tp_size = 1, tp_rank = 0, vocab_rows = 0, vocab0 = 0;
@@ -534,6 +535,8 @@ static DecodeLaunch persistent_launch(const Plan *p, StepMode mode)
     L.grid = p->dec_grid;
     L.ring_bytes = p->dec_ring_bytes;
     L.l2_prefetch = p->dec_l2_prefetch;
+    L.ring_pre = p->dec_ring_pre;
+    L.kcache = p->kcache; L.vcache = p->vcache;
     L.df = p->dec_df;
     if (p->tp_size > 1) {  // partial sums and logits go through the ranks' exchange regions
         L.tp = p->tp_size; L.tp_rank = p->tp_rank; L.vocab0 = p->vocab0;
@@ -704,6 +707,7 @@ static bool setup_persistent(Plan *p)
     if (env_size("NYA_CUDA_RING_BYTES", &v)) p->dec_ring_bytes = (unsigned)std::min<size_t>(v, 1u << 20);
     const char *pf = std::getenv("NYA_CUDA_L2_PREFETCH");
     if (pf && (!std::strcmp(pf, "1") || !std::strcmp(pf, "2"))) p->dec_l2_prefetch = pf[0] - '0';
+    if (env_size("NYA_CUDA_RING_PRE", &v)) p->dec_ring_pre = (unsigned)std::min<size_t>(v, 64);  // the kernel clamps to the ring
     DecodeGeometry g;
     g.nl = p->nl; g.d = p->d; g.H = p->H; g.Hkv = p->Hkv; g.hd = p->hd; g.ffn = p->ffn; g.V = p->vocab_rows;
     g.capacity = (unsigned)p->capacity;
@@ -1167,6 +1171,20 @@ extern "C" int fyb_attention_decode(const float *q, const void *k, const void *v
     L.seq_stride = seq_stride; L.lengths = lengths;
     L.nseq = nseq; L.heads = heads; L.kv_heads = kv_heads; L.head_dim = head_dim; L.capacity = capacity;
     L.scale = scale; L.out = out; L.splits = splits ? splits : 8;
+    L.workspace = workspace; L.workspace_bytes = workspace_bytes;
+    if (!lengths) return -1;
+    return launch_attention(L, (cudaStream_t)stream);
+}
+
+extern "C" int fyb_attention_verify(const float *q, const void *k, const void *v, size_t seq_stride,
+    const unsigned *lengths, unsigned nseq, unsigned queries, unsigned heads, unsigned kv_heads, unsigned head_dim,
+    unsigned capacity, float scale, float *out, unsigned splits, void *workspace, size_t workspace_bytes, void *stream)
+{
+    AttentionLaunch L;
+    L.q = q; L.k = (const __half *)k; L.v = (const __half *)v;
+    L.seq_stride = seq_stride; L.lengths = lengths;
+    L.nseq = nseq; L.queries = queries; L.heads = heads; L.kv_heads = kv_heads; L.head_dim = head_dim;
+    L.capacity = capacity; L.scale = scale; L.out = out; L.splits = splits ? splits : 8;
     L.workspace = workspace; L.workspace_bytes = workspace_bytes;
     if (!lengths) return -1;
     return launch_attention(L, (cudaStream_t)stream);

@@ -69,6 +69,19 @@ int fyb_attention_decode(const float *q, const void *k_cache, const void *v_cach
     unsigned capacity, float scale, float *out, unsigned splits, void *workspace, size_t workspace_bytes,
     void *stream);
 
+/* Speculative verification: `queries` query rows per sequence (the draft
+   tokens), causal within the draft (no counterpart in the reference, whose
+   verification runs the drafts one decode step at a time,
+   backend/core/llm_cpu.c:1274-1305). q and out are
+   [nseq][queries][heads][head_dim]; lengths[s] counts sequence s's cached
+   positions including its draft (>= queries), and query j attends positions
+   0 .. lengths[s] - queries + j. workspace: fyb_attention_workspace(nseq *
+   queries, ...) bytes, zero before the first call. nseq * queries <= 65535. */
+int fyb_attention_verify(const float *q, const void *k_cache, const void *v_cache, size_t seq_stride,
+    const unsigned *lengths, unsigned nseq, unsigned queries, unsigned heads, unsigned kv_heads, unsigned head_dim,
+    unsigned capacity, float scale, float *out, unsigned splits, void *workspace, size_t workspace_bytes,
+    void *stream);
+
 /* fyb_attention_decode without a workspace argument and without allocating
    anything (no counterpart in the reference). Same arguments and results as
    fyb_attention_decode; the scratch is a fixed array of
