@@ -333,7 +333,7 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def attention_c4(reps=20, warmup=3, splits_decode=32, splits_verify=8):
+def attention_c4(reps=20, warmup=3, splits_decode=16, splits_verify=4):
     """The ragged-batch attention configuration: 32 sequences with context
     lengths uniform in [128, 32768] (seeded), 32 query / 8 KV heads, head_dim
     128, fp16 K/V; decode (one query per sequence) and speculative
@@ -486,6 +486,7 @@ def main():
                     help="trace N persistent 8B decode steps per CTA and report the last (profiling)")
     ap.add_argument("--trace-raw", default="", help="with --trace-step: also save the raw trace (.npy)")
     ap.add_argument("--layers", type=int, default=0, help="with --eager-steps: layers of the model (small ncu cases)")
+    ap.add_argument("--attention", action="store_true", help="time the ragged-batch attention configuration only")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -496,6 +497,8 @@ def main():
     args = ap.parse_args()
     if args.kernel:
         run_kernel_mode(args)
+    elif args.attention:
+        print(json.dumps({"attention_c4": attention_c4(reps=args.reps, warmup=3)}))
     elif args.eager_steps:
         run_steps_mode(args)
     elif args.trace_step:

@@ -14,11 +14,15 @@
 // slots in partition order and writes the normalized output, so the result
 // does not depend on scheduling. Nothing of size L is materialized.
 //
-// Inside a CTA each warp takes 32 positions at a time: lane j computes the
-// full 128-wide dot products of position j with all G query heads (K row read
-// as 16-byte vectors, query broadcast from shared memory), the warp updates
-// the online softmax, then the lanes switch to 4 output dimensions each and
-// accumulate p * v over the 32 positions.
+// Inside a CTA (two warps: with 32 KB of stages per warp, three CTAs share an
+// SM, which measured faster than one CTA of four warps or six of one) each
+// warp takes tiles of 32 positions (warp w: tiles w, w + 2, ...),
+// double-buffered in shared memory: while it computes one tile, the
+// K and V rows of its next tile stream in through cp.async (16-byte chunks,
+// coalesced). Lane j computes the full dot products of position j with all G
+// query heads (K row read from its swizzled stage, query broadcast from
+// shared memory), the warp updates the online softmax, then the lanes switch
+// to DPL output dimensions each and accumulate p * v over the tile.
 #include "common.cuh"
 #include "fyodor_b200.h"
 #include "kernels.h"
@@ -27,7 +31,7 @@
 
 namespace fyb {
 
-constexpr int AT_WARPS = 4;
+constexpr int AT_WARPS = 2;
 constexpr int AT_THREADS = AT_WARPS * 32;
 
 struct AtParams {
@@ -42,6 +46,40 @@ struct AtParams {
     float *partials;
     unsigned *counters;
 };
+
+constexpr int AT_TILE = 32;    // positions per warp tile
+constexpr int AT_STAGES = 2;   // tiles per warp in shared memory (one streams in while one is used)
+
+FYB_DEV void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
+}
+FYB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+FYB_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+// Copy the K and V rows of positions [base, min(base + AT_TILE, end)) into a
+// warp's stage: 16-byte chunks, consecutive lanes on consecutive chunks
+// (coalesced). K chunk c of row r goes to chunk c ^ (r % (HD/8)) of its row,
+// so the lane-per-row dot products read shared memory without bank
+// conflicts; V keeps its layout (lanes read along a row).
+template <int HD>
+FYB_DEV void at_stage_tile(__half *Ks, __half *Vs, const __half *K, const __half *V, unsigned base, unsigned end,
+    unsigned lane)
+{
+    constexpr int CH = HD / 8;  // chunks per row
+    const unsigned rows = end > base ? min((unsigned)AT_TILE, end - base) : 0u;
+#pragma unroll 4
+    for (unsigned q = lane; q < rows * CH; q += 32) {
+        const unsigned r = q / CH, c = q % CH;
+        cp_async16(Ks + r * HD + ((c ^ (r % CH)) * 8), K + (size_t)(base + r) * HD + c * 8);
+        cp_async16(Vs + r * HD + c * 8, V + (size_t)(base + r) * HD + c * 8);
+    }
+}
+
+// Dynamic shared memory of attention_kernel<HD, *>: AT_STAGES stages of K
+// and V tiles per warp.
+constexpr size_t at_stage_bytes(int hd) { return (size_t)AT_WARPS * AT_STAGES * 2 * AT_TILE * hd * sizeof(__half); }
 
 template <int HD, int G>
 __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
@@ -83,41 +121,56 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
         for (int e = 0; e < DPL; ++e) o[g][e] = 0.f;
     }
 
-    for (unsigned base = c0 + warp * 32; base < c1; base += AT_WARPS * 32) {
+    // this warp's stages of (K tile, V tile): AT_TILE positions each
+    extern __shared__ __align__(128) unsigned char at_stage[];
+    __half *stage = reinterpret_cast<__half *>(at_stage) + (size_t)warp * AT_STAGES * 2 * AT_TILE * HD;
+    const unsigned ntiles = c1 > c0 ? (c1 - c0 + AT_TILE - 1) / AT_TILE : 0;
+    auto issue = [&](unsigned tile) {  // tile-th tile of this warp: positions c0 + (warp + AT_WARPS tile) * AT_TILE ...
+        const unsigned base = c0 + (warp + AT_WARPS * tile) * AT_TILE;
+        __half *Ks = stage + (size_t)(tile % AT_STAGES) * 2 * AT_TILE * HD, *Vs = Ks + AT_TILE * HD;
+        at_stage_tile<HD>(Ks, Vs, K, V, base, c1, lane);
+        cp_async_commit();
+    };
+    const unsigned mine = ntiles > warp ? (ntiles - warp + AT_WARPS - 1) / AT_WARPS : 0;  // tiles of this warp
+    for (unsigned t0 = 0; t0 + 1 < AT_STAGES && t0 < mine; ++t0) issue(t0);
+    for (unsigned it = 0; it < mine; ++it) {
+        // the stage of tile it + AT_STAGES - 1 held tile it - 1, done with at the end of the last pass
+        if (it + AT_STAGES - 1 < mine) issue(it + AT_STAGES - 1);
+        const unsigned ahead = min(mine - 1 - it, (unsigned)AT_STAGES - 1);  // groups that may stay in flight
+        if (ahead >= 2) cp_async_wait<2>();
+        else if (ahead == 1) cp_async_wait<1>();
+        else cp_async_wait<0>();
+        __syncwarp();
+        const unsigned base = c0 + (warp + AT_WARPS * it) * AT_TILE;
+        const __half *Ks = stage + (size_t)(it % AT_STAGES) * 2 * AT_TILE * HD, *Vs = Ks + AT_TILE * HD;
         const unsigned t = base + lane;
         const bool valid = t < c1;
         float s[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) s[g] = 0.f;
         if (valid) {
-            // the whole K row in two batches of loads, then the dot products
-            const uint4 *krow = reinterpret_cast<const uint4 *>(K + (size_t)t * HD);
+            // row `lane` of the K tile, chunk c stored at chunk c ^ (lane % CH) (no bank conflicts)
+            constexpr int CH = HD / 8;
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint4 kk[HD / 16];
+            for (int c = 0; c < CH; ++c) {
+                const uint4 kk = *reinterpret_cast<const uint4 *>(Ks + lane * HD + ((c ^ (lane % CH)) * 8));
+                const __half2 *h2 = reinterpret_cast<const __half2 *>(&kk);
+                float kf[8];
 #pragma unroll
-                for (int c = 0; c < HD / 16; ++c) kk[c] = __ldg(krow + half * (HD / 16) + c);
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f2 = __half22float2(h2[e]);
+                    kf[2 * e] = f2.x; kf[2 * e + 1] = f2.y;
+                }
 #pragma unroll
-                for (int c = 0; c < HD / 16; ++c) {
-                    const __half2 *h2 = reinterpret_cast<const __half2 *>(&kk[c]);
-                    float kf[8];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f2 = __half22float2(h2[e]);
-                        kf[2 * e] = f2.x; kf[2 * e + 1] = f2.y;
-                    }
-                    const int col = 8 * (half * (HD / 16) + c);
-#pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][col]);
-                        const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][col + 4]);
-                        float acc = s[g];
-                        acc = fmaf(qa.x, kf[0], acc); acc = fmaf(qa.y, kf[1], acc);
-                        acc = fmaf(qa.z, kf[2], acc); acc = fmaf(qa.w, kf[3], acc);
-                        acc = fmaf(qb.x, kf[4], acc); acc = fmaf(qb.y, kf[5], acc);
-                        acc = fmaf(qb.z, kf[6], acc); acc = fmaf(qb.w, kf[7], acc);
-                        s[g] = acc;
-                    }
+                for (int g = 0; g < G; ++g) {
+                    const float4 qa = *reinterpret_cast<const float4 *>(&qs[g][8 * c]);
+                    const float4 qb = *reinterpret_cast<const float4 *>(&qs[g][8 * c + 4]);
+                    float acc = s[g];
+                    acc = fmaf(qa.x, kf[0], acc); acc = fmaf(qa.y, kf[1], acc);
+                    acc = fmaf(qa.z, kf[2], acc); acc = fmaf(qa.w, kf[3], acc);
+                    acc = fmaf(qb.x, kf[4], acc); acc = fmaf(qb.y, kf[5], acc);
+                    acc = fmaf(qb.z, kf[6], acc); acc = fmaf(qb.w, kf[7], acc);
+                    s[g] = acc;
                 }
             }
         }
@@ -135,39 +188,29 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
             pbuf[warp][lane][g] = pv;
         }
         __syncwarp();
-        const unsigned n = min(32u, c1 - base);
-        // V rows of the tile: all loads first (8 at a time), then the FMAs
-#pragma unroll
-        for (unsigned j0 = 0; j0 < 32; j0 += 8) {
-            if (j0 >= n) break;
-            float vf[8][DPL];
-#pragma unroll
-            for (unsigned jj = 0; jj < 8; ++jj) {
-                const unsigned j = j0 + jj < n ? j0 + jj : n - 1;
-                const __half *vrow = V + (size_t)(base + j) * HD + lane * DPL;
-                if constexpr (DPL == 4) {
-                    uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vrow));
-                    const float2 a = __half22float2(*reinterpret_cast<__half2 *>(&vv.x));
-                    const float2 b = __half22float2(*reinterpret_cast<__half2 *>(&vv.y));
-                    vf[jj][0] = a.x; vf[jj][1] = a.y; vf[jj][2] = b.x; vf[jj][3] = b.y;
-                } else {
-                    unsigned vv = __ldg(reinterpret_cast<const unsigned *>(vrow));
-                    const float2 a = __half22float2(*reinterpret_cast<__half2 *>(&vv));
-                    vf[jj][0] = a.x; vf[jj][1] = a.y;
-                }
+        const unsigned n = min((unsigned)AT_TILE, c1 - base);
+        // lanes own DPL output dimensions; V rows are read straight from the stage
+        for (unsigned j = 0; j < n; ++j) {
+            const __half *vrow = Vs + j * HD + lane * DPL;
+            float vf[DPL];
+            if constexpr (DPL == 4) {
+                const uint2 vv = *reinterpret_cast<const uint2 *>(vrow);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+                vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
+            } else {
+                const unsigned vv = *reinterpret_cast<const unsigned *>(vrow);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&vv));
+                vf[0] = a.x; vf[1] = a.y;
             }
 #pragma unroll
-            for (unsigned jj = 0; jj < 8; ++jj) {
-                if (j0 + jj >= n) break;
+            for (int g = 0; g < G; ++g) {
+                const float pj = pbuf[warp][j][g];
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float pj = pbuf[warp][j0 + jj][g];
-#pragma unroll
-                    for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pj, vf[jj][e], o[g][e]);
-                }
+                for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pj, vf[e], o[g][e]);
             }
         }
-        __syncwarp();
+        __syncwarp();  // the stage and pbuf are reused
     }
 
     // merge the warps of this CTA
@@ -233,9 +276,13 @@ static cudaError_t launch_at(const AtParams &p, dim3 grid, cudaStream_t s, bool 
 {
     cudaFuncSetAttribute(attention_kernel<HD, G>, cudaFuncAttributePreferredSharedMemoryCarveout,
                          cudaSharedmemCarveoutMaxShared);
+    if (cudaFuncSetAttribute(attention_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)at_stage_bytes(HD)) != cudaSuccess)
+        return cudaErrorInvalidConfiguration;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(AT_THREADS);
+    cfg.dynamicSmemBytes = at_stage_bytes(HD);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
