@@ -243,6 +243,7 @@ def run_provider(args):
                "sample": "%d decode tokens of the same 8B model through the Fyodor engine's CPU provider "
                          "(nya_llm_session_run, NYA_CPU_THREADS=%d) from an empty cache; prompt not prefilled" % (n, threads)}
     attn_c4 = attention_c4() if rank == 0 and world == 1 else None
+    mv_c2 = matvec_c2() if rank == 0 and world == 1 else None
     line = {
         "metric": "8B Q4_K decode tok/s (bs1)",
         "value": round(value, 2),
@@ -277,6 +278,7 @@ def run_provider(args):
                     "logits": [round(lg_ms * 1e3, 2), round(lg_bytes / lg_ms / 1e6, 1)],
                     "units": "stand-alone GEMV launches (matvec/matmul path): [us per launch, GB/s]"},
         "attention_c4": attn_c4,
+        "matvec_c2": mv_c2,
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
@@ -377,6 +379,57 @@ def attention_c4(reps=20, warmup=3, splits_decode=16, splits_verify=4):
     torch.cuda.empty_cache()
     res["units"] = "[us per launch, GB/s of unique K/V + q + out]; 32 sequences, lengths U[128, 32768]"
     return res
+
+
+def matvec_c2(reps=10, warmup=3):
+    """The matvec / small-batch GEMM sweep: Q4_K and Q6_K weights of the four
+    projection shapes (out x in) at batches 1, 2, 4, 8, 16, repacked once
+    (fyb_quant_repack) and multiplied with fyb_quant_matmul_prepared. Consecutive
+    timed launches rotate over copies of the weights totalling at least 512 MB
+    (more than L2). Values: {shape: {type: {batch: [us, GB/s]}}}, GB/s =
+    (GGUF weight bytes once + 4 B x batch x (in + out)) / time."""
+    import ctypes as C
+    import torch
+    import fyodor_b200 as F
+    P = lambda t: C.c_void_p(t.data_ptr())
+    stream = lambda: C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out = {}
+    for rows, cols in ((4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)):
+        shape = "%dx%d" % (rows, cols)
+        out[shape] = {}
+        for tname, t in (("q4_k", F.Q4_K), ("q6_k", F.Q6_K)):
+            nbytes = rows * F.row_bytes(t, cols)
+            data = np.empty(nbytes, np.uint8)
+            F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, t, 2024, rows * 7 + cols)
+            wsb = F.lib.fyb_quant_matmul_workspace(rows, cols, t, 16)
+            ws0 = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+            dw = torch.from_numpy(data).cuda()
+            assert F.lib.fyb_quant_repack(P(dw), rows, cols, t, P(ws0), wsb, stream()) == 0
+            del dw
+            copies = [ws0] + [ws0.clone() for _ in range(max(0, -(-(512 << 20) // wsb) - 1))]
+            x = torch.randn((16, cols), device="cuda")
+            y = torch.empty((16, rows), device="cuda")
+            res = {}
+            for batch in (1, 2, 4, 8, 16):
+                for i in range(warmup):
+                    F.lib.fyb_quant_matmul_prepared(rows, cols, t, P(x), P(y), batch, P(copies[i % len(copies)]),
+                                                    wsb, stream())
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for i in range(reps):
+                    r = F.lib.fyb_quant_matmul_prepared(rows, cols, t, P(x), P(y), batch,
+                                                        P(copies[i % len(copies)]), wsb, stream())
+                    assert r == 0
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / reps
+                res[batch] = [round(ms * 1e3, 2), round((nbytes + 4 * batch * (rows + cols)) / ms / 1e6, 1)]
+            out[shape][tname] = res
+            del copies, ws0
+            torch.cuda.empty_cache()
+    out["units"] = "[us per call, GB/s of GGUF weight bytes once + x + y]; batches > 2 run ceil(batch/2) passes"
+    return out
 
 
 # ----------------------------------------------------------------------------- profiling modes
@@ -487,6 +540,7 @@ def main():
     ap.add_argument("--trace-raw", default="", help="with --trace-step: also save the raw trace (.npy)")
     ap.add_argument("--layers", type=int, default=0, help="with --eager-steps: layers of the model (small ncu cases)")
     ap.add_argument("--attention", action="store_true", help="time the ragged-batch attention configuration only")
+    ap.add_argument("--matvec", action="store_true", help="time the matvec / small-batch GEMM sweep only")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -497,6 +551,8 @@ def main():
     args = ap.parse_args()
     if args.kernel:
         run_kernel_mode(args)
+    elif args.matvec:
+        print(json.dumps({"matvec_c2": matvec_c2()}))
     elif args.attention:
         print(json.dumps({"attention_c4": attention_c4(reps=args.reps, warmup=3)}))
     elif args.eager_steps:

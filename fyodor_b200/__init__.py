@@ -93,6 +93,9 @@ def _load():
     lib.fyb_quant_matmul_workspace.restype = C.c_size_t
     lib.fyb_quant_matmul_workspace.argtypes = [C.c_size_t, C.c_size_t, C.c_uint, C.c_size_t]
     lib.fyb_quant_matmul.argtypes = [_P, C.c_size_t, C.c_size_t, C.c_uint, _P, _P, C.c_size_t, _P, C.c_size_t, _P]
+    lib.fyb_quant_repack.argtypes = [_P, C.c_size_t, C.c_size_t, C.c_uint, _P, C.c_size_t, _P]
+    lib.fyb_quant_matmul_prepared.argtypes = [C.c_size_t, C.c_size_t, C.c_uint, _P, _P, C.c_size_t, _P,
+                                              C.c_size_t, _P]
     lib.fyb_attention_workspace.restype = C.c_size_t
     lib.fyb_attention_workspace.argtypes = [C.c_uint] * 5
     lib.fyb_attention_decode.argtypes = [_P, _P, _P, C.c_size_t, _P, C.c_uint, C.c_uint, C.c_uint, C.c_uint,
@@ -127,7 +130,8 @@ lib = _load()
 
 # exported names declared in include/fyodor_b200.h
 EXPORTS = ["nya_cuda_backend", "fyb_version", "fyb_device_count", "fyb_dequantize", "fyb_quant_matmul_workspace",
-           "fyb_quant_matmul", "fyb_attention_workspace", "fyb_attention_decode", "fyb_attention_verify",
+           "fyb_quant_matmul", "fyb_quant_repack", "fyb_quant_matmul_prepared", "fyb_attention_workspace",
+           "fyb_attention_decode", "fyb_attention_verify",
            "fyb_attention_decode_static", "fyb_plan_decode_greedy",
            "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_decode_form", "fyb_plan_profile", "fyb_plan_trace",
            "fyb_plan_tp_info", "fyb_plan_tp_handle", "fyb_plan_tp_connect", "fyb_plan_time_projection",

@@ -1153,6 +1153,42 @@ extern "C" int fyb_quant_matmul(const void *w, size_t rows, size_t cols, unsigne
     return device_matmul(&qw, w, row_bytes, rows, cols, type, x, y, batch, sc, s, sms) ? -2 : 0;
 }
 
+// fyb_quant_matmul in two halves: the repack into the workspace's units
+// (once per weight matrix), then any number of products from them.
+extern "C" int fyb_quant_repack(const void *w, size_t rows, size_t cols, unsigned type, void *workspace,
+    size_t workspace_bytes, void *stream)
+{
+    size_t block, bbytes;
+    if (!w || !rows || !cols || rows > 0x7fffffffu || !type_geometry(type, &block, &bbytes) || cols % block ||
+        !qgemv_supported(type, cols, 1) || !workspace)
+        return -1;
+    size_t cb, pb, ub;
+    qm_layout(rows, cols, type, current_sms(), &cb, &pb, &ub);
+    if (workspace_bytes < cb + pb + ub) return -1;
+    unsigned char *ws = (unsigned char *)workspace;
+    return repack_units(w, nullptr, rows, cols, type, REPACK_PLAIN, ws + cb + pb, (unsigned)((rows + 15) / 16),
+                        (cudaStream_t)stream) ? -2 : 0;
+}
+
+extern "C" int fyb_quant_matmul_prepared(size_t rows, size_t cols, unsigned type, const float *x, float *y,
+    size_t batch, void *workspace, size_t workspace_bytes, void *stream)
+{
+    if (!x || !y || !rows || !cols || !batch || rows > 0x7fffffffu || !qgemv_supported(type, cols, 1) || !workspace)
+        return -1;
+    const int sms = current_sms();
+    size_t cb, pb, ub;
+    qm_layout(rows, cols, type, sms, &cb, &pb, &ub);
+    if (workspace_bytes < cb + pb + ub) return -1;
+    unsigned char *ws = (unsigned char *)workspace;
+    QWeights qw;
+    qw.units = ws + cb + pb; qw.type = type; qw.cols = (unsigned)cols; qw.tiles = (unsigned)((rows + 15) / 16);
+    unsigned *counters = (unsigned *)ws;
+    float *partials = (float *)(ws + cb);
+    size_t cbytes = cb, pbytes = pb;
+    const Scratch sc{&counters, &cbytes, &partials, &pbytes};
+    return device_matmul(&qw, nullptr, 0, rows, cols, type, x, y, batch, sc, (cudaStream_t)stream, sms) ? -2 : 0;
+}
+
 extern "C" size_t fyb_attention_workspace(unsigned nseq, unsigned heads, unsigned kv_heads, unsigned head_dim, unsigned splits)
 {
     if (!kv_heads || !nseq) return 0;

@@ -55,6 +55,15 @@ size_t fyb_quant_matmul_workspace(size_t rows, size_t columns, unsigned type, si
 int fyb_quant_matmul(const void *weights, size_t rows, size_t columns, unsigned type,
     const float *x, float *y, size_t batch, void *workspace, size_t workspace_bytes, void *stream);
 
+/* fyb_quant_matmul in two halves (Q4_K/Q6_K only, -1 for other types): the
+   repack of W into the workspace's units, once per weight matrix, then any
+   number of products from the repacked workspace (the timed path of the
+   matvec sweep). Same workspace size and results as fyb_quant_matmul. */
+int fyb_quant_repack(const void *weights, size_t rows, size_t columns, unsigned type, void *workspace,
+    size_t workspace_bytes, void *stream);
+int fyb_quant_matmul_prepared(size_t rows, size_t columns, unsigned type, const float *x, float *y, size_t batch,
+    void *workspace, size_t workspace_bytes, void *stream);
+
 /* Decode attention over an fp16 KV cache for a ragged batch of sequences
    (no reference counterpart at this level; the engine's semantics are
    backend/core/llm_cpu.c:510-535 with an F32 cache).

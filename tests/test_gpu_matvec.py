@@ -155,3 +155,31 @@ def test_f32_257x1025_like_engine_test(provider):
         e = w.reshape(rows, cols).astype(np.float64) @ x.astype(np.float64)
         bad = np.nonzero(np.abs(y - e) > 1e-4 * (1 + np.abs(e)))[0]
         assert bad.size == 0, (p, bad[:8].tolist(), y[bad[:4]].tolist(), e[bad[:4]].tolist())
+
+
+@pytest.mark.parametrize("type_id", [F.Q4_K, F.Q6_K])
+def test_prepared_matches_one_call(type_id):
+    """fyb_quant_repack + fyb_quant_matmul_prepared (repack once, multiply
+    many times) give fyb_quant_matmul's results bitwise, for odd and even
+    batches; the workspace's counters stay zero between calls."""
+    import torch
+    rows, cols = 1040, 4096
+    nbytes = rows * F.row_bytes(type_id, cols)
+    data = np.empty(nbytes, np.uint8)
+    F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, type_id, 7, 3)
+    dw = torch.from_numpy(data).cuda()
+    wsb = F.lib.fyb_quant_matmul_workspace(rows, cols, type_id, 5)
+    ws1 = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    ws2 = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    P = lambda t: C.c_void_p(t.data_ptr())
+    assert F.lib.fyb_quant_repack(P(dw), rows, cols, type_id, P(ws2), wsb, None) == 0
+    x = torch.randn((5, cols), device="cuda")
+    for batch in (1, 2, 3, 5):
+        y1 = torch.empty((batch, rows), device="cuda")
+        y2 = torch.empty((batch, rows), device="cuda")
+        assert F.lib.fyb_quant_matmul(P(dw), rows, cols, type_id, P(x), P(y1), batch, P(ws1), wsb, None) == 0
+        for _ in range(2):
+            assert F.lib.fyb_quant_matmul_prepared(rows, cols, type_id, P(x), P(y2), batch, P(ws2), wsb, None) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(y1, y2), batch
+    assert F.lib.fyb_quant_matmul_prepared(rows, cols, F.Q8_0, P(x), P(y2), 1, P(ws2), wsb, None) == -1
