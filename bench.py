@@ -229,10 +229,10 @@ def run_provider(args):
     bpt = mean_bytes_per_token() / world  # with tensor parallelism each GPU streams its shard
     per_launch_ms = total_ms / (args.steps * DECODE)
     achieved = bpt / (per_launch_ms / 1000.0) / 1e9
-    traffic = None
+    traffic = None  # ncu DRAM bytes per launch of the single-GPU kernel (no capture of a shard)
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get("decode_kernel_8b")
+            traffic = json.load(f).get("decode_kernel_8b") if world == 1 else None
     except (OSError, ValueError):
         pass
 

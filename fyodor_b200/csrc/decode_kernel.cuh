@@ -744,7 +744,9 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, Ring &r, const X
     wstamp(p, ph, 5, lane);
     // the lanes that wrote outputs (tig 0) order them before the CTA's counter update
     if ((lane & 3) == 0 || p.tp > 1) {  // (prep_tp's shares are written by any thread)
-        if (p.tp > 1) __threadfence_system();  // outputs reach other GPUs before their counters move
+        // phases whose outputs other GPUs read (the exchanged O and down rows,
+        // the gathered logits) order them at system scope before the counters
+        if (p.tp > 1 && (ph.kind == PH_O || ph.kind == PH_DOWN || ph.kind == PH_LOGITS)) __threadfence_system();
         else fence_acq_rel_gpu();
     }
     wstamp(p, ph, 6, lane);
