@@ -1,6 +1,6 @@
 """Benchmark: 8B-class Q4_K decode at batch 1 through the B200 provider.
 
-Workload (BASELINE config 3): a Llama-style decoder with 32 layers, d_model
+Workload: a Llama-style decoder with 32 layers, d_model
 4096, 32 query / 8 KV heads of 128, SwiGLU FFN 14336, vocabulary 128256,
 RMSNorm eps 1e-5, RoPE theta 500000; projections Q4_K, token embedding and
 output Q6_K; fp16 KV cache. Random-init weights from the seeded synthetic
@@ -17,9 +17,13 @@ e2e    tokens/s through the engine-facing vtable (plan_token with a host
 
 --impl reference times the Fyodor engine's own CPU path (compiled from the
 reference sources into oracle/_ref) on this host's cores for the same
-workload and metric.
+workload and metric: the same model bytes (oracle/libsynth.so, the seeded
+generator built on its own), the same 512-token prompt prefilled by the
+engine's batched CPU prefill, then greedy decode tokens at positions 512 and
+up. It loads no library of this provider.
 """
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -37,8 +41,17 @@ PROMPT = 512
 DECODE = 256
 CFG8B = dict(layers=32, embedding=4096, heads=32, kv_heads=8, feed_forward=14336, vocabulary=128256, context=1024,
              rope_base=500000.0, epsilon=1e-5, seed=1234, norm_mode=1)
-# algorithmic bytes per token: weights + mean KV read
+# algorithmic bytes per token: every weight byte once + the fp16 KV rows read
+# (Q4_K linears 3,925,868,544 + Q6_K output 430,940,160 + F32 norms
+# 1,064,960 + one Q6_K embedding row 3,360)
 WEIGHT_BYTES_8B = 4_357_877_024
+
+
+METRIC = "8B Q4_K decode tok/s (bs1)"
+CONFIG8B = {"workload": "8B-class Llama decode: prompt 512 then 256 greedy tokens per step, batch 1",
+            "layers": 32, "d_model": 4096, "heads": "32/8", "ffn": 14336, "vocab": 128256,
+            "weights": "Q4_K projections, Q6_K embedding/output", "kv": "fp16",
+            "l2": "inputs larger than L2 (4.36 GB of weights per token)"}
 
 
 def kv_bytes(position):  # fp16 K+V of every layer at attention length position+1
@@ -130,20 +143,36 @@ def barrier(dist):
 
 
 # ----------------------------------------------------------------------------- CPU reference
-def cpu_reference_rate(model, sample_seconds, max_tokens=64):
-    """Decode tokens through the engine's own CPU provider (its SIMD kernels and
-    worker pool, as fyodor-bench -b cpu) on this model; returns (tok/s, tokens,
+def cpu_reference_session(model_ptr, vocabulary):
+    """The engine's CPU provider (its SIMD kernels and worker pool, as
+    fyodor-bench -b cpu) on all host threads, with the bench prompt prefilled
+    by the engine's batched CPU prefill. Returns (session, first greedy token,
     threads)."""
     import oracle as O
     from tests.patterns import bench_tokens
     threads = os.cpu_count() or 1
     os.environ["NYA_CPU_THREADS"] = str(threads)
-    s = O.RefSession(model.ptr, 1024, model.vocabulary, provider="cpu")
-    toks = bench_tokens(max_tokens, model.vocabulary)
-    s.run(toks[:1])  # warm the worker pool and page in the weights
+    s = O.RefSession(model_ptr, PROMPT + DECODE, vocabulary, provider="cpu")
+    s.run(bench_tokens(PROMPT, vocabulary), each=False)
+    return s, int(np.argmax(s.logits())), threads
+
+
+def cpu_greedy(s, token, count):
+    """count greedy decode steps on an engine session; the last token."""
+    for _ in range(count):
+        s.run(np.array([token], np.uint32))
+        token = int(np.argmax(s.logits()))
+    return token
+
+
+def cpu_reference_rate(model_ptr, vocabulary, sample_seconds, max_tokens=64):
+    """Greedy decode on the engine's CPU provider at positions PROMPT.. (the
+    GPU's positions); returns (tok/s, tokens, threads)."""
+    s, t, threads = cpu_reference_session(model_ptr, vocabulary)
+    t = cpu_greedy(s, t, 1)  # warm the worker pool
     n, t0 = 0, time.perf_counter()
     while n < max_tokens - 1 and (time.perf_counter() - t0 < sample_seconds or n < 2):
-        s.run(toks[n + 1:n + 2])
+        t = cpu_greedy(s, t, 1)
         n += 1
     rate = n / (time.perf_counter() - t0)
     s.close()
@@ -170,8 +199,7 @@ def run_provider(args):
     if plan is None:
         raise SystemExit("the provider declined the 8B plan")
     if world > 1:
-        handle = plan.tp_handle()
-        if handle is None or plan.tp_connect(F.tp_exchange(handle)) != 0:
+        if not F.tp_connect_all(plan):
             raise SystemExit("connecting the tensor-parallel ranks failed")
         barrier(dist)
     prompt = bench_tokens(PROMPT, model.vocabulary)
@@ -195,6 +223,13 @@ def run_provider(args):
             total_ms += ms
     torch.cuda.synchronize()
     launches = plan.stats()["kernel_launches"] - launches_before  # counted by the plan, graph nodes included
+    # the first 64 greedy tokens of the timed decode (same start, same positions),
+    # comparable across GPU counts
+    digest_tokens = plan.decode_greedy(first, PROMPT, 64)
+    if digest_tokens is None:
+        raise SystemExit("greedy digest run failed")
+    digest = {"tokens": 64, "sha1": hashlib.sha1(np.asarray(digest_tokens, np.uint32).tobytes()).hexdigest()[:16],
+              "first8": [int(x) for x in digest_tokens[:8]]}
     barrier(dist)
     total_ms = max_over_ranks(dist, total_ms)
     tokens = args.steps * DECODE
@@ -238,14 +273,15 @@ def run_provider(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, n, threads = cpu_reference_rate(model, args.cpu_seconds)
+        rate, n, threads = cpu_reference_rate(model.ptr, model.vocabulary, args.cpu_seconds)
         cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "reference",
-               "sample": "%d decode tokens of the same 8B model through the Fyodor engine's CPU provider "
-                         "(nya_llm_session_run, NYA_CPU_THREADS=%d) from an empty cache; prompt not prefilled" % (n, threads)}
+               "sample": "%d greedy decode tokens of the same 8B model at positions 513.. through the Fyodor "
+                         "engine's CPU provider (nya_llm_session_run, NYA_CPU_THREADS=%d), after the same "
+                         "512-token prompt prefilled by its batched CPU prefill" % (n, threads)}
     attn_c4 = attention_c4() if rank == 0 and world == 1 else None
     mv_c2 = matvec_c2() if rank == 0 and world == 1 else None
     line = {
-        "metric": "8B Q4_K decode tok/s (bs1)",
+        "metric": METRIC,
         "value": round(value, 2),
         "unit": "tok/s",
         "n_gpus": world,
@@ -257,11 +293,8 @@ def run_provider(args):
         "vs_baseline": None,
         "dtype": "q4_k weights, s8 limb x u8/s8 int MMA, fp32 accumulate, fp16 KV",
         "data": "synthetic (seeded random-init weights, random prompt ids)",
-        "config": {"workload": "8B-class Llama decode: prompt 512 then 256 greedy tokens per step, batch 1",
-                   "layers": 32, "d_model": 4096, "heads": "32/8", "ffn": 14336, "vocab": 128256,
-                   "weights": "Q4_K projections, Q6_K embedding/output", "kv": "fp16",
-                   "parallelism": "tp%d" % world if world > 1 else "single-gpu",
-                   "l2": "inputs larger than L2 (4.36 GB of weights per token)"},
+        "config": dict(CONFIG8B, parallelism="tp%d" % world if world > 1 else "single-gpu"),
+        "greedy_digest": digest,
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * DECODE,
                 "d2h_bytes_per_step": 4 * model.vocabulary * DECODE},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
@@ -295,42 +328,41 @@ def run_provider(args):
 
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
-    import fyodor_b200 as F
+    """The engine's own CPU path on this host's cores: the bench model's bytes
+    from oracle/libsynth.so, the same prompt prefilled by the engine's batched
+    CPU prefill (untimed), then each step = ref_tokens greedy decode tokens at
+    the GPU arm's positions. No library of this provider is loaded."""
     import oracle as O
+    from oracle.synth import SynthModel, Q4_K, Q6_K
     rank, world, _ = dist_env()
     if rank != 0:
         return
     if not O.reference_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libnya_ref.so was not built"}))
         return
-    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **CFG8B)
+    model = SynthModel(matrix_type=Q4_K, embed_type=Q6_K, output_type=Q6_K, **CFG8B)
     per_step = max(1, args.ref_tokens)
-    threads = os.cpu_count() or 1
-    os.environ["NYA_CPU_THREADS"] = str(threads)
-    s = O.RefSession(model.ptr, 1024, model.vocabulary, provider="cpu")
-    from tests.patterns import bench_tokens
-    toks = bench_tokens(1 + (args.warmup + args.steps) * per_step, model.vocabulary)
-    s.run(toks[:1])
-    pos = 1
+    s, t, threads = cpu_reference_session(model.ptr, model.vocabulary)
     for _ in range(args.warmup):
-        for _ in range(per_step):
-            s.run(toks[pos:pos + 1]); pos += 1
+        t = cpu_greedy(s, t, per_step)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        for _ in range(per_step):
-            s.run(toks[pos:pos + 1]); pos += 1
+        t = cpu_greedy(s, t, per_step)
     elapsed = time.perf_counter() - t0
     value = args.steps * per_step / elapsed
+    last = PROMPT + (args.warmup + args.steps) * per_step
     s.close()
-    line = {"impl": "reference", "metric": "8B Q4_K decode tok/s (bs1)", "value": round(value, 3), "unit": "tok/s",
+    model.close()
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(elapsed * 1000 / args.steps, 2), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "q4_k weights, fp32 (engine CPU provider)",
-            "data": "synthetic (seeded random-init weights)",
-            "config": {"workload": "8B-class Llama decode, batch 1 (bounded CPU sample: %d tokens per step)" % per_step},
+            "data": "synthetic (seeded random-init weights, random prompt ids)",
+            "config": dict(CONFIG8B, parallelism="tp%d" % world if world > 1 else "single-gpu"),
             "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": threads, "kind": "reference",
-                             "sample": "%d decode tokens per step through nya_llm_session_run with the engine's "
-                                       "cpu provider, positions 1..%d" % (per_step, pos)},
+                             "sample": "%d greedy decode tokens per step through nya_llm_session_run with the "
+                                       "engine's cpu provider at positions %d..%d, after the 512-token prompt "
+                                       "(batched CPU prefill, untimed)" % (per_step, PROMPT + 1, last)},
             "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

@@ -107,6 +107,7 @@ def _load():
     lib.fyb_plan_tp_info.argtypes = [_P, _P, _P]
     lib.fyb_plan_tp_handle.argtypes = [_P, _P, C.c_size_t]
     lib.fyb_plan_tp_connect.argtypes = [_P, _P, C.c_size_t]
+    lib.fyb_plan_tp_disconnect.argtypes = [_P]
     lib.fyb_plan_trace.restype = C.c_long
     lib.fyb_plan_trace.argtypes = [_P, C.c_uint32, C.c_size_t, _P, C.c_size_t, _P, _P, C.c_size_t]
     lib.fyb_plan_decode_greedy.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t, _P]
@@ -134,7 +135,7 @@ EXPORTS = ["nya_cuda_backend", "fyb_version", "fyb_device_count", "fyb_dequantiz
            "fyb_attention_decode", "fyb_attention_verify",
            "fyb_attention_decode_static", "fyb_plan_decode_greedy",
            "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_decode_form", "fyb_plan_profile", "fyb_plan_trace",
-           "fyb_plan_tp_info", "fyb_plan_tp_handle", "fyb_plan_tp_connect", "fyb_plan_time_projection",
+           "fyb_plan_tp_info", "fyb_plan_tp_handle", "fyb_plan_tp_connect", "fyb_plan_tp_disconnect", "fyb_plan_time_projection",
            "fyb_synth_create",
            "fyb_synth_free", "fyb_synth_fill"]
 
@@ -200,6 +201,32 @@ def tp_exchange(handle, group=None):
     if any(h is None or len(h) != IPC_HANDLE_BYTES for h in out):
         raise ValueError("a rank has no exchange-region handle")
     return out
+
+
+def tp_connect_all(plan, group=None):
+    """Connect one rank's shard plan with every other rank's, or none of them.
+
+    Every rank calls this with its plan (None when its plan_create declined).
+    Returns True when all ranks opened all exchange regions. When any rank
+    has no plan or no handle, no rank connects; when any rank fails to open
+    the regions, the ranks that succeeded disconnect again. In both cases
+    every rank returns False and its plan declines its steps (-1) without
+    launching anything that would wait for the failed rank."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    handle = plan.tp_handle() if plan is not None else None
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(handle) if handle is not None else None, group=group)
+    if any(h is None or len(h) != IPC_HANDLE_BYTES for h in handles):
+        return False
+    ok = plan.tp_connect(handles) == 0
+    oks = [None] * world
+    dist.all_gather_object(oks, ok, group=group)
+    if not all(oks):
+        if ok:
+            plan.tp_disconnect()
+        return False
+    return True
 
 
 class Provider:
@@ -309,6 +336,10 @@ class Plan:
         """Open the other ranks' regions; handles: one bytes object per rank, in rank order."""
         blob = b"".join(handles)
         return lib.fyb_plan_tp_connect(C.c_void_p(self.ptr), C.c_char_p(blob), len(handles))
+
+    def tp_disconnect(self):
+        """Decline every later step without launching (another rank failed)."""
+        return lib.fyb_plan_tp_disconnect(C.c_void_p(self.ptr))
 
     def trace(self, token, position, warps=False):
         """Per-CTA trace points of one persistent decode step: array

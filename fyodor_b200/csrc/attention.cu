@@ -338,7 +338,11 @@ int launch_attention(const AttentionLaunch &L, cudaStream_t s)
 //
 // Set-up: the first call on a device (with that device current) looks up the
 // array's device address with cudaGetSymbolAddress and keeps it; that first
-// call should therefore come before any stream capture on the device. Every
+// call should therefore come before any stream capture on the device. The
+// kept address assumes the device's primary context lives until the process
+// exits (the provider never resets a device); after a reset it would be stale.
+// The array takes 4 MiB on every device that loads this library, whether or
+// not the entry point is called, outside any NYA_CUDA_MEMORY_MIB budget. Every
 // call clears the counters it will use (the only part that must start at
 // zero) with cudaMemsetAsync on the caller's stream, then launches.
 // Problems whose scratch exceeds FYB_ATTENTION_STATIC_SCRATCH_BYTES are
@@ -380,7 +384,12 @@ extern "C" int fyb_attention_decode_static(const float *q, const void *k, const 
     L.seq_stride = seq_stride; L.lengths = lengths;
     L.nseq = nseq; L.heads = heads; L.kv_heads = kv_heads; L.head_dim = head_dim; L.capacity = capacity;
     L.scale = scale; L.out = out; L.splits = splits ? splits : 8;
-    if (!lengths || !kv_heads || !nseq || heads % kv_heads) return -1;
+    // every argument launch_attention checks, checked before the stream is touched
+    if (!q || !k || !v || !out || !lengths || !kv_heads || !nseq || !capacity || heads % kv_heads ||
+        nseq > 65535 || (head_dim != 64 && head_dim != 128))
+        return -1;
+    const unsigned groups = heads / kv_heads;
+    if (groups != 1 && groups != 2 && groups != 4 && groups != 8) return -1;
     const size_t need = attention_workspace_bytes(L);
     if (need > kStaticScratchBytes) return -3;
     int device = -1;

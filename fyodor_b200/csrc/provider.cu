@@ -1327,6 +1327,14 @@ extern "C" int fyb_plan_tp_connect(void *opaque, const void *handles, size_t cou
     return 0;
 }
 
+extern "C" int fyb_plan_tp_disconnect(void *opaque)
+{
+    Plan *p = (Plan *)opaque;
+    if (!p || p->tp_size < 2) return -1;
+    p->connected = false;  // plan_token and the greedy loop now decline without launching
+    return 0;
+}
+
 extern "C" long fyb_plan_trace(void *opaque, uint32_t token, size_t position, unsigned long long *out,
     size_t out_count, unsigned *grid_out, unsigned long long *warp_out, size_t warp_count)
 {

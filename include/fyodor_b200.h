@@ -104,7 +104,10 @@ int fyb_attention_verify(const float *q, const void *k_cache, const void *v_cach
    - Returns -3, launching nothing, when the problem needs more scratch than
      the array holds (fyb_attention_workspace() gives the need).
    - One array per device: calls that overlap in time on one device (other
-     streams or threads) race on it and must be serialized by the caller. */
+     streams or threads) race on it and must be serialized by the caller.
+   - The array is resident on every device that loads the library (4 MiB,
+     outside the NYA_CUDA_MEMORY_MIB budget), and the address found at the
+     first call assumes the device's primary context is never reset. */
 #define FYB_ATTENTION_STATIC_SCRATCH_BYTES ((size_t)4 << 20)
 int fyb_attention_decode_static(const float *q, const void *k_cache, const void *v_cache, size_t seq_stride,
     const unsigned *lengths, unsigned nseq, unsigned heads, unsigned kv_heads, unsigned head_dim,
@@ -197,6 +200,10 @@ int fyb_plan_tp_info(const void *plan, unsigned *rank, unsigned *size);
 int fyb_plan_tp_handle(void *plan, void *handle, size_t bytes);
 /* opens the other ranks' regions; handles = count (= size) handles in rank order. */
 int fyb_plan_tp_connect(void *plan, const void *handles, size_t count);
+/* marks a connected plan unconnected again, so plan_token, plan_prefill and
+   the greedy loop return -1 without launching: what every rank does when
+   another rank could not create its plan or open the regions. */
+int fyb_plan_tp_disconnect(void *plan);
 
 /* ---- synthetic GGUF-layout models (no reference counterpart) -------------
    Builds an in-memory model in the engine's own binding layout

@@ -36,6 +36,8 @@ def _load_oracle():
     o.orc_round_f16.argtypes = [C.c_float]
     o.orc_dequantize.argtypes = [_P, C.c_uint32, C.c_size_t, _P]
     o.orc_matvec.argtypes = [_P, _P, C.c_uint32, _P, C.c_size_t, C.c_size_t]
+    o.orc_matvec_threaded.argtypes = [_P, _P, C.c_uint32, _P, C.c_size_t, C.c_size_t]
+    o.orc_set_threads.argtypes = [C.c_int]
     o.orc_attention.restype = C.c_int
     o.orc_attention.argtypes = [_P, _P, _P, _P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t,
                                 C.c_float, _P]
@@ -76,6 +78,21 @@ def matvec(data, type_id, x, cols, rows):
     data = np.ascontiguousarray(data)
     x = np.ascontiguousarray(x, np.float32)
     lib.orc_matvec(_arr(out), _arr(data), type_id, _arr(x), cols, rows)
+    return out
+
+
+def set_threads(n):
+    """Threads of the oracle's matrix products (sessions and matvec_threaded).
+    Each row keeps the engine's summation order, so results do not change."""
+    lib.orc_set_threads(int(n))
+
+
+def matvec_threaded(data, type_id, x, cols, rows):
+    """matvec with rows spread over the threads set by set_threads()."""
+    out = np.empty(rows, np.float32)
+    data = np.ascontiguousarray(data)
+    x = np.ascontiguousarray(x, np.float32)
+    lib.orc_matvec_threaded(_arr(out), _arr(data), type_id, _arr(x), cols, rows)
     return out
 
 

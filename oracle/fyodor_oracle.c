@@ -23,6 +23,7 @@
 #include "fyodor_b200_abi.h"
 
 #include <math.h>
+#include <pthread.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -136,12 +137,73 @@ void orc_dequantize(const unsigned char *data, uint32_t type, size_t count, floa
     for (size_t i = 0; i < count; ++i) out[i] = orc_tensor_value(&t, i);
 }
 
-/* llm_quant.c:145-312 - scalar reference matvec; identical summation order. */
-void orc_matvec(float *output, const unsigned char *data, uint32_t type,
-    const float *input, size_t columns, size_t rows)
+/* K-quant rows [row0, row1) four at a time: the four running sums are
+   independent chains, each updated in exactly the order of the scalar loop
+   below (block, group, value), so every row's result is bit-identical to
+   llm_quant.c:145-312; only the instruction-level interleaving differs. */
+static void orc_kquant_rows4(float *output, const unsigned char *data, uint32_t type, const float *input,
+    size_t columns, size_t row0)
+{
+    size_t block_bytes = type == NYA_LLM_TENSOR_Q4_K ? 144 : 210, blocks = columns / 256;
+    float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (size_t b = 0; b < blocks; ++b) {
+        const unsigned char *blk[4];
+        for (int r = 0; r < 4; ++r) blk[r] = data + (row0 + (size_t)r) * blocks * block_bytes + b * block_bytes;
+        const float *x = input + b * 256;
+        if (type == NYA_LLM_TENSOR_Q4_K) {
+            float d[4], minimum[4];
+            for (int r = 0; r < 4; ++r) { d[r] = orc_half_at(blk[r]); minimum[r] = orc_half_at(blk[r] + 2); }
+            for (size_t g = 0; g < 8; ++g) {
+                float factor[4], bias[4];
+                const unsigned char *packed[4];
+                for (int r = 0; r < 4; ++r) {
+                    const unsigned char *s = blk[r] + 4;
+                    unsigned sc = g < 4 ? s[g] & 63U : (s[g + 4] & 15U) | ((unsigned)(s[g - 4] >> 6) << 4);
+                    unsigned mn = g < 4 ? s[g + 4] & 63U : (s[g + 4] >> 4) | ((unsigned)(s[g] >> 6) << 4);
+                    factor[r] = d[r] * (float)sc;
+                    bias[r] = minimum[r] * (float)mn;
+                    packed[r] = blk[r] + 16 + g / 2 * 32;
+                }
+                unsigned shift = (unsigned)(g % 2 * 4);
+                for (size_t j = 0; j < 32; ++j) {
+                    float xv = x[g * 32 + j];
+                    for (int r = 0; r < 4; ++r)
+                        sum[r] += (factor[r] * (float)((packed[r][j] >> shift) & 15U) - bias[r]) * xv;
+                }
+            }
+        } else {
+            float d[4];
+            for (int r = 0; r < 4; ++r) d[r] = orc_half_at(blk[r] + 208);
+            for (size_t g = 0; g < 16; ++g) {
+                size_t half = g / 8, quarter = g % 8 / 2, lane_base = g % 2 * 16;
+                float factor[4];
+                for (int r = 0; r < 4; ++r) {
+                    int8_t sc; memcpy(&sc, blk[r] + 192 + g, 1);
+                    factor[r] = d[r] * (float)sc;
+                }
+                for (size_t j = 0; j < 16; ++j) {
+                    size_t lane = lane_base + j;
+                    float xv = x[g * 16 + j];
+                    for (int r = 0; r < 4; ++r) {
+                        unsigned lo = blk[r][half * 64 + quarter % 2 * 32 + lane];
+                        unsigned hi = blk[r][128 + half * 32 + lane];
+                        int q = (int)(((lo >> (quarter / 2 * 4)) & 15U) | (((hi >> (quarter * 2)) & 3U) << 4)) - 32;
+                        sum[r] += factor[r] * (float)q * xv;
+                    }
+                }
+            }
+        }
+    }
+    for (int r = 0; r < 4; ++r) output[row0 + (size_t)r] = sum[r];
+}
+
+/* llm_quant.c:145-312 - scalar reference matvec over rows [row0, row1);
+   identical summation order. */
+static void orc_matvec_range(float *output, const unsigned char *data, uint32_t type,
+    const float *input, size_t columns, size_t row0, size_t rows)
 {
     if (type == NYA_LLM_TENSOR_F32) {
-        for (size_t row = 0; row < rows; ++row) {
+        for (size_t row = row0; row < rows; ++row) {
             const unsigned char *w = data + row * columns * 4;
             double sum = 0.0f;
             for (size_t c = 0; c < columns; ++c) { float v; memcpy(&v, w + c * 4, 4); sum += (double)v * input[c]; }
@@ -150,7 +212,7 @@ void orc_matvec(float *output, const unsigned char *data, uint32_t type,
         return;
     }
     if (type == NYA_LLM_TENSOR_F16 || type == NYA_LLM_TENSOR_BF16) {
-        for (size_t row = 0; row < rows; ++row) {
+        for (size_t row = row0; row < rows; ++row) {
             const unsigned char *w = data + row * columns * 2;
             float sum = 0.0f;
             for (size_t c = 0; c < columns; ++c) {
@@ -167,7 +229,7 @@ void orc_matvec(float *output, const unsigned char *data, uint32_t type,
     }
     if (type == NYA_LLM_TENSOR_Q8_0) {
         size_t row_bytes = columns / 32 * 34;
-        for (size_t row = 0; row < rows; ++row) {
+        for (size_t row = row0; row < rows; ++row) {
             const unsigned char *w = data + row * row_bytes;
             float sum = 0.0f;
             for (size_t b = 0; b < columns / 32; ++b) {
@@ -184,7 +246,8 @@ void orc_matvec(float *output, const unsigned char *data, uint32_t type,
     }
     if (type == NYA_LLM_TENSOR_Q4_K || type == NYA_LLM_TENSOR_Q6_K) {
         size_t block_bytes = type == NYA_LLM_TENSOR_Q4_K ? 144 : 210, blocks = columns / 256;
-        for (size_t row = 0; row < rows; ++row) {
+        for (; row0 + 4 <= rows; row0 += 4) orc_kquant_rows4(output, data, type, input, columns, row0);
+        for (size_t row = row0; row < rows; ++row) {
             const unsigned char *row_data = data + row * blocks * block_bytes;
             float sum = 0.0f;
             for (size_t b = 0; b < blocks; ++b) {
@@ -224,7 +287,7 @@ void orc_matvec(float *output, const unsigned char *data, uint32_t type,
     }
     {   /* Q4_0: llm_quant.c:278-311 */
         size_t row_bytes = columns / 32 * 18;
-        for (size_t row = 0; row < rows; ++row) {
+        for (size_t row = row0; row < rows; ++row) {
             const unsigned char *w = data + row * row_bytes;
             float sum = 0.0f;
             for (size_t b = 0; b < columns / 32; ++b) {
@@ -240,6 +303,57 @@ void orc_matvec(float *output, const unsigned char *data, uint32_t type,
             output[row] = sum;
         }
     }
+}
+
+/* Worker of the threaded matvec: rows [row0, row1) of one call. */
+typedef struct {
+    float *output;
+    const unsigned char *data;
+    const float *input;
+    size_t columns, row0, row1;
+    uint32_t type;
+} orc_matvec_job;
+
+static void *orc_matvec_worker(void *arg)
+{
+    orc_matvec_job *j = (orc_matvec_job *)arg;
+    orc_matvec_range(j->output, j->data, j->type, j->input, j->columns, j->row0, j->row1);
+    return NULL;
+}
+
+static int orc_threads = 1;
+
+/* Threads used by the session's matrix products (rows split evenly; each
+   row is still summed in the reference order, so results do not depend on
+   the count). */
+void orc_set_threads(int threads) { orc_threads = threads < 1 ? 1 : threads > 256 ? 256 : threads; }
+
+/* llm_quant.c:145-312, the engine's scalar matvec: one thread per call. */
+void orc_matvec(float *output, const unsigned char *data, uint32_t type,
+    const float *input, size_t columns, size_t rows)
+{
+    orc_matvec_range(output, data, type, input, columns, 0, rows);
+}
+
+/* The same products with rows spread over orc_threads threads. */
+void orc_matvec_threaded(float *output, const unsigned char *data, uint32_t type,
+    const float *input, size_t columns, size_t rows)
+{
+    int n = orc_threads;
+    if (n <= 1 || rows < 64) { orc_matvec_range(output, data, type, input, columns, 0, rows); return; }
+    if ((size_t)n > rows / 16) n = (int)(rows / 16);
+    pthread_t tid[256];
+    int started[256];
+    orc_matvec_job job[256];
+    for (int t = 0; t < n; ++t) {
+        /* boundaries on multiples of four rows keep the four-row groups whole */
+        size_t a = rows * (size_t)t / (size_t)n / 4 * 4;
+        size_t b = t + 1 == n ? rows : rows * (size_t)(t + 1) / (size_t)n / 4 * 4;
+        job[t] = (orc_matvec_job){output, data, input, columns, a, b, type};
+        started[t] = t + 1 < n && pthread_create(&tid[t], NULL, orc_matvec_worker, &job[t]) == 0;
+        if (!started[t]) orc_matvec_worker(&job[t]);  /* the last share, or one whose thread did not start */
+    }
+    for (int t = 0; t < n; ++t) if (started[t]) pthread_join(tid[t], NULL);
 }
 
 /* llm_cpu.c:83-103 - RMSNorm; the sum of squares is accumulated in double. */
@@ -364,26 +478,26 @@ int orc_session_forward(orc_session *s, uint32_t token, size_t position, int com
         size_t offset = w->cache_offset * s->capacity;
         float *key = s->keys + offset + position * kvdim, *value = s->values + offset + position * kvdim;
         orc_rms_norm(s->norm, s->x, w->attention_norm, d, c->norm_epsilon);
-        orc_matvec(s->query, w->query->data, w->query->type, s->norm, d, qdim);
-        orc_matvec(key, w->key->data, w->key->type, s->norm, d, kvdim);
-        orc_matvec(value, w->value->data, w->value->type, s->norm, d, kvdim);
+        orc_matvec_threaded(s->query, w->query->data, w->query->type, s->norm, d, qdim);
+        orc_matvec_threaded(key, w->key->data, w->key->type, s->norm, d, kvdim);
+        orc_matvec_threaded(value, w->value->data, w->value->type, s->norm, d, kvdim);
         orc_rope(key, kvh, hd, s->co, s->si);
         if (s->kv_f16) for (size_t j = 0; j < kvdim; ++j) { key[j] = orc_round_f16(key[j]); value[j] = orc_round_f16(value[j]); }
         orc_rope(s->query, heads, hd, s->co, s->si);
         if (orc_attention(s->query, s->keys + offset, s->values + offset, s->norm, heads, kvh, hd,
                 0, position, 1.0f / sqrtf((float)hd), s->scores) != 0) return -1;
-        orc_matvec(s->residual, w->attention_output->data, w->attention_output->type, s->norm, qdim, d);
+        orc_matvec_threaded(s->residual, w->attention_output->data, w->attention_output->type, s->norm, qdim, d);
         for (size_t j = 0; j < d; ++j) s->x[j] += s->residual[j];
         orc_rms_norm(s->norm, s->x, w->feed_forward_norm, d, c->norm_epsilon);
-        orc_matvec(s->gate, w->feed_forward_gate->data, w->feed_forward_gate->type, s->norm, d, hid);
-        orc_matvec(s->up, w->feed_forward_up->data, w->feed_forward_up->type, s->norm, d, hid);
+        orc_matvec_threaded(s->gate, w->feed_forward_gate->data, w->feed_forward_gate->type, s->norm, d, hid);
+        orc_matvec_threaded(s->up, w->feed_forward_up->data, w->feed_forward_up->type, s->norm, d, hid);
         for (size_t j = 0; j < hid; ++j) { float g = s->gate[j]; s->gate[j] = g / (1.0f + expf(-g)) * s->up[j]; }
-        orc_matvec(s->residual, w->feed_forward_down->data, w->feed_forward_down->type, s->gate, hid, d);
+        orc_matvec_threaded(s->residual, w->feed_forward_down->data, w->feed_forward_down->type, s->gate, hid, d);
         for (size_t j = 0; j < d; ++j) s->x[j] += s->residual[j];
     }
     if (!compute_logits) return 0;
     orc_rms_norm(s->norm, s->x, c->output_norm, d, c->norm_epsilon);
-    orc_matvec(s->logits, c->output->data, c->output->type, s->norm, d, c->tokenizer.vocabulary_size);
+    orc_matvec_threaded(s->logits, c->output->data, c->output->type, s->norm, d, c->tokenizer.vocabulary_size);
     for (size_t j = 0; j < c->tokenizer.vocabulary_size; ++j) if (!isfinite(s->logits[j])) return -1;
     for (size_t j = 0; j < c->tokenizer.suppressed_count; ++j) s->logits[c->tokenizer.suppressed_tokens[j]] = -INFINITY;
     return 0;

@@ -112,16 +112,16 @@ def double_reference(data, type_id, xs, cols, rows, chunk=8192):
 @pytest.mark.parametrize("type_id", [F.Q4_K, F.Q6_K])
 @pytest.mark.parametrize("rows,cols", SWEEP)
 def test_projection_sweep(provider, type_id, rows, cols):
-    """C2 shapes with BASELINE value distributions; batches 1, 2 and 4.
+    """C2 shapes with BASELINE value distributions; batches 1, 2, 4, 8 and 16.
     Bounds: the reference's forward-error bound against the double dot,
     |a - s| <= 1e-6 (1 + sum|w x|), and the north-star 1e-3 relative."""
     nbytes = rows * F.row_bytes(type_id, cols)
     data = np.empty(nbytes, np.uint8)
     F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, type_id, 2024, rows * 7 + cols)
     rng = np.random.default_rng(rows + cols)
-    xs = rng.standard_normal((4, cols)).astype(np.float32)
+    xs = rng.standard_normal((16, cols)).astype(np.float32)
     s, mag = double_reference(data, type_id, xs, cols, rows)
-    for batch in (1, 2, 4):
+    for batch in (1, 2, 4, 8, 16):
         y = provider.matmul(data, rows, cols, type_id, xs[:batch], batch)
         assert y is not None
         for b in range(batch):

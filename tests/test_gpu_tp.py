@@ -1,7 +1,7 @@
-"""Tensor parallelism over two GPUs: two processes, each holding one shard of
-every layer (half of the heads and FFN rows, half of the vocabulary), run
-the same decode steps; the persistent kernel exchanges the partial
-attention-output and down rows over NVLink. Both ranks must return the same
+"""Tensor parallelism over 2, 4 and 8 GPUs: one process per GPU, each holding
+one shard of every layer (1/N of the heads and FFN rows, 1/N of the
+vocabulary), run the same decode steps; the persistent kernel exchanges the partial
+attention-output and down rows over NVLink. All ranks must return the same
 logits (bitwise: every rank adds the partials in rank order), within 1e-3 of
 the logit scale of the fp16-KV oracle with the same argmax, and the same
 greedy tokens as the oracle over 64 steps.
@@ -17,7 +17,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
+WORLDS = [2, 4, 8]
 PREFILL = 3  # tokens taken by plan_prefill before single steps
 
 
@@ -44,7 +44,7 @@ def _rank_main(rank, world, port, cfg, tokens, greedy_steps, out_dir):
         assert plan is not None, "the shard plan was declined"
         assert plan.tp_info() == (rank, world)
         assert plan.token(tokens[0], 0) == -1  # not connected yet
-        assert plan.tp_connect(F.tp_exchange(plan.tp_handle())) == 0
+        assert F.tp_connect_all(plan)
         # a prefill (steps without logits, then one with) and single steps after it
         logits = []
         assert plan.prefill(tokens[:PREFILL], 0) == 0
@@ -64,25 +64,26 @@ def _rank_main(rank, world, port, cfg, tokens, greedy_steps, out_dir):
         dist.destroy_process_group()
 
 
-def _run(cfg, tokens, greedy_steps, tmp_path):
+def _run(world, cfg, tokens, greedy_steps, tmp_path):
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < WORLD:
-        pytest.skip("needs %d GPUs" % WORLD)
-    mp.spawn(_rank_main, args=(WORLD, _free_port(), cfg, tokens, greedy_steps, str(tmp_path)), nprocs=WORLD,
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    mp.spawn(_rank_main, args=(world, _free_port(), cfg, tokens, greedy_steps, str(tmp_path)), nprocs=world,
              join=True)
-    return [np.load(os.path.join(str(tmp_path), "rank%d.npz" % r)) for r in range(WORLD)]
+    return [np.load(os.path.join(str(tmp_path), "rank%d.npz" % r)) for r in range(world)]
 
 
-def _check(cfg, tokens, greedy_steps, tmp_path):
+def _check(world, cfg, tokens, greedy_steps, tmp_path):
     import fyodor_b200 as F
     import oracle as O
     from tests.test_gpu_plan import logit_error
-    res = _run(cfg, tokens, greedy_steps, tmp_path)
-    for r in range(1, WORLD):
+    res = _run(world, cfg, tokens, greedy_steps, tmp_path)
+    for r in range(1, world):
         assert (res[r]["logits"] == res[0]["logits"]).all()
         assert (res[r]["greedy"] == res[0]["greedy"]).all()
     m = F.SynthModel(**cfg)
+    O.set_threads(os.cpu_count() or 1)
     ref = O.Session(m.ptr, len(tokens) + greedy_steps + 1, m.vocabulary, kv_f16=True)
     for i, t in enumerate(tokens):
         e = ref.forward(t, i)
@@ -96,20 +97,38 @@ def _check(cfg, tokens, greedy_steps, tmp_path):
     for i in range(greedy_steps):
         t = O.argmax(ref.forward(t, len(tokens) + i))
         expected.append(t)
+    O.set_threads(1)
     assert list(res[0]["greedy"]) == expected
     m.close()
 
 
-def test_tp2_small_model(tmp_path):
-    from tests.patterns import SMALL_MODELS
-    name, cfg, tokens = SMALL_MODELS[0]
-    _check(dict(cfg, context=96), tokens, 64, tmp_path)
+# a small model every world size shards: 16/8 heads of 128, FFN 2048, vocabulary 1024
+SMALL_TP = dict(layers=2, embedding=2048, heads=16, kv_heads=8, feed_forward=2048, vocabulary=1024, context=96,
+                seed=21, norm_mode=2, centered=1)
 
 
-def test_tp2_8b_layer_shapes(tmp_path):
-    """Two layers at the 8B geometry, sharded in two (16/4 heads, 7168 FFN rows,
-    64128 vocabulary rows per rank)."""
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_small_model(world, tmp_path):
+    from tests.patterns import bench_tokens
+    _check(world, SMALL_TP, [int(t) for t in bench_tokens(12, 1024)], 64, tmp_path)
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_8b_layer_shapes(world, tmp_path):
+    """Two layers at the 8B geometry, sharded N ways (32/N query and 8/N KV
+    heads, 14336/N FFN rows and 128256/N vocabulary rows per rank)."""
     from tests.patterns import bench_tokens
     cfg = dict(layers=2, embedding=4096, heads=32, kv_heads=8, feed_forward=14336, vocabulary=128256, context=32,
                seed=99, norm_mode=2, centered=1)
-    _check(cfg, [int(t) for t in bench_tokens(5, 128256)], 8, tmp_path)
+    _check(world, cfg, [int(t) for t in bench_tokens(5, 128256)], 8, tmp_path)
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_tp_70b_layer_shapes(world, tmp_path):
+    """Two layers at the 70B geometry (d 8192, 64/8 heads of 128, FFN 28672,
+    vocabulary 128256; Q4_K projections and output head, Q6_K embedding)."""
+    from tests.patterns import bench_tokens
+    import fyodor_b200 as F
+    cfg = dict(layers=2, embedding=8192, heads=64, kv_heads=8, feed_forward=28672, vocabulary=128256, context=32,
+               matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q4_K, seed=70, norm_mode=2, centered=1)
+    _check(world, cfg, [int(t) for t in bench_tokens(5, 128256)], 8, tmp_path)

@@ -96,3 +96,42 @@ def test_engine_cross_check_when_built():
         data = m.tensor_bytes(4)
         x = rng.standard_normal(512).astype(np.float32)
         assert (O.matvec(data, type_id, x, 512, 512) == O.ref_matvec(data, type_id, x, 512, 512)).all()
+
+
+@pytest.mark.parametrize("type_id", [F.Q4_K, F.Q6_K, F.Q8_0, F.F16])
+@pytest.mark.parametrize("threads", [1, 3, 8])
+def test_threaded_matvec_bit_identical(type_id, threads):
+    """The threaded oracle product (rows spread over threads, K-quant rows four
+    at a time) equals the scalar restatement bit for bit: every row keeps the
+    engine's summation order (llm_quant.c:145-312)."""
+    g = load("quant_kernels.npz")
+    data = quant_kernel_weights(type_id, 65, 1024)
+    O.set_threads(threads)
+    try:
+        for p in range(3):
+            x = quant_kernel_inputs(1024, p)
+            assert (O.matvec_threaded(data, type_id, x, 1024, 65) == g["y_%d_%d" % (type_id, p)]).all()
+        rng = np.random.default_rng(threads)
+        m = F.SynthModel(layers=1, embedding=512, heads=4, kv_heads=2, feed_forward=1024, vocabulary=64, context=4,
+                         matrix_type=type_id if type_id in (F.Q4_K, F.Q6_K) else F.Q4_K, seed=threads)
+        w = m.tensor_bytes(10)  # blk.0.ffn_down.weight: 512 rows x 1024 columns
+        x = rng.standard_normal(1024).astype(np.float32)
+        tid = type_id if type_id in (F.Q4_K, F.Q6_K) else F.Q4_K
+        assert (O.matvec_threaded(w, tid, x, 1024, 512) == O.matvec(w, tid, x, 1024, 512)).all()
+    finally:
+        O.set_threads(1)
+
+
+def test_threaded_session_bit_identical():
+    """A session whose products run on several threads gives the same logits
+    as the single-threaded session (and so as the engine)."""
+    name, cfg, tokens = SMALL_MODELS[0]
+    g = load("small_models.npz")
+    m = F.SynthModel(**cfg)
+    O.set_threads(5)
+    try:
+        s = O.Session(m.ptr, len(tokens), m.vocabulary, kv_f16=False)
+        for i, t in enumerate(tokens):
+            assert (s.forward(t, i) == g[name + "_logits"][i]).all(), i
+    finally:
+        O.set_threads(1)

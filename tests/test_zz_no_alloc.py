@@ -53,12 +53,20 @@ def test_static_matches_workspace(shape):
                                       scale, _P(ref), splits, _P(ws), need, None) == 0
     torch.cuda.synchronize()
     e = ref.cpu().numpy()
-    for call in range(2):
-        out = torch.full((nseq, heads, hd), float("nan"), dtype=torch.float32, device="cuda")
+    outs = [torch.full((nseq, heads, hd), float("nan"), dtype=torch.float32, device="cuda") for _ in range(2)]
+    free_after_first = None
+    for call, out in enumerate(outs):
         r = F.lib.fyb_attention_decode_static(_P(q), _P(k), _P(v), stride, _P(dl), nseq, heads, kv_heads, hd,
                                               capacity, scale, _P(out), splits, None)
         assert r == 0, (call, r)
         torch.cuda.synchronize()
+        # the entry point allocates nothing: free device memory does not move
+        # between the first call (which looks up the array) and the next
+        free = torch.cuda.mem_get_info()[0]
+        if free_after_first is None:
+            free_after_first = free
+        else:
+            assert free == free_after_first, (free, free_after_first)
         got = out.cpu().numpy()
         assert np.isfinite(got).all(), call
         err = np.abs(got - e) / (1 + np.abs(e))
@@ -79,3 +87,20 @@ def test_static_rejects_oversize():
     assert r == -3
     torch.cuda.synchronize()
     assert bool((out == 7.0).all())
+
+
+def test_static_rejects_bad_arguments():
+    """Unsupported head dimension or group size, or a null pointer, returns -1
+    before anything is queued (the output keeps its sentinel)."""
+    import torch
+    q, k, v, dl = _inputs([40, 50], 32, 8, 128, 64, seed=9)
+    out = torch.full((2, 32, 128), 5.0, dtype=torch.float32, device="cuda")
+    sc = C.c_float(0.088)
+    call = lambda **kw: F.lib.fyb_attention_decode_static(
+        kw.get("q", _P(q)), _P(k), _P(v), 8 * 64 * 128, _P(dl), 2, kw.get("heads", 32), kw.get("kv", 8),
+        kw.get("hd", 128), 64, sc, _P(out), 4, None)
+    assert call(hd=96) == -1      # head dimension other than 64 or 128
+    assert call(heads=24) == -1   # 3 query heads per KV head
+    assert call(q=None) == -1     # null query
+    torch.cuda.synchronize()
+    assert bool((out == 5.0).all())
