@@ -502,31 +502,26 @@ PHASE_KINDS = ["qkv", "attention", "o", "gateup", "down"]
 
 
 def summarize_trace(tr, layers):
-    """Per phase kind: CTA-median microseconds waiting for the input,
-    preparing it and working, summed over layers (trace of one step)."""
+    """Per phase kind: the CTA-median microseconds from the end of the
+    previous phase to the end of this one (waiting for its input, preparing
+    it, the units and the tile outputs), summed over the layers of one step."""
     t = tr.astype(np.int64) - int(tr[0].min())
-    out = {k: {"wait": 0.0, "prep": 0.0, "work": 0.0} for k in PHASE_KINDS + ["logits"]}
+    out = {k: 0.0 for k in PHASE_KINDS + ["logits"]}
     for l in range(layers):
-        base = 1 + 15 * l
-        # layout per layer: qkv A B C | att A B C | o A B C | gu A B C | down A B C
         for k in range(5):
-            a, b, c = t[base + 3 * k], t[base + 3 * k + 1], t[base + 3 * k + 2]
-            nxt = t[base + 3 * k + 3]  # the next phase's idle point (or logits / exit)
-            out[PHASE_KINDS[k]]["wait"] += float(np.median(b - a)) / 1e3
-            out[PHASE_KINDS[k]]["prep"] += float(np.median(c - b)) / 1e3 if k != 1 else 0.0
-            out[PHASE_KINDS[k]]["work"] += float(np.median(nxt - c if k != 1 else c - b)) / 1e3
-    lb = 1 + 15 * layers
-    out["logits"]["wait"] = float(np.median(t[lb + 1] - t[lb])) / 1e3
-    out["logits"]["prep"] = float(np.median(t[lb + 2] - t[lb + 1])) / 1e3
-    out["logits"]["work"] = float(np.median(t[lb + 3] - t[lb + 2])) / 1e3
-    res = {k: {x: round(v, 1) for x, v in d.items()} for k, d in out.items()}
+            i = 1 + 5 * l + k
+            out[PHASE_KINDS[k]] += float(np.median(t[i] - t[i - 1])) / 1e3
+    lb = 1 + 5 * layers
+    out["logits"] = float(np.median(t[lb] - t[lb - 1])) / 1e3
+    res = {k: round(v, 1) for k, v in out.items()}
+    res["exit"] = round(float(np.median(t[lb + 1] - t[lb])) / 1e3, 1)
     res["step_us"] = round(float(t[-1].max()) / 1e3, 1)
     return res
 
 
 def trace_summary(plan, token, position, layers):
-    """One traced persistent decode step (None when the plan does not use the
-    barrier form of the kernel, whose CTA trace points this summary reads)."""
+    """One traced persistent decode step (None when the plan does not run the
+    persistent kernel)."""
     if plan.decode_form() != 1:
         return None
     tr = plan.trace(token, position)
@@ -536,9 +531,8 @@ def trace_summary(plan, token, position, layers):
 def run_trace_mode(args):
     """Where one persistent decode step spends its time: the 8B model after a
     PROMPT-token prefill, one step traced per CTA (globaltimer), reported per
-    phase kind as the CTA-median time spent waiting for the phase's input,
-    preparing it, and working (GEMV units or attention items), summed over
-    layers, in microseconds."""
+    phase kind as the CTA-median time from the end of the previous phase to
+    the end of this one, summed over layers, in microseconds."""
     import fyodor_b200 as F
     from tests.patterns import bench_tokens
     model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **CFG8B)
@@ -547,16 +541,11 @@ def run_trace_mode(args):
         raise SystemExit("8B plan or prefill failed")
     tr = None
     for i in range(args.trace_step):  # the last traced step is reported (earlier ones warm up)
-        res = plan.trace(17 + i, PROMPT + i, warps=bool(args.trace_raw))
-        if res is None:
+        tr = plan.trace(17 + i, PROMPT + i)
+        if tr is None:
             raise SystemExit("trace failed (persistent kernel not in use?)")
-        tr = res[0] if args.trace_raw else res
     if args.trace_raw:
         np.save(args.trace_raw, tr)
-        np.save(args.trace_raw.replace(".npy", "") + "_warps.npy", res[1])
-    if plan.decode_form() != 1:  # the dataflow form: only the raw per-warp records mean anything
-        print(json.dumps({"decode_form": plan.decode_form(), "grid": int(tr.shape[1])}))
-        return
     res = summarize_trace(tr, model.config.layers)
     step = res.pop("step_us")
     print(json.dumps({"trace_us": res, "step_us": step, "grid": int(tr.shape[1]), "points": int(tr.shape[0])}))

@@ -316,7 +316,7 @@ class Plan:
         return lib.fyb_plan_launches_per_token(C.c_void_p(self.ptr))
 
     def decode_form(self):
-        """0 per-operation kernels, 1 persistent kernel, 2 its dataflow form."""
+        """0 per-operation kernels, 1 the persistent decode kernel."""
         return lib.fyb_plan_decode_form(C.c_void_p(self.ptr))
 
     def tp_info(self):
@@ -341,25 +341,20 @@ class Plan:
         """Decline every later step without launching (another rank failed)."""
         return lib.fyb_plan_tp_disconnect(C.c_void_p(self.ptr))
 
-    def trace(self, token, position, warps=False):
+    def trace(self, token, position):
         """Per-CTA trace points of one persistent decode step: array
-        [points][grid] of globaltimer nanoseconds, or None. With warps=True,
-        a pair (that array, per-warp GEMV records [layers*5 + 1][warps][8])."""
+        [points][grid] of globaltimer nanoseconds (start, then per layer the
+        ends of QKV, attention, O, gate/up and down, the end of the logits,
+        exit), or None."""
         grid = C.c_uint(0)
         L = self.model.config.layers
-        n = (1 + 15 * L + 5) * 1024
+        points = 1 + 5 * L + 2
+        n = points * 1024
         out = np.zeros(n, np.uint64)
-        wn = (L * 5 + 1) * 1024 * 16 * 8
-        wout = np.zeros(wn, np.uint64) if warps else None
-        r = lib.fyb_plan_trace(C.c_void_p(self.ptr), token, position, _ptr(out), n, C.byref(grid),
-                               _ptr(wout) if warps else None, wn if warps else 0)
+        r = lib.fyb_plan_trace(C.c_void_p(self.ptr), token, position, _ptr(out), n, C.byref(grid), None, 0)
         if r < 0:
             return None
-        cta = out[: r * grid.value].reshape(r, grid.value)
-        if not warps:
-            return cta
-        nw = grid.value * 16
-        return cta, wout[: (L * 5 + 1) * nw * 8].reshape(L * 5 + 1, nw, 8)
+        return out[: r * grid.value].reshape(r, grid.value)
 
     def profile(self, token, position, steps):
         """Per-class milliseconds of one decode step: matrix, attention, other."""

@@ -31,8 +31,8 @@ def _nvcc():
 # instantiation of the persistent decode kernel is its own compilation, so
 # they run in parallel.
 VARIANTS = {
-    "decode_inst.cu": [("%d_%d_%d" % (df, hd, g), ["-DFYB_DK_DF=%d" % df, "-DFYB_DK_HD=%d" % hd, "-DFYB_DK_G=%d" % g])
-                       for df in (0, 1) for hd in (128, 64) for g in (1, 2, 4, 8)],
+    "decode_inst.cu": [("%d_%d" % (hd, g), ["-DFYB_DK_HD=%d" % hd, "-DFYB_DK_G=%d" % g])
+                       for hd in (128, 64) for g in (1, 2, 4, 8)],
 }
 
 

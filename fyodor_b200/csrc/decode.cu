@@ -1,21 +1,17 @@
 // decode.cu - host side of the persistent decode kernel: shared-memory
-// sizing, support checks, grid choice and the cooperative launch. The kernels
-// themselves (decode_kernel.cuh, decode_df.cuh) are instantiated once per
-// (form, head dimension, group size) in decode_inst.cu, which the build
-// compiles once per variant so the instantiations compile in parallel.
+// sizing, support checks, grid choice and the cooperative launch. The kernel
+// itself (decode_kernel.cuh) is instantiated once per (head dimension, group
+// size) in decode_inst.cu, which the build compiles once per variant so the
+// instantiations compile in parallel.
 #include "decode_kernel.cuh"
-#include "decode_df.cuh"
 
 namespace fyb {
 
-#define FYB_DK_DECL(DF, HD, G) DecodeKernel decode_entry_##DF##_##HD##_##G();
-FYB_DK_DECL(0, 128, 1) FYB_DK_DECL(0, 128, 2) FYB_DK_DECL(0, 128, 4) FYB_DK_DECL(0, 128, 8)
-FYB_DK_DECL(0, 64, 1) FYB_DK_DECL(0, 64, 2) FYB_DK_DECL(0, 64, 4) FYB_DK_DECL(0, 64, 8)
-FYB_DK_DECL(1, 128, 1) FYB_DK_DECL(1, 128, 2) FYB_DK_DECL(1, 128, 4) FYB_DK_DECL(1, 128, 8)
-FYB_DK_DECL(1, 64, 1) FYB_DK_DECL(1, 64, 2) FYB_DK_DECL(1, 64, 4) FYB_DK_DECL(1, 64, 8)
+#define FYB_DK_DECL(HD, G) DecodeKernel decode_entry_##HD##_##G();
+FYB_DK_DECL(128, 1) FYB_DK_DECL(128, 2) FYB_DK_DECL(128, 4) FYB_DK_DECL(128, 8)
+FYB_DK_DECL(64, 1) FYB_DK_DECL(64, 2) FYB_DK_DECL(64, 4) FYB_DK_DECL(64, 8)
 #undef FYB_DK_DECL
 
-// ------------------------------------------------------------ host side
 constexpr size_t SMEM_LIMIT = 227 * 1024;
 
 // Ring bytes per warp for the rest of the layout taking `other` bytes: what
@@ -32,83 +28,33 @@ static unsigned ring_bytes_left(size_t other, unsigned want)
 
 static unsigned ring_bytes_for(const DecodeGeometry &g, unsigned want = 0)
 {
-    return ring_bytes_left(smem_layout(g.d, g.ffn, g.H, g.Hkv, g.hd, 0).total, want);
+    return ring_bytes_left(smem_layout(g.H, g.Hkv, g.hd, 0).total, want);
 }
 
 static size_t decode_smem_bytes(const DecodeGeometry &g, unsigned want = 0)
 {
-    return smem_layout(g.d, g.ffn, g.H, g.Hkv, g.hd, ring_bytes_for(g, want)).total;
+    return smem_layout(g.H, g.Hkv, g.hd, ring_bytes_for(g, want)).total;
 }
 
 int decode_supported(const DecodeGeometry &g, unsigned type_out)
 {
-    if (!g.nl || !g.Hkv || g.H % g.Hkv) return 0;
+    if (!g.nl || g.nl > 254 || !g.Hkv || g.H % g.Hkv) return 0;
     const unsigned G = g.H / g.Hkv;
     if ((g.hd != 64 && g.hd != 128) || !(G == 1 || G == 2 || G == 4 || G == 8)) return 0;
-    if (g.d % 256 || g.ffn % 256 || (g.H * g.hd) % 256 || g.d > 32768 || g.ffn > 65536) return 0;
+    if (g.d % 256 || g.ffn % 256 || (g.H * g.hd) % 256 || g.d / 256 > NORM_BLOCKS_MAX || g.ffn > 65536) return 0;
     if (type_out != T_Q4_K && type_out != T_Q6_K) return 0;
     return ring_bytes_for(g) != 0 && decode_smem_bytes(g) <= SMEM_LIMIT;
 }
 
-unsigned decode_max_tiles(const DecodeGeometry &g)
-{
-    const unsigned t[4] = {(g.H + 2 * g.Hkv) * g.hd / 16, g.d / 16, g.ffn / 8, (g.V + 15) / 16};
-    return std::max(std::max(t[0], t[1]), std::max(t[2], t[3]));
-}
-
-size_t decode_partials_bytes(const DecodeGeometry &g, int grid)
-{
-    const unsigned long long NW = (unsigned long long)grid * QG_WARPS;
-    const unsigned tiles[5] = {(g.H + 2 * g.Hkv) * g.hd / 16, g.d / 16, g.ffn / 8, g.d / 16, (g.V + 15) / 16};
-    const unsigned ks[5] = {g.d, g.H * g.hd, g.d, g.ffn, g.d};
-    size_t best = 0;
-    for (int i = 0; i < 5; ++i) {
-        const unsigned long long nblk = ks[i] / 256, U = (unsigned long long)tiles[i] * nblk;
-        const unsigned long long slots = (nblk * NW + U - 1) / U + 2;
-        best = std::max<size_t>(best, (size_t)tiles[i] * slots * 16 * sizeof(float));
-    }
-    return best;
-}
-
-static DecodeKernel decode_kernel_for(const DecodeGeometry &g, bool df = false)
+static DecodeKernel decode_kernel_for(const DecodeGeometry &g)
 {
     const unsigned G = g.Hkv ? g.H / g.Hkv : 0;
 #define FYB_DK(HDV, GV) \
-    if (g.hd == HDV && G == GV) return df ? decode_entry_1_##HDV##_##GV() : decode_entry_0_##HDV##_##GV();
+    if (g.hd == HDV && G == GV) return decode_entry_##HDV##_##GV();
     FYB_DK(128, 1) FYB_DK(128, 2) FYB_DK(128, 4) FYB_DK(128, 8)
     FYB_DK(64, 1) FYB_DK(64, 2) FYB_DK(64, 4) FYB_DK(64, 8)
 #undef FYB_DK
     return nullptr;
-}
-
-// Ring bytes per warp of the dataflow form.
-static unsigned df_ring_bytes_for(const DecodeGeometry &g, unsigned want = 0)
-{
-    return ring_bytes_left(df_layout(g.d, g.ffn, g.H, g.Hkv, g.hd, 0).total, want);
-}
-
-static size_t df_smem_bytes(const DecodeGeometry &g, unsigned want = 0)
-{
-    return df_layout(g.d, g.ffn, g.H, g.Hkv, g.hd, df_ring_bytes_for(g, want)).total;
-}
-
-int decode_df_supported(const DecodeGeometry &g, unsigned type_out, int grid)
-{
-    if (grid <= 0 || !decode_supported(g, type_out)) return 0;
-    if (!df_ring_bytes_for(g) || df_smem_bytes(g) > SMEM_LIMIT) return 0;
-    // a CTA's tiles of one phase must fit its shared-tile counters
-    const unsigned tiles[5] = {(g.H + 2 * g.Hkv) * g.hd / 16, g.d / 16, g.ffn / 8, g.d / 16, (g.V + 15) / 16};
-    for (unsigned t : tiles)
-        if ((t + (unsigned)grid - 1) / (unsigned)grid > DF_TILES_PER_CTA) return 0;
-    const DecodeKernel k = decode_kernel_for(g, true);
-    const size_t smem = df_smem_bytes(g);
-    int per_sm = 0;
-    if (!k || cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, QG_THREADS, smem) != cudaSuccess) {
-        cudaGetLastError();
-        return 0;
-    }
-    return per_sm >= 1;
 }
 
 // One CTA per SM when one fits with the geometry's shared memory, else 0.
@@ -129,7 +75,8 @@ int decode_grid(int sms, const DecodeGeometry &g)
 int launch_decode(const DecodeLaunch &L, cudaStream_t s)
 {
     if (!decode_supported(L.g, L.out_head.type) || L.grid <= 0 || !L.layers) return -1;
-    if (L.tp > 1 && (!L.peers || L.g.d > 16u * QG_THREADS)) return -1;  // prep_tp: one slot per thread
+    if (!L.ll.xa || !L.ll.xm || !L.ll.q || !L.ll.kvnew || !L.ll.attn || !L.ll.h || !L.attn_partials) return -1;
+    if (L.tp > 1 && !L.peers) return -1;
     DecodeParams p = {};
     p.layers = L.layers;
     p.nl = L.g.nl; p.d = L.g.d; p.H = L.g.H; p.Hkv = L.g.Hkv; p.hd = L.g.hd; p.ffn = L.g.ffn; p.V = L.g.V;
@@ -139,28 +86,20 @@ int launch_decode(const DecodeLaunch &L, cudaStream_t s)
     p.eps = L.eps; p.attn_scale = L.attn_scale;
     p.rope_cos = L.rope_cos; p.rope_sin = L.rope_sin;
     p.request = L.request;
-    p.xa = L.xa; p.xm = L.xm; p.q = L.q; p.attn = L.attn; p.h = L.h; p.logits = L.logits;
-    p.ss_o = L.ss_o; p.ss_d = L.ss_d;
+    p.ll = L.ll;
+    p.logits = L.logits;
     p.sync = L.sync;
-    p.partials = L.partials;
     p.attn_partials = L.attn_partials; p.attn_splits = L.attn_splits;
     p.argmax_key = L.argmax_key; p.argmax_token = L.argmax_token; p.tokens_log = L.tokens_log;
     p.error = L.error;
     p.logits_mode = L.logits_mode;
     p.ring_bytes = ring_bytes_for(L.g, L.ring_bytes);
-    p.l2_prefetch = L.l2_prefetch;
-    p.ring_pre = L.ring_pre;
     p.kcache = L.kcache; p.vcache = L.vcache;
     p.trace = L.trace; p.trace_slots = L.trace_slots;
-    p.wtrace = L.wtrace;
     p.tp = L.tp; p.tp_rank = L.tp_rank; p.vocab0 = L.vocab0; p.peers = L.peers; p.xl = L.xl;
-    const bool df = L.df.bo != nullptr;
-    if (df && (L.tp > 1 || !L.df.bgu || !L.df.bdn || !L.df.attn_kv)) return -1;
-    p.df = L.df;
-    if (df) p.ring_bytes = df_ring_bytes_for(L.g, L.ring_bytes);
-    if (p.ring_bytes < 2 * Q6_UNIT) return -1;  // every unit size needs two ring slots
-    const size_t smem = df ? df_smem_bytes(L.g, L.ring_bytes) : decode_smem_bytes(L.g, L.ring_bytes);
-    const DecodeKernel decode_kernel = decode_kernel_for(L.g, df);
+    if (p.ring_bytes < 2 * Q6_UNIT || !p.kcache || !p.vcache) return -1;  // every unit size needs two ring slots
+    const size_t smem = decode_smem_bytes(L.g, L.ring_bytes);
+    const DecodeKernel decode_kernel = decode_kernel_for(L.g);
     if (!decode_kernel) return -1;
     if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return -2;

@@ -4,37 +4,42 @@
 //
 // One 512-thread CTA per SM, launched cooperatively so that every CTA is
 // resident and waits between CTAs cannot deadlock. Per layer the CTAs walk
-// the phases QKV(+RoPE, fp16 KV append) -> attention -> O -> gate/up(+SwiGLU)
-// -> down, then logits(+argmax). Each GEMV phase splits its (16-row tile,
-// 256-column block) units over all warps of the grid like the stand-alone
-// GEMV (qgemv.cu); phases meet through counters in global memory instead of
-// kernel boundaries:
-//   qkv_done[l][kv head]  Q/K/V tiles of that KV head's group finished
-//   attn_done[l]          KV heads whose attention output is final
-//   o_done / gu_done / down_done[l]   finished tiles of those phases
-// Counters only grow (modulo 2^32): step e waits for e * (tiles per step),
-// compared wrap-safe, so nothing is reset between steps. The step number is
-// request[3] + 1; the last CTA to leave increments request[3].
-// Producers write their outputs, fence, then add to a counter; the waiting
-// thread reads it with ld.acquire.gpu and the CTA reads produced data through
-// L2 (ld.cg), never through the non-coherent read-only path. Every wait is
-// bounded: on timeout the kernel records ERR_TIMEOUT and raises an abort word
-// at which all CTAs leave (after their in-flight bulk copies land).
+// the phases QKV(+RoPE, fp16 KV append) -> attention -> O(+residual) ->
+// gate/up(+SwiGLU) -> down(+residual), then logits(+argmax).
 //
-// Weights stream through a per-warp ring of shared memory sized in bytes
-// (4 Q4_K or 3 Q6_K units for the 8B shapes). A warp that finishes its units
-// of a phase fills its ring with its first units of the next phase at once,
-// so while the CTA waits for the next phase's input those weights are already
-// on their way; small phases (QKV, O) arrive almost entirely during the wait.
-// Inside a phase a warp only computes: outputs of tiles it owns completely
-// are written as they finish, while fences, counter updates and the stream-K
-// fix-up of tiles shared with neighbouring warps wait until its last unit.
+// Hand-off between phases: every vector a phase produces for another CTA
+// (q, the new K/V rows, the attention output, x after O, h, x after down, and
+// with tensor parallelism the ranks' partial rows) is stored as 8-byte words
+// {value, tag} with tag = (step, layer). A consumer polls the words it needs
+// until every tag matches; an aligned 8-byte store and load are single-copy
+// atomic, so a matching tag means a complete value, and no fence, counter or
+// grid barrier sits between a producer's store and its consumer's load. The
+// dependency chain of the step (every phase needs every tile of the phase
+// before it, through attention or the full-vector products) guarantees that
+// a word is not overwritten by its next layer before all its readers read it.
 //
-// The residual adds and the RMSNorm sums of squares live in the epilogues of
-// the O and down tiles (x_mid = x + o_out, x_next = x_mid + down_out, one
-// double per 16-row tile, summed in a fixed order by the consumers), so the
-// input preparation of a phase is one round of loads, x * scale * weight and
-// the limb split.
+// GEMV phases. CTA c owns whole 16-row tiles [T*c/C, T*(c+1)/C) of the phase;
+// they are processed in chunks of up to CHUNK tiles. Inside a chunk the
+// (tile, 256-column block) units are ordered block-major and split evenly
+// over the 16 warps, so a warp multiplies one or a few input blocks against
+// several tiles: it polls and prepares only those blocks (256 values: the
+// RMSNorm weight product, per-block exponent and four signed 8-bit limbs,
+// the integer-MMA unit math of qgemv_core.cuh) into its private limb slot,
+// with no CTA barrier before its first unit. Each unit's result is added to
+// the warp's partial row slots in shared memory; after one CTA barrier per
+// chunk the rows are summed over the warps in warp order (results do not
+// depend on timing), scaled by the RMSNorm factor 1/sqrt(mean(x^2) + eps)
+// (W (x * s * w) = s * W (x * w); the block sums of squares come from the
+// warps that prepared the blocks), and the tile outputs are stored.
+//
+// Weights stream through a per-warp ring of shared memory (bulk copies with
+// an mbarrier per slot, bounded waits); a warp that finishes its units of a
+// phase fills its ring with its first units of the next phase at once.
+//
+// Every wait is bounded: on timeout the kernel records ERR_TIMEOUT and raises
+// an abort word at which all CTAs leave (after their in-flight bulk copies
+// land); CTA barriers inside a phase are __syncthreads_or over the CTA's
+// abort state, so an abort never leaves part of a CTA at a barrier.
 #pragma once
 #include "qgemv_core.cuh"
 #include "dequant.cuh"
@@ -43,6 +48,12 @@ namespace fyb {
 
 constexpr unsigned WAIT_LIMIT = 1u << 22;  // polls (with a short sleep) before ERR_TIMEOUT
 constexpr unsigned RING_BARS = 8;          // mbarriers (max units in flight) per warp
+constexpr unsigned CHUNK = 8;              // tiles per reduction chunk
+constexpr unsigned LIMB_STRIDE = 256 + QG_XPAD;  // limb-row stride of a one-block slot (64 mod 128)
+constexpr unsigned LIMB_SLOT = 4 * LIMB_STRIDE + 16 + 32 + 16;  // 4 limb rows | exponent | 8 group sums | pad
+constexpr unsigned NORM_BLOCKS_MAX = 64;   // 256-value blocks of a normalized input (d <= 16384)
+
+typedef unsigned long long u64;
 
 struct DecodeParams {
     const DecodeLayer *layers;
@@ -55,10 +66,9 @@ struct DecodeParams {
     float eps, attn_scale;
     const float *rope_cos, *rope_sin;
     unsigned *request;
-    float *xa, *xm, *q, *attn, *h, *logits;
-    double *ss_o, *ss_d;
+    DecodeLL ll;                // tagged vectors
+    float *logits;
     DecodeSync sync;
-    float *partials;
     float *attn_partials;
     unsigned attn_splits;
     unsigned long long *argmax_key;
@@ -66,17 +76,13 @@ struct DecodeParams {
     unsigned *error;
     int logits_mode;
     unsigned ring_bytes;        // per warp, a multiple of 16
-    unsigned ring_pre;          // units a warp requests when it starts a phase's ring early (0: all S)
-    int l2_prefetch;            // L2 prefetch of weights: 0 none, 1 the phase after next, 2 the rest of the next phase
-    unsigned long long *trace;  // optional [stamp][CTA] globaltimer values
+    unsigned long long *trace;  // optional [point][CTA] globaltimer values
     unsigned trace_slots;
-    unsigned long long *wtrace;  // optional [layer][phase kind][warp][WTRACE_POINTS] records
     // tensor parallelism (tp > 1): H, Hkv, ffn and V above are this rank's
     unsigned tp, tp_rank, vocab0;
     unsigned char *const *peers;  // [tp] exchange regions, this rank's at tp_rank
     XchgLayout xl;
-    __half *kcache, *vcache;      // all layers' caches in one allocation each (null: use the layer table)
-    DecodeDfSync df;  // dataflow form only (df.bo null otherwise)
+    __half *kcache, *vcache;      // all layers' caches, layer l at l * Hkv * capacity * hd
 };
 
 enum PhaseKind { PH_QKV = 0, PH_O = 1, PH_GATEUP = 2, PH_DOWN = 3, PH_LOGITS = 4 };
@@ -86,44 +92,33 @@ struct Phase {
     unsigned K, nblk, kind, layer;
 };
 
-// A warp's weight ring. Per phase it holds S = min(RING_BARS, bytes / unit)
-// units; unit k of the phase goes to slot k % S. Bit s of `par` is the
-// parity the next wait on mbarrier s expects. The ring is empty between
-// phases, so each phase may use its own unit size.
-struct Ring {
-    unsigned char *base;
-    uint64_t *bars;
-    unsigned bytes, par, pre;
-    unsigned S, ub, issued, consumed, n;
-    unsigned long long u0;
-    const unsigned char *src;
-};
-
-struct XBuf {
-    signed char *xl;
-    unsigned xstride;
-    int *exps;
-    float *gsums;
-};
-
-FYB_DEV unsigned ld_acquire(const unsigned *p)
+// ------------------------------------------------------------ tagged words
+// Tag of the words written by layer l (l = -1: before the first layer) of
+// step `step`; 0 is never a tag, and a zeroed buffer never matches.
+FYB_DEV unsigned ll_tag(unsigned step, int l) { return (step << 8) | (unsigned)((l + 1) & 0xff); }
+FYB_DEV u64 ll_pack(float v, unsigned tag) { return ((u64)tag << 32) | (u64)__float_as_uint(v); }
+FYB_DEV void ll_put(u64 *dst, float v, unsigned tag)
 {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" :: "l"(dst), "l"(ll_pack(v, tag)) : "memory");
+}
+// a word for another GPU (peer memory over NVLink)
+FYB_DEV void ll_put_sys(u64 *dst, float v, unsigned tag)
+{
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" :: "l"(dst), "l"(ll_pack(v, tag)) : "memory");
+}
+FYB_DEV u64 ll_get(const u64 *src)
+{
+    u64 v;
+    asm volatile("ld.volatile.global.b64 %0, [%1];" : "=l"(v) : "l"(src) : "memory");
     return v;
 }
-
-FYB_DEV unsigned ld_acquire_sys(const unsigned *p)
+FYB_DEV void ll_get2(const u64 *src, u64 &a, u64 &b)
 {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+    asm volatile("ld.volatile.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(src) : "memory");
 }
+FYB_DEV bool ll_ok(u64 w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
+FYB_DEV float ll_val(u64 w) { return __uint_as_float((unsigned)w); }
 
-FYB_DEV bool reached(unsigned value, unsigned target) { return (int)(value - target) >= 0; }
-
-// Exchange counters of rank j (tensor parallelism): o_x[l] at l, d_x[l] at
-// nl + l, argmax keys at 2 nl, the shared abort word at 2 nl + 1.
 FYB_DEV unsigned *xctr(const DecodeParams &p, unsigned j)
 {
     return reinterpret_cast<unsigned *>(p.peers[j] + p.xl.ctr);
@@ -141,6 +136,57 @@ FYB_DEV bool aborted(const DecodeParams &p) { return *(volatile unsigned *)p.syn
 // The same answer for every lane of the warp (ring counters must not diverge).
 FYB_DEV bool warp_aborted(const DecodeParams &p) { return __shfl_sync(0xffffffffu, aborted(p) ? 1 : 0, 0) != 0; }
 
+FYB_DEV unsigned ld_acquire_sys(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+FYB_DEV bool reached(unsigned value, unsigned target) { return (int)(value - target) >= 0; }
+
+// One word, by one thread, until its tag matches (bounded). False on abort.
+FYB_DEV bool ll_wait1(const DecodeParams &p, const u64 *src, unsigned tag, float &v)
+{
+    u64 w = ll_get(src);
+    for (unsigned i = 0; !ll_ok(w, tag); ++i) {
+        if (i >= WAIT_LIMIT) { raise_abort(p, ERR_TIMEOUT); return false; }
+        if (aborted(p)) return false;
+        __nanosleep(20);
+        w = ll_get(src);
+    }
+    v = ll_val(w);
+    return true;
+}
+
+// Eight consecutive words per lane (src is this lane's first word, 16-byte
+// aligned), warp-uniform: returns when every lane's words carry `tag`; false
+// for the whole warp on abort or timeout.
+FYB_DEV bool ll_wait8(const DecodeParams &p, const u64 *src, unsigned tag, float (&v)[8])
+{
+    u64 r[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ll_get2(src + 2 * i, r[2 * i], r[2 * i + 1]);
+    for (unsigned it = 0;; ++it) {
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ok = ok && ll_ok(r[i], tag);
+        if (__all_sync(0xffffffffu, ok)) break;
+        if (it >= WAIT_LIMIT) {
+            if ((threadIdx.x & 31) == 0) raise_abort(p, ERR_TIMEOUT);
+            return false;
+        }
+        if (warp_aborted(p)) return false;
+        __nanosleep(20);
+        if (!ok) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) ll_get2(src + 2 * i, r[2 * i], r[2 * i + 1]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = ll_val(r[i]);
+    return true;
+}
+
 FYB_DEV unsigned long long globaltimer()
 {
     unsigned long long t;
@@ -150,450 +196,9 @@ FYB_DEV unsigned long long globaltimer()
 
 // Profiling: thread 0 records the time of trace point `ts` (every CTA passes
 // the same trace points in the same order).
-FYB_DEV void stamp(const DecodeParams &p, unsigned &ts)
+FYB_DEV void stamp(const DecodeParams &p, unsigned ts)
 {
-    if (p.trace && threadIdx.x == 0 && ts < p.trace_slots)
-        p.trace[(size_t)ts * gridDim.x + blockIdx.x] = globaltimer();
-    ++ts;
-}
-
-// Whole-CTA wait until *ctr reached target (ctr null: only the abort check).
-// Thread 0 polls; false (for every thread) on abort or timeout. Trace points:
-// the CTA is idle (all its warps arrived), the wait is over.
-FYB_DEV bool cta_wait(const DecodeParams &p, const unsigned *ctr, unsigned target, unsigned *flag, unsigned &ts,
-    bool sys = false)
-{
-    __syncthreads();
-    stamp(p, ts);
-    if (threadIdx.x == 0) {
-        unsigned ok = 0;
-        for (unsigned i = 0;; ++i) {
-            if (aborted(p)) break;
-            if (!ctr || reached(sys ? ld_acquire_sys(ctr) : ld_acquire(ctr), target)) { ok = 1; break; }
-            if (i >= WAIT_LIMIT) { raise_abort(p, ERR_TIMEOUT); break; }
-#ifndef FYB_POLL_NS
-#define FYB_POLL_NS 32
-#endif
-            if (FYB_POLL_NS) __nanosleep(FYB_POLL_NS);
-        }
-        *flag = ok;
-    }
-    stamp(p, ts);
-    __syncthreads();
-    return *flag != 0;
-}
-
-// ------------------------------------------------------------ weight ring
-// CTA c owns tiles [T*c/C, T*(c+1)/C) of the phase (whole tiles, balanced to
-// one tile); its warps split that range of units evenly.
-FYB_DEV void cta_tiles(const Phase &ph, unsigned &tb, unsigned &te)
-{
-    const unsigned long long T = ph.w.tiles, C = gridDim.x;
-    tb = (unsigned)(T * blockIdx.x / C);
-    te = (unsigned)(T * (blockIdx.x + 1) / C);
-}
-
-FYB_DEV void warp_range(const Phase &ph, unsigned long long &u0, unsigned &n)
-{
-    unsigned tb, te;
-    cta_tiles(ph, tb, te);
-    const unsigned Uc = (te - tb) * ph.nblk, w = threadIdx.x >> 5;
-    const unsigned a = Uc * w / QG_WARPS, b = Uc * (w + 1) / QG_WARPS;
-    u0 = (unsigned long long)tb * ph.nblk + a;
-    n = b - a;
-}
-
-FYB_DEV void ring_issue(Ring &r, unsigned lane)
-{
-    const unsigned slot = r.issued % r.S;
-    if (lane == 0) {
-        fence_proxy_async();
-        mbar_expect_tx(r.bars + slot, r.ub);
-        bulk_copy_g2s(r.base + slot * r.ub, r.src + (r.u0 + r.issued) * r.ub, r.ub, r.bars + slot);
-    }
-    ++r.issued;
-}
-
-// Start a phase on an empty ring: this warp's range, and its first units.
-// L2 prefetch (one bulk prefetch per warp) mode 2: the warp's units of this
-// phase beyond the ring's first S, so HBM streams the whole phase into L2
-// while the CTAs still wait for its input; mode 1 (with `next`): the warp's
-// units of the phase after this one.
-FYB_DEV void ring_begin(const Phase &ph, Ring &r, unsigned lane, const Phase *next, int l2_prefetch)
-{
-    warp_range(ph, r.u0, r.n);
-    r.ub = unit_bytes(ph.w.type);
-    r.S = min(RING_BARS, r.bytes / r.ub);
-    r.src = ph.w.units;
-    r.issued = r.consumed = 0;
-    const unsigned pre = r.pre ? min(r.pre, r.S) : r.S;
-    while (r.issued < r.n && r.issued < pre) ring_issue(r, lane);
-    if (l2_prefetch == 2 && r.n > r.S && lane == 0)
-        bulk_prefetch_l2(r.src + (r.u0 + r.S) * r.ub, (r.n - r.S) * r.ub);
-    if (next && l2_prefetch == 1 && lane == 0) {
-        unsigned long long v0;
-        unsigned nn;
-        warp_range(*next, v0, nn);
-        const unsigned ubn = unit_bytes(next->w.type);
-        if (nn) bulk_prefetch_l2(next->w.units + v0 * ubn, nn * ubn);
-    }
-}
-
-// Wait for the next unit; its shared-memory address, or null on timeout.
-FYB_DEV const unsigned char *ring_wait(Ring &r)
-{
-    const unsigned slot = r.consumed % r.S;
-    const bool landed = mbar_wait_bounded(r.bars + slot, (r.par >> slot) & 1u);
-    if (!__all_sync(0xffffffffu, landed)) return nullptr;
-    r.par ^= 1u << slot;
-    ++r.consumed;
-    return r.base + slot * r.ub;
-}
-
-// Before leaving early: let the copies still in flight land (bounded).
-FYB_DEV void ring_drain(Ring &r)
-{
-    while (r.consumed != r.issued)
-        if (!ring_wait(r)) break;
-}
-
-// ------------------------------------------------------------ input preparation
-// x = the embedding row of the request's token (layer 0) or a buffer written
-// earlier in this step, RMS-normalized when norm_w is set (scale from the
-// per-tile sums `ss`, or a block reduction for the embedding row), split into
-// limbs in shared memory. All loads of a pass are issued before any result
-// is used, so a pass costs one round trip to L2.
-FYB_DEV void prep_input(const DecodeParams &p, bool embed, const float *buf, const double *ss, unsigned ss_n,
-    const float *norm_w, unsigned K, const XBuf &xb, double *red, float *scale_smem)
-{
-    const unsigned tid = threadIdx.x, nslot = K / 16, nblk = K / 256;
-    const unsigned char *erow = nullptr;
-    if (embed) erow = p.embd + (unsigned long long)__ldcg(p.request) * p.embd_row_bytes;
-    auto load = [&](unsigned sl, float (&x)[16]) {
-        if (embed) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) x[j] = dequant_any(erow, 16ull * sl + j, p.embd_type);
-        } else {
-            load16(buf + 16 * sl, x);
-        }
-    };
-    if (norm_w && nslot <= QG_THREADS) {
-        // one pass: x and the norm weight stay in registers while the scale forms
-        const bool ok = tid < nslot;
-        const unsigned sl = ok ? tid : 0;
-        float x[16], w[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) { x[j] = 0.f; w[j] = 0.f; }
-        if (ok) { load(sl, x); load16(norm_w + 16 * sl, w); }
-        double total = 0.0;
-        if (embed) {
-            if (ok) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) total += (double)x[j] * (double)x[j];
-            }
-            total = block_sum_double(total, red);
-            if (tid == 0) *scale_smem = (float)(1.0 / sqrt(total / (double)K + (double)p.eps));
-        } else if (tid < 32) {
-#pragma unroll 8
-            for (unsigned i = tid; i < ss_n; i += 32) total += __ldcg(ss + i);
-#pragma unroll
-            for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-            if (tid == 0) *scale_smem = (float)(1.0 / sqrt(total / (double)K + (double)p.eps));
-        }
-        __syncthreads();
-        const float scale = *scale_smem;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) x[j] = __fmul_rn(__fmul_rn(x[j], scale), w[j]);
-        prep_slot(x, ok, 0, sl, K, nblk, xb.xl, xb.xstride, xb.exps, xb.gsums, p.error);
-        __syncthreads();
-        return;
-    }
-    float scale = 1.f;
-    if (norm_w) {  // larger vectors: the scale first, then the passes
-        double total = 0.0;
-        if (embed) {
-            for (unsigned s = tid; s < nslot; s += QG_THREADS) {
-                float x[16];
-                load(s, x);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) total += (double)x[j] * (double)x[j];
-            }
-            total = block_sum_double(total, red);
-            if (tid == 0) *scale_smem = (float)(1.0 / sqrt(total / (double)K + (double)p.eps));
-        } else if (tid < 32) {
-#pragma unroll 8
-            for (unsigned i = tid; i < ss_n; i += 32) total += __ldcg(ss + i);
-#pragma unroll
-            for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-            if (tid == 0) *scale_smem = (float)(1.0 / sqrt(total / (double)K + (double)p.eps));
-        }
-        __syncthreads();
-        scale = *scale_smem;
-    }
-    // two passes per round of loads
-    for (unsigned s0 = 0; s0 < nslot; s0 += 2 * QG_THREADS) {
-        const unsigned sa = s0 + tid, sb = s0 + QG_THREADS + tid;
-        const bool oka = sa < nslot, okb = sb < nslot;
-        float xa[16], xb2[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) { xa[j] = 0.f; xb2[j] = 0.f; }
-        if (oka) load(sa, xa);
-        if (okb) load(sb, xb2);
-        if (norm_w) {
-            float w[16];
-            if (oka) {
-                load16(norm_w + 16 * sa, w);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) xa[j] = __fmul_rn(__fmul_rn(xa[j], scale), w[j]);
-            }
-            if (okb) {
-                load16(norm_w + 16 * sb, w);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) xb2[j] = __fmul_rn(__fmul_rn(xb2[j], scale), w[j]);
-            }
-        }
-        prep_slot(xa, oka, 0, oka ? sa : 0, K, nblk, xb.xl, xb.xstride, xb.exps, xb.gsums, p.error);
-        if (s0 + QG_THREADS < nslot)  // uniform: whether a second pass exists
-            prep_slot(xb2, okb, 0, okb ? sb : 0, K, nblk, xb.xl, xb.xstride, xb.exps, xb.gsums, p.error);
-    }
-    __syncthreads();
-}
-
-// Tensor-parallel input of QKV, gate/up and the logits: x = base + the ranks'
-// partial rows in rank order (so every rank computes the same x), or the
-// embedding row; x is written back in shares (slot s by CTA s % grid) when
-// `share` is set, its sum of squares reduced over the CTA, and x * scale * w
-// split into limbs. One slot per thread (d <= 16 * threads).
-FYB_DEV void prep_tp(const DecodeParams &p, bool embed, const float *base, const float *parts, float *share,
-    const float *norm_w, const XBuf &xb, double *red)
-{
-    const unsigned tid = threadIdx.x, K = p.d, nslot = K / 16, nblk = K / 256;
-    const bool ok = tid < nslot;
-    const unsigned sl = ok ? tid : 0;
-    float x[16], w[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) { x[j] = 0.f; w[j] = 0.f; }
-    if (ok) {
-        load16(norm_w + 16 * sl, w);
-        if (embed) {
-            const unsigned char *erow = p.embd + (unsigned long long)__ldcg(p.request) * p.embd_row_bytes;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) x[j] = dequant_any(erow, 16ull * sl + j, p.embd_type);
-        } else {
-            load16(base + 16 * sl, x);
-#pragma unroll 8
-            for (unsigned r = 0; r < 8; ++r) {
-                if (r < p.tp) {
-                    float y[16];
-                    load16(parts + (size_t)r * K + 16 * sl, y);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) x[j] = __fadd_rn(x[j], y[j]);
-                }
-            }
-        }
-        if (share && sl % gridDim.x == blockIdx.x) {
-            float4 *o4 = reinterpret_cast<float4 *>(share + 16 * sl);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) o4[i] = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
-        }
-    }
-    double ss = 0.0;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) ss += (double)x[j] * (double)x[j];
-    ss = block_sum_double(ss, red);
-    const float scale = (float)(1.0 / sqrt(ss / (double)K + (double)p.eps));
-#pragma unroll
-    for (int j = 0; j < 16; ++j) x[j] = __fmul_rn(__fmul_rn(x[j], scale), w[j]);
-    prep_slot(x, ok, 0, sl, K, nblk, xb.xl, xb.xstride, xb.exps, xb.gsums, p.error);
-    __syncthreads();
-}
-
-// ------------------------------------------------------------ tile outputs
-FYB_DEV float residual_in(const DecodeParams &p, unsigned layer, unsigned r)
-{
-    if (layer == 0)
-        return dequant_any(p.embd + (unsigned long long)__ldcg(p.request) * p.embd_row_bytes, r, p.embd_type);
-    return __ldcg(p.xa + r);
-}
-
-FYB_DEV unsigned qkv_kvh(const DecodeParams &p, unsigned tile)
-{
-    const unsigned tq = p.H * p.hd / 16, tk = p.Hkv * p.hd / 16;
-    if (tile < tq) return (tile * 16 / p.hd) / (p.H / p.Hkv);
-    return ((tile < tq + tk ? tile - tq : tile - tq - tk) * 16) / p.hd;
-}
-
-// Layer l's K (or V) cache: one allocation for all layers when the plan gives
-// its base (no pointer chase through the layer table), else the table.
-FYB_DEV __half *kv_layer(const DecodeParams &p, unsigned l, bool v)
-{
-    if (p.kcache) return (v ? p.vcache : p.kcache) + (size_t)l * p.Hkv * p.capacity * p.hd;
-    return v ? p.layers[l].vcache : p.layers[l].kcache;
-}
-
-// Inputs the output tiles of a warp need besides the GEMV result (for the
-// first two tiles it touches): RoPE factors (QKV) or residual rows (O, down).
-struct TileIn {
-    float a0, a1, b0, b1;
-};
-
-// RoPE factors of the QKV tiles (constant tables: loaded at phase start).
-FYB_DEV void fetch_rope(const DecodeParams &p, const Phase &ph, unsigned ta, unsigned tz, unsigned lane,
-    TileIn &in)
-{
-    const unsigned gid = lane >> 2;
-    const unsigned tq = p.H * p.hd / 16, tk = p.Hkv * p.hd / 16, hd = p.hd;
-    in.a0 = in.a1 = in.b0 = in.b1 = 0.f;
-    if (ph.kind != PH_QKV || (lane & 3)) return;
-    const unsigned pos = __ldcg(p.request + 1);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const unsigned t = ta + k;
-        if (t >= tz || t >= tq + tk) continue;
-        const unsigned lt = t < tq ? t : t - tq, pair = ((lt * 16 + 2 * gid) % hd) >> 1;
-        const float c = p.rope_cos[(size_t)pos * (hd >> 1) + pair], s = p.rope_sin[(size_t)pos * (hd >> 1) + pair];
-        if (k == 0) { in.a0 = c; in.b0 = s; } else { in.a1 = c; in.b1 = s; }
-    }
-}
-
-// Residual rows of the O (layers after the first) and down tiles. The
-// barrier form loads them at phase start (their writers finished phases
-// ago); the dataflow form once the warp's first input block is ready, which
-// orders them after their writers.
-FYB_DEV void fetch_resid(const DecodeParams &p, const Phase &ph, unsigned ta, unsigned tz, unsigned lane,
-    TileIn &in)
-{
-    const unsigned gid = lane >> 2;
-    if (lane & 3) return;
-    const float *src = ph.kind == PH_O ? p.xa : p.xm;
-    if (ta < tz) { in.a0 = __ldcg(src + ta * 16 + gid); in.b0 = __ldcg(src + ta * 16 + gid + 8); }
-    if (ta + 1 < tz) { in.a1 = __ldcg(src + (ta + 1) * 16 + gid); in.b1 = __ldcg(src + (ta + 1) * 16 + gid + 8); }
-}
-
-// Output of one complete tile (no fences, no counters). Lanes with tig == 0
-// hold yA (MMA row gid) and yB (row gid + 8). LOGITS folds the tile's rows
-// into the warp's running argmax key. `in` holds the RoPE factors or
-// residual rows of tiles ta and ta + 1 (other tiles load them here).
-FYB_DEV void tile_output(const DecodeParams &p, const Phase &ph, unsigned tile, float yA, float yB, unsigned lane,
-    unsigned long long &key, const TileIn &in, unsigned ta)
-{
-    const int k = tile == ta ? 0 : tile == ta + 1 ? 1 : -1;
-    const unsigned gid = lane >> 2;
-    const bool mine = (lane & 3) == 0;
-    const unsigned l = ph.layer;
-    if (ph.kind == PH_QKV) {
-        // rows 2*gid and 2*gid+1 of the tile form one RoPE pair (llm_cpu.c:298-327)
-        const unsigned tq = p.H * p.hd / 16, tk = p.Hkv * p.hd / 16, hd = p.hd;
-        const unsigned seg = tile < tq ? 0 : tile < tq + tk ? 1 : 2;
-        const unsigned lt = tile - (seg == 0 ? 0 : seg == 1 ? tq : tq + tk);
-        const unsigned rowA = lt * 16 + 2 * gid;
-        if (mine) {
-            const unsigned pos = __ldcg(p.request + 1), pair = (rowA % hd) >> 1;
-            float a = yA, b = yB;
-            if (seg <= 1) {
-                const float c = k == 0 ? in.a0 : k == 1 ? in.a1 : p.rope_cos[(size_t)pos * (hd >> 1) + pair];
-                const float s = k == 0 ? in.b0 : k == 1 ? in.b1 : p.rope_sin[(size_t)pos * (hd >> 1) + pair];
-                a = __fsub_rn(__fmul_rn(yA, c), __fmul_rn(yB, s));
-                b = __fadd_rn(__fmul_rn(yA, s), __fmul_rn(yB, c));
-            }
-            if (seg == 0) {
-                *reinterpret_cast<float2 *>(p.q + rowA) = make_float2(a, b);
-            } else {
-                const unsigned kvh = rowA / hd, dd = rowA % hd;
-                __half *cache = kv_layer(p, l, seg == 2);
-                *reinterpret_cast<__half2 *>(cache + ((size_t)kvh * p.capacity + pos) * hd + dd) =
-                    __halves2half2(__float2half_rn(a), __float2half_rn(b));
-            }
-        }
-        return;
-    }
-    if ((ph.kind == PH_O || ph.kind == PH_DOWN) && p.tp > 1) {
-        // this rank's partial rows go to every rank's exchange region; the
-        // residual add and the sum of squares follow the exchange
-        if (mine) {
-            const size_t off = (ph.kind == PH_O ? p.xl.xo : p.xl.xd) + ((size_t)p.tp_rank * p.d + tile * 16 + gid) * 4;
-            for (unsigned j = 0; j < p.tp; ++j) {
-                float *dst = reinterpret_cast<float *>(p.peers[j] + off);
-                dst[0] = yA;
-                dst[8] = yB;
-            }
-        }
-        return;
-    }
-    if (ph.kind == PH_O || ph.kind == PH_DOWN) {
-        const unsigned rA = tile * 16 + gid, rB = rA + 8;
-        double sq = 0.0;
-        if (mine) {
-            float xA, xB;
-            const bool pre = k >= 0 && !(ph.kind == PH_O && l == 0);  // prefetched residual rows
-            if (ph.kind == PH_O) {
-                xA = __fadd_rn(pre ? (k ? in.a1 : in.a0) : residual_in(p, l, rA), yA);
-                xB = __fadd_rn(pre ? (k ? in.b1 : in.b0) : residual_in(p, l, rB), yB);
-                p.xm[rA] = xA; p.xm[rB] = xB;
-            } else {
-                xA = __fadd_rn(pre ? (k ? in.a1 : in.a0) : __ldcg(p.xm + rA), yA);
-                xB = __fadd_rn(pre ? (k ? in.b1 : in.b0) : __ldcg(p.xm + rB), yB);
-                p.xa[rA] = xA; p.xa[rB] = xB;
-            }
-            sq = (double)xA * (double)xA + (double)xB * (double)xB;
-        }
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        if (lane == 0) (ph.kind == PH_O ? p.ss_o : p.ss_d)[tile] = sq;
-        return;
-    }
-    if (ph.kind == PH_GATEUP) {
-        if (mine) {  // llm_cpu.c:336-342: gate / (1 + expf(-gate)) * up
-            const float g = __fdiv_rn(yA, __fadd_rn(1.0f, expf(-yA)));
-            p.h[tile * 8 + gid] = __fmul_rn(g, yB);
-        }
-        return;
-    }
-    // PH_LOGITS: store; argmax key = (order key, ~index) so ties go to the
-    // lowest index (llm_cpu.c:896-905)
-    const unsigned rA = tile * 16 + gid, rB = rA + 8;  // this rank's rows; p.vocab0 + row is the token
-    unsigned long long kk = 0ull;
-    if (mine) {
-        const bool okA = rA < p.V, okB = rB < p.V;
-        if (p.tp == 1) {
-            if (okA) p.logits[rA] = yA;
-            if (okB) p.logits[rB] = yB;
-        } else if (p.logits_mode == 1) {  // every rank gathers the whole vocabulary
-            for (unsigned j = 0; j < p.tp; ++j) {
-                float *lg = reinterpret_cast<float *>(p.peers[j] + p.xl.logits) + p.vocab0;
-                if (okA) lg[rA] = yA;
-                if (okB) lg[rB] = yB;
-            }
-        }
-        if (((okA && !isfinite(yA)) || (okB && !isfinite(yB))) && p.error) atomicCAS(p.error, 0u, ERR_NONFINITE);
-        const unsigned gA = p.vocab0 + rA, gB = p.vocab0 + rB;
-        const unsigned long long kA = okA ? ((unsigned long long)float_order_key(yA) << 32) | (0xffffffffu - gA) : 0ull;
-        const unsigned long long kB = okB ? ((unsigned long long)float_order_key(yB) << 32) | (0xffffffffu - gB) : 0ull;
-        kk = kA > kB ? kA : kB;
-    }
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long other = __shfl_xor_sync(0xffffffffu, kk, o);
-        kk = other > kk ? other : kk;
-    }
-    key = kk > key ? kk : key;
-}
-
-// Counter updates for `count` complete tiles starting at `first` (lane 0,
-// after the fence that orders their outputs).
-FYB_DEV void signal_tiles(const DecodeParams &p, const Phase &ph, unsigned first, unsigned count)
-{
-    if (!count) return;
-    const unsigned l = ph.layer;
-    if (ph.kind == PH_QKV) {
-        for (unsigned t = first; t < first + count; ++t) atomicAdd(p.sync.qkv_done + l * p.Hkv + qkv_kvh(p, t), 1u);
-    } else if (ph.kind == PH_O) {
-        atomicAdd(p.sync.o_done + l, count);
-    } else if (ph.kind == PH_GATEUP) {
-        atomicAdd(p.sync.gu_done + l, count);
-    } else if (ph.kind == PH_DOWN) {
-        atomicAdd(p.sync.down_done + l, count);
-    }
+    if (p.trace && threadIdx.x == 0 && ts < p.trace_slots) p.trace[(size_t)ts * gridDim.x + blockIdx.x] = globaltimer();
 }
 
 // ------------------------------------------------------------ phases
@@ -626,186 +231,482 @@ FYB_DEV bool phase_after(const DecodeParams &p, unsigned kind, unsigned l, Phase
     return false;
 }
 
-// cur <- the GEMV phase after cur (unchanged at the end of the step)
-FYB_DEV void advance(const DecodeParams &p, Phase &cur)
+FYB_DEV void cta_tiles(const Phase &ph, unsigned &tb, unsigned &te)
 {
-    Phase nx;
-    if (phase_after(p, cur.kind, cur.layer, nx)) cur = nx;
+    const unsigned long long T = ph.w.tiles, C = gridDim.x;
+    tb = (unsigned)(T * blockIdx.x / C);
+    te = (unsigned)(T * (blockIdx.x + 1) / C);
 }
 
-// Start the ring on the phase after `ph` (and prefetch the one after that into L2).
+// A warp's units of one phase: chunk by chunk, and inside chunk c (Tc tiles)
+// the units u = b * Tc + t in [Uc * w / W, Uc * (w + 1) / W), Uc = nblk * Tc.
+struct Walk {
+    unsigned T, nblk, c, k, e, Tc;
+};
+
+FYB_DEV void walk_chunk(Walk &wk, unsigned warp)
+{
+    wk.Tc = min(CHUNK, wk.T - wk.c * CHUNK);
+    const unsigned Uc = wk.Tc * wk.nblk;
+    wk.k = Uc * warp / QG_WARPS;
+    wk.e = Uc * (warp + 1) / QG_WARPS;
+}
+
+FYB_DEV void walk_begin(Walk &wk, unsigned T, unsigned nblk, unsigned warp)
+{
+    wk.T = T; wk.nblk = nblk; wk.c = 0;
+    wk.k = wk.e = wk.Tc = 0;
+    if (T) walk_chunk(wk, warp);
+}
+
+// Next unit (t: tile index within the CTA's range, b: block); false at the end.
+FYB_DEV bool walk_next(Walk &wk, unsigned warp, unsigned &t, unsigned &b)
+{
+    while (wk.k == wk.e) {
+        if ((wk.c + 1) * CHUNK >= wk.T) return false;
+        ++wk.c;
+        walk_chunk(wk, warp);
+    }
+    b = wk.k / wk.Tc;
+    t = wk.c * CHUNK + (wk.k - b * wk.Tc);
+    ++wk.k;
+    return true;
+}
+
+FYB_DEV unsigned walk_count(unsigned T, unsigned nblk, unsigned warp)
+{
+    unsigned n = 0;
+    for (unsigned c = 0; c * CHUNK < T; ++c) {
+        const unsigned Uc = min(CHUNK, T - c * CHUNK) * nblk;
+        n += Uc * (warp + 1) / QG_WARPS - Uc * warp / QG_WARPS;
+    }
+    return n;
+}
+
+// ------------------------------------------------------------ weight ring
+// A warp's weight ring. Per phase it holds S = min(RING_BARS, bytes / unit)
+// units; unit k of the phase goes to slot k % S. Bit s of `par` is the
+// parity the next wait on mbarrier s expects. The ring is empty between
+// phases, so each phase may use its own unit size.
+struct Ring {
+    unsigned char *base;
+    uint64_t *bars;
+    unsigned bytes, par;
+    unsigned S, ub, issued, consumed, n, tb;
+    const unsigned char *src;
+    unsigned nblk;
+    Walk iw;  // issue cursor
+};
+
+FYB_DEV void ring_issue(Ring &r, unsigned lane)
+{
+    unsigned t = 0, b = 0;
+    walk_next(r.iw, threadIdx.x >> 5, t, b);
+    const unsigned slot = r.issued % r.S;
+    if (lane == 0) {
+        fence_proxy_async();
+        mbar_expect_tx(r.bars + slot, r.ub);
+        bulk_copy_g2s(r.base + slot * r.ub, r.src + ((unsigned long long)(r.tb + t) * r.nblk + b) * r.ub, r.ub,
+                      r.bars + slot);
+    }
+    ++r.issued;
+}
+
+// Start a phase on an empty ring: this warp's units and its first S copies.
+FYB_DEV void ring_begin(const Phase &ph, Ring &r, unsigned lane)
+{
+    unsigned te;
+    cta_tiles(ph, r.tb, te);
+    const unsigned warp = threadIdx.x >> 5;
+    r.nblk = ph.nblk;
+    r.n = walk_count(te - r.tb, ph.nblk, warp);
+    walk_begin(r.iw, te - r.tb, ph.nblk, warp);
+    r.ub = unit_bytes(ph.w.type);
+    r.S = min(RING_BARS, r.bytes / r.ub);
+    r.src = ph.w.units;
+    r.issued = r.consumed = 0;
+    while (r.issued < r.n && r.issued < r.S) ring_issue(r, lane);
+}
+
+// Wait for the next unit; its shared-memory address, or null on timeout.
+FYB_DEV const unsigned char *ring_wait(Ring &r)
+{
+    const unsigned slot = r.consumed % r.S;
+    const bool landed = mbar_wait_bounded(r.bars + slot, (r.par >> slot) & 1u);
+    if (!__all_sync(0xffffffffu, landed)) return nullptr;
+    r.par ^= 1u << slot;
+    ++r.consumed;
+    return r.base + slot * r.ub;
+}
+
+// Before leaving early: let the copies still in flight land (bounded).
+FYB_DEV void ring_drain(Ring &r)
+{
+    while (r.consumed != r.issued)
+        if (!ring_wait(r)) break;
+}
+
 FYB_DEV void ring_next(const DecodeParams &p, const Phase &ph, Ring &r, unsigned lane)
 {
-    Phase nx, nx2;
-    if (!phase_after(p, ph.kind, ph.layer, nx)) return;
-    const bool has2 = phase_after(p, nx.kind, nx.layer, nx2);
-    ring_begin(nx, r, lane, has2 ? &nx2 : nullptr, p.l2_prefetch);
+    Phase nx;
+    if (phase_after(p, ph.kind, ph.layer, nx)) ring_begin(nx, r, lane);
+}
+
+// ------------------------------------------------------------ shared memory of a CTA
+struct LimbSlot {           // one prepared 256-value block (a warp's private slot)
+    signed char *xl;        // 4 limb rows, stride LIMB_STRIDE
+    int *exps;              // the block exponent
+    float *gsums;           // 8 group sums of 32 values
+};
+
+struct Cta {
+    float *parts;           // [2][CHUNK][warps][16] partial rows of a chunk's tiles
+    double *bss;            // [2][NORM_BLOCKS_MAX] block sums of squares of a phase's input
+    unsigned long long *keys;  // [warps] logits argmax keys
+    unsigned *flag;
+};
+
+FYB_DEV LimbSlot limb_slot(unsigned char *base, unsigned warp)
+{
+    LimbSlot s;
+    unsigned char *b = base + (size_t)warp * LIMB_SLOT;
+    s.xl = reinterpret_cast<signed char *>(b);
+    s.exps = reinterpret_cast<int *>(b + 4 * LIMB_STRIDE);
+    s.gsums = reinterpret_cast<float *>(b + 4 * LIMB_STRIDE + 16);
+    return s;
+}
+
+// ------------------------------------------------------------ input preparation
+// Lane i holds values 8i..8i+7 of a 256-value block (x * w already): the
+// block exponent, four signed limbs per value (the same split as prep_slot in
+// qgemv_core.cuh, stored in its lane-major layout) and the eight 32-value
+// group sums.
+FYB_DEV void split_block(float (&x)[8], unsigned lane, const LimbSlot &s, unsigned *error)
+{
+    float gs = 0.f, mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { gs = __fadd_rn(gs, x[j]); mx = fmaxf(mx, fabsf(x[j])); }
+    gs = __fadd_rn(gs, __shfl_xor_sync(0xffffffffu, gs, 1));
+    gs = __fadd_rn(gs, __shfl_xor_sync(0xffffffffu, gs, 2));
+    if ((lane & 3) == 0) s.gsums[lane >> 2] = gs;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    int E = 0;
+    const bool bad = !(mx <= 3.0e38f);  // inf or NaN in the block
+    if (!bad && mx > 0.f) {
+        frexpf(mx, &E);
+        if (E < -120) E = -120;  // below 2^-121 the limbs round to zero anyway
+    }
+    if (lane == 0) *s.exps = E;
+    if (lane == 0 && bad && error) *(volatile unsigned *)error = ERR_NONFINITE;
+    const float sc = pow2f(6 - E);
+    unsigned words[4][2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        unsigned t[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float r = bad ? 0.f : __fmul_rn(x[4 * q + i], sc);
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const float m = __fadd_rn(r, 12582912.0f);  // rint via the 1.5*2^23 magic
+                const float X = __fsub_rn(m, 12582912.0f);
+                t[l][i] = __float_as_uint(m);
+                r = __fmul_rn(__fsub_rn(r, X), 128.0f);
+            }
+        }
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const unsigned lo = __byte_perm(t[l][0], t[l][1], 0x0040);
+            const unsigned hi = __byte_perm(t[l][2], t[l][3], 0x0040);
+            words[l][q] = __byte_perm(lo, hi, 0x5410);
+        }
+    }
+    // natural words 2i and 2i+1 of the limb row: chunk (i / 8), word w = 2 (i % 8) (+1)
+    const unsigned chunk = (lane >> 3) * 64u, w0 = (lane & 7u) * 2u, w1 = w0 + 1u;
+    const unsigned p0 = chunk + ((w0 & 3u) * 4u + (w0 >> 2)) * 4u, p1 = chunk + ((w1 & 3u) * 4u + (w1 >> 2)) * 4u;
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        *reinterpret_cast<unsigned *>(s.xl + l * LIMB_STRIDE + p0) = words[l][0];
+        *reinterpret_cast<unsigned *>(s.xl + l * LIMB_STRIDE + p1) = words[l][1];
+    }
+}
+
+// Block b of a phase's input into the warp's limb slot; the block's sum of
+// squares (before the norm weight) into bss[b] for normalized inputs. Sources:
+// QKV: the embedding row (layer 0) or x after the previous layer; O: the
+// attention output; gate/up: x after O; down: h; logits: x after the last
+// layer. With tensor parallelism the d-row inputs are a base vector plus the
+// ranks' partial rows, added in rank order (every rank computes the same x),
+// and the last CTA stores the summed x for the next exchange's base.
+FYB_DEV bool prep_block(const DecodeParams &p, const Phase &ph, unsigned b, unsigned step, const LimbSlot &s,
+    double *bss, unsigned lane)
+{
+    const unsigned i0 = b * 256 + lane * 8;
+    const int l = (int)ph.layer;
+    float x[8];
+    const bool norm = ph.kind == PH_QKV || ph.kind == PH_GATEUP || ph.kind == PH_LOGITS;
+    const int prev = ph.kind == PH_LOGITS ? (int)p.nl - 1 : l - 1;  // the layer whose output QKV / logits read
+    if (ph.kind == PH_QKV && l == 0) {
+        const unsigned char *erow = p.embd + (unsigned long long)__ldcg(p.request) * p.embd_row_bytes;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = dequant_any(erow, (unsigned long long)i0 + j, p.embd_type);
+        if (p.tp > 1 && blockIdx.x == gridDim.x - 1) {  // the base of layer 0's O exchange
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ll_put(p.ll.xa + i0 + j, x[j], ll_tag(step, -1));
+        }
+    } else if (ph.kind == PH_O) {
+        if (!ll_wait8(p, p.ll.attn + i0, ll_tag(step, l), x)) return false;
+    } else if (ph.kind == PH_DOWN) {
+        if (!ll_wait8(p, p.ll.h + i0, ll_tag(step, l), x)) return false;
+    } else if (p.tp == 1) {
+        const u64 *src = ph.kind == PH_GATEUP ? p.ll.xm : p.ll.xa;
+        const unsigned tag = ll_tag(step, ph.kind == PH_GATEUP ? l : prev);
+        if (!ll_wait8(p, src + i0, tag, x)) return false;
+    } else {
+        // x = base + the ranks' partial rows: QKV / logits: x after O plus the
+        // down rows; gate/up: x after the previous exchange plus the O rows
+        // tags: the base is tagged with the layer whose output it completes
+        // (gate/up: the previous layer), the partial rows with their layer
+        const bool gu = ph.kind == PH_GATEUP;
+        const unsigned tag = ll_tag(step, gu ? l : prev);
+        const u64 *base = gu ? p.ll.xa : p.ll.xm;
+        const u64 *parts = reinterpret_cast<const u64 *>(p.peers[p.tp_rank] + (gu ? p.xl.xo : p.xl.xd));
+        if (!ll_wait8(p, base + i0, ll_tag(step, gu ? l - 1 : prev), x)) return false;
+        for (unsigned r = 0; r < p.tp; ++r) {
+            float y[8];
+            if (!ll_wait8(p, parts + (size_t)r * p.d + i0, tag, y)) return false;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) x[j] = __fadd_rn(x[j], y[j]);
+        }
+        if (ph.kind != PH_LOGITS && blockIdx.x == gridDim.x - 1) {  // the next exchange's base
+            u64 *dst = gu ? p.ll.xm : p.ll.xa;
+            const unsigned wt = ll_tag(step, gu ? l : prev);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ll_put(dst + i0 + j, x[j], wt);
+        }
+    }
+    if (norm) {
+        double ss = 0.0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += (double)x[j] * (double)x[j];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) bss[b] = ss;
+        const float *nw = ph.kind == PH_QKV ? p.layers[l].attn_norm
+                        : ph.kind == PH_GATEUP ? p.layers[l].ffn_norm : p.out_norm;
+        const float4 w0 = __ldg(reinterpret_cast<const float4 *>(nw + i0));
+        const float4 w1 = __ldg(reinterpret_cast<const float4 *>(nw + i0 + 4));
+        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = __fmul_rn(x[j], w[j]);
+    }
+    split_block(x, lane, s, p.error);
+    __syncwarp();
+    return true;
+}
+
+// ------------------------------------------------------------ tile outputs
+FYB_DEV __half *kv_layer(const DecodeParams &p, unsigned l, bool v)
+{
+    return (v ? p.vcache : p.kcache) + (size_t)l * p.Hkv * p.capacity * p.hd;
+}
+
+// Output of rows j and j + 8 of `tile` (the MMA rows gid and gid + 8 of the
+// repacked layouts): QKV: the RoPE pair (2i, 2i+1) of a head, q or K/V;
+// O / down: x rows (residual added) or, with tensor parallelism, this
+// rank's partial rows for every rank; gate/up: gate and up row j of the
+// tile's 8 FFN rows; logits: two vocabulary rows and their argmax key.
+FYB_DEV bool pair_output(const DecodeParams &p, const Phase &ph, unsigned step, unsigned tile, unsigned j, float yA,
+    float yB, unsigned long long &key)
+{
+    const unsigned l = ph.layer;
+    const unsigned tag = ll_tag(step, (int)l);
+    if (ph.kind == PH_QKV) {
+        // rows 2*j and 2*j+1 of the tile form one RoPE pair (llm_cpu.c:298-327)
+        const unsigned tq = p.H * p.hd / 16, tk = p.Hkv * p.hd / 16, hd = p.hd;
+        const unsigned seg = tile < tq ? 0 : tile < tq + tk ? 1 : 2;
+        const unsigned lt = tile - (seg == 0 ? 0 : seg == 1 ? tq : tq + tk);
+        const unsigned rowA = lt * 16 + 2 * j;
+        const unsigned pos = __ldcg(p.request + 1), pair = (rowA % hd) >> 1;
+        float a = yA, b = yB;
+        if (seg <= 1) {
+            const float c = __ldg(p.rope_cos + (size_t)pos * (hd >> 1) + pair);
+            const float s = __ldg(p.rope_sin + (size_t)pos * (hd >> 1) + pair);
+            a = __fsub_rn(__fmul_rn(yA, c), __fmul_rn(yB, s));
+            b = __fadd_rn(__fmul_rn(yA, s), __fmul_rn(yB, c));
+        }
+        if (seg == 0) {
+            ll_put(p.ll.q + rowA, a, tag);
+            ll_put(p.ll.q + rowA + 1, b, tag);
+        } else {
+            const unsigned kvh = rowA / hd, dd = rowA % hd;
+            const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+            *reinterpret_cast<__half2 *>(kv_layer(p, l, seg == 2) + ((size_t)kvh * p.capacity + pos) * hd + dd) =
+                __halves2half2(ha, hb);
+            u64 *nw = p.ll.kvnew + (seg == 2 ? p.Hkv * hd : 0u) + rowA;  // the attention reads row pos here
+            ll_put(nw, __half2float(ha), tag);
+            ll_put(nw + 1, __half2float(hb), tag);
+        }
+        return true;
+    }
+    if (ph.kind == PH_O || ph.kind == PH_DOWN) {
+        const unsigned rA = tile * 16 + j;
+        if (p.tp > 1) {  // this rank's partial rows, to every rank's exchange region
+            const size_t off = (ph.kind == PH_O ? p.xl.xo : p.xl.xd) + ((size_t)p.tp_rank * p.d + rA) * 8;
+            for (unsigned r = 0; r < p.tp; ++r) {
+                u64 *dst = reinterpret_cast<u64 *>(p.peers[r] + off);
+                if (r == p.tp_rank) { ll_put(dst, yA, tag); ll_put(dst + 8, yB, tag); }
+                else { ll_put_sys(dst, yA, tag); ll_put_sys(dst + 8, yB, tag); }
+            }
+            return true;
+        }
+        if (ph.kind == PH_O && l == 0) {  // layer 0: the residual is the embedding row
+            const unsigned char *erow = p.embd + (unsigned long long)__ldcg(p.request) * p.embd_row_bytes;
+            yA = __fadd_rn(dequant_any(erow, rA, p.embd_type), yA);
+            yB = __fadd_rn(dequant_any(erow, rA + 8, p.embd_type), yB);
+        }  // other layers: the caller added the residual rows
+        u64 *dst = ph.kind == PH_O ? p.ll.xm : p.ll.xa;
+        ll_put(dst + rA, yA, tag);
+        ll_put(dst + rA + 8, yB, tag);
+        return true;
+    }
+    if (ph.kind == PH_GATEUP) {  // llm_cpu.c:336-342: gate / (1 + expf(-gate)) * up
+        const float g = __fdiv_rn(yA, __fadd_rn(1.0f, expf(-yA)));
+        ll_put(p.ll.h + tile * 8 + j, __fmul_rn(g, yB), tag);
+        return true;
+    }
+    // PH_LOGITS: store; argmax key = (order key, ~index) so ties go to the
+    // lowest index (llm_cpu.c:896-905)
+    const unsigned rA = tile * 16 + j, rB = rA + 8;  // this rank's rows; p.vocab0 + row is the token
+    const bool okA = rA < p.V, okB = rB < p.V;
+    if (p.tp == 1) {
+        if (okA) p.logits[rA] = yA;
+        if (okB) p.logits[rB] = yB;
+    } else if (p.logits_mode == 1) {  // every rank gathers the whole vocabulary
+        for (unsigned r = 0; r < p.tp; ++r) {
+            float *lg = reinterpret_cast<float *>(p.peers[r] + p.xl.logits) + p.vocab0;
+            if (okA) lg[rA] = yA;
+            if (okB) lg[rB] = yB;
+        }
+    }
+    if (((okA && !isfinite(yA)) || (okB && !isfinite(yB))) && p.error) atomicCAS(p.error, 0u, ERR_NONFINITE);
+    const unsigned gA = p.vocab0 + rA, gB = p.vocab0 + rB;
+    const unsigned long long kA = okA ? ((unsigned long long)float_order_key(yA) << 32) | (0xffffffffu - gA) : 0ull;
+    const unsigned long long kB = okB ? ((unsigned long long)float_order_key(yB) << 32) | (0xffffffffu - gB) : 0ull;
+    const unsigned long long kk = kA > kB ? kA : kB;
+    key = kk > key ? kk : key;
+    return true;
 }
 
 // ------------------------------------------------------------ GEMV phase
-// Profiling: per-warp records of a GEMV phase, WTRACE_POINTS words each:
-// 0 entry (ns), 1 SM clock cycles spent waiting for weights, 2 all units
-// computed (ns), 3 outputs done (ns); then in the barrier form the times
-// (ns) after 4 the CTA barrier following the units, 5 the shared tiles'
-// outputs, 6 the fence, 7 the second CTA barrier; in the dataflow form
-// 4 its input preparation at phase entry done (ns), 5 cycles waiting for
-// input blocks between units, 6 cycles spent in tile outputs.
-FYB_DEV void wrecord(const DecodeParams &p, const Phase &ph, unsigned point, unsigned lane, unsigned long long value)
-{
-    if (!p.wtrace || lane) return;
-    const unsigned long long NW = (unsigned long long)gridDim.x * QG_WARPS;
-    const unsigned long long gw = (unsigned long long)blockIdx.x * QG_WARPS + (threadIdx.x >> 5);
-    const unsigned slot = ph.kind == PH_LOGITS ? p.nl * 5 : ph.layer * 5 + ph.kind;
-    p.wtrace[((size_t)slot * NW + gw) * WTRACE_POINTS + point] = value;
-}
-FYB_DEV void wstamp(const DecodeParams &p, const Phase &ph, unsigned point, unsigned lane)
-{
-    if (p.wtrace) wrecord(p, ph, point, lane, globaltimer());
-}
-
-// A warp's partial result for a tile it shares with other warps of its CTA.
-struct PartSlot {
-    unsigned tile;   // ~0u: empty
-    unsigned last;   // 1: this segment holds the tile's last unit
-    float v[16];     // rows 0..15 of the tile
-};
-constexpr unsigned PART_SLOTS_BYTES = QG_WARPS * 2 * sizeof(PartSlot) + QG_WARPS * 8;
-
-// One GEMV phase of this CTA: its warps compute their units (ring_begin
-// issued the first ones); a tile a warp covers completely produces its
-// output at once, while the at most two tiles it shares with neighbouring
-// warps (its first and last) leave partial sums in shared memory. After one
-// CTA barrier the warp holding a shared tile's last unit adds the partials
-// in warp order (so results do not depend on timing) and produces the
-// output. Then one fence and one counter update per CTA publish its tiles.
+// One GEMV phase of this CTA (see the file comment). `seq` counts the chunks
+// this CTA has reduced (it picks the partial-row buffer) and `pseq` the
+// phases (it picks the block sums of squares). False for every thread on
+// abort.
 template <unsigned TYPE>
-FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, Ring &r, const XBuf &xb, unsigned lane,
-    PartSlot *parts, unsigned long long *keys)
+FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, Ring &r, const LimbSlot &slot,
+    const Cta &cta, unsigned lane, unsigned &seq, unsigned pseq, unsigned long long &key)
 {
-    wstamp(p, ph, 0, lane);
-    const unsigned warp = threadIdx.x >> 5, n = r.n;
-    const unsigned nblk = ph.nblk, gid = lane >> 2, tig = lane & 3;
-    while (r.issued < n && r.issued < r.S) ring_issue(r, lane);  // the ring may have started shallow
-    // side inputs of the first two tiles this warp touches, loaded while the units run
-    const unsigned ta = (unsigned)(r.u0 / nblk), tz = (unsigned)((r.u0 + n + nblk - 1) / nblk);
-    TileIn in;
-    fetch_rope(p, ph, ta, tz, lane, in);
-    if (p.tp == 1 && (ph.kind == PH_DOWN || (ph.kind == PH_O && ph.layer > 0))) fetch_resid(p, ph, ta, tz, lane, in);
-    PartSlot *mine = parts + warp * 2;
-    if (lane < 2) mine[lane].tile = ~0u;
-    float accA = 0.f, accB = 0.f;
-    unsigned tile = (unsigned)(r.u0 / nblk), tile_units = 0, np = 0;
-    unsigned blk = (unsigned)(r.u0 - (unsigned long long)tile * nblk);  // advanced per unit, no division
-    unsigned long long key = 0ull;
-    long long wait_cycles = 0;
-    bool ok = true;
-    for (unsigned i = 0; i < n; ++i) {
-        const long long c0 = p.wtrace ? clock64() : 0;
-        const unsigned char *unit = ring_wait(r);
-        if (!unit) { raise_abort(p, ERR_TIMEOUT); ok = false; break; }
-        if (p.wtrace) wait_cycles += clock64() - c0;
-        compute_unit<TYPE, 1>(unit, blk, xb.xl, xb.xstride, xb.exps, nblk, xb.gsums, ph.K / 32, lane, accA, accB);
-        __syncwarp();
-        if (r.issued < n) ring_issue(r, lane);
-        ++tile_units;
-        const bool tile_end = blk + 1 == nblk;
-        blk = tile_end ? 0 : blk + 1;
-        if (!tile_end && i + 1 != n) continue;
-        const float yA = lane_total<1>(accA), yB = lane_total<1>(accB);
-        if (tile_units == nblk) {
-            tile_output(p, ph, tile, yA, yB, lane, key, in, ta);
-        } else if (np < 2) {  // only the first and the last tile can be shared
-            if (tig == 0) { mine[np].v[gid] = yA; mine[np].v[gid + 8] = yB; }
-            if (lane == 0) { mine[np].tile = tile; mine[np].last = tile_end ? 1u : 0u; }
-            ++np;
-        }
-        accA = 0.f; accB = 0.f;
-        tile_units = 0;
-        if (tile_end) ++tile;
-    }
-    wrecord(p, ph, 1, lane, (unsigned long long)wait_cycles);
-    wstamp(p, ph, 2, lane);
-    // the ring is empty: the next phase's weights start now
-    if (ok && !warp_aborted(p)) ring_next(p, ph, r, lane);
-    __syncthreads();
-    wstamp(p, ph, 4, lane);
-    // shared tiles: the warp with the tile's last unit sums every warp's part
-    for (unsigned k = 0; k < 2; ++k) {
-        const unsigned t = mine[k].tile;
-        if (t == ~0u || !mine[k].last) continue;
-        float yA = 0.f, yB = 0.f;
-        for (unsigned w = 0; w <= warp; ++w)
-#pragma unroll
-            for (unsigned j = 0; j < 2; ++j)
-                if (parts[w * 2 + j].tile == t) { yA += parts[w * 2 + j].v[gid]; yB += parts[w * 2 + j].v[gid + 8]; }
-        tile_output(p, ph, t, yA, yB, lane, key, in, ta);
-    }
-    if (ph.kind == PH_LOGITS && lane == 0) keys[warp] = key;
-    wstamp(p, ph, 5, lane);
-    // the lanes that wrote outputs (tig 0) order them before the CTA's counter update
-    if ((lane & 3) == 0 || p.tp > 1) {  // (prep_tp's shares are written by any thread)
-        // phases whose outputs other GPUs read (the exchanged O and down rows,
-        // the gathered logits) order them at system scope before the counters
-        if (p.tp > 1 && (ph.kind == PH_O || ph.kind == PH_DOWN || ph.kind == PH_LOGITS)) __threadfence_system();
-        else fence_acq_rel_gpu();
-    }
-    wstamp(p, ph, 6, lane);
-    __syncthreads();
-    wstamp(p, ph, 7, lane);
+    const unsigned warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
     unsigned tb, te;
     cta_tiles(ph, tb, te);
-    if (ph.kind == PH_QKV) {
-        if (warp == 0)
-            for (unsigned t = tb + lane; t < te; t += 32) atomicAdd(p.sync.qkv_done + ph.layer * p.Hkv + qkv_kvh(p, t), 1u);
-    } else if (threadIdx.x == 0 && te > tb) {
-        if (ph.kind == PH_LOGITS) {
-            unsigned long long best = 0ull;
-            for (unsigned w = 0; w < QG_WARPS; ++w) best = keys[w] > best ? keys[w] : best;
-            atomicMax(p.argmax_key, best);
-            __threadfence();
-            // the CTA that completes the last tile publishes the token (with
-            // tensor parallelism: this rank's best key, to every rank)
-            if (atomicAdd(p.sync.logit_tiles, te - tb) + (te - tb) == ph.w.tiles) {
-                __threadfence();
-                const unsigned long long k = atomicExch(p.argmax_key, 0ull);
-                atomicExch(p.sync.logit_tiles, 0u);
-                if (p.tp == 1) {
-                    *p.argmax_token = 0xffffffffu - (unsigned)(k & 0xffffffffu);
-                } else {
-                    for (unsigned j = 0; j < p.tp; ++j)
-                        reinterpret_cast<unsigned long long *>(p.peers[j] + p.xl.keys)[p.tp_rank] = k;
-                    __threadfence_system();
-                    for (unsigned j = 0; j < p.tp; ++j) atomicAdd_system(xctr(p, j) + 2 * p.nl, 1u);
-                }
+    const unsigned T = te - tb, nblk = ph.nblk;
+    const bool norm = ph.kind == PH_QKV || ph.kind == PH_GATEUP || ph.kind == PH_LOGITS;
+    double *bss = cta.bss + (pseq & 1) * NORM_BLOCKS_MAX;
+    bool ok = true;
+    unsigned cur_b = ~0u;
+    if (r.n == 0 && !warp_aborted(p)) ring_next(p, ph, r, lane);  // no units here: only the next ring
+    if (T == 0) return __syncthreads_or(aborted(p)) == 0;  // keeps the CTA's phases in step (bss, parts)
+    for (unsigned c = 0; c * CHUNK < T; ++c) {
+        Walk wk;
+        wk.T = T; wk.nblk = nblk; wk.c = c;
+        walk_chunk(wk, warp);
+        const unsigned Tc = wk.Tc;
+        float *parts = cta.parts + (size_t)(seq & 1) * CHUNK * QG_WARPS * 16;
+        // this warp's partial rows of the chunk's tiles start at zero
+        for (unsigned i = lane; i < Tc * 16; i += 32) parts[((i >> 4) * QG_WARPS + warp) * 16 + (i & 15)] = 0.f;
+        __syncwarp();
+        for (unsigned k = wk.k; k < wk.e && ok; ++k) {
+            const unsigned b = k / Tc, t = k - b * Tc;
+            if (b != cur_b) {
+                ok = prep_block(p, ph, b, step, slot, bss, lane);
+                cur_b = b;
+                if (!ok) break;
             }
-        } else if (p.tp > 1 && (ph.kind == PH_O || ph.kind == PH_DOWN)) {
-            const unsigned idx = (ph.kind == PH_O ? 0 : p.nl) + ph.layer;
-            for (unsigned j = 0; j < p.tp; ++j) atomicAdd_system(xctr(p, j) + idx, te - tb);
-        } else {
-            signal_tiles(p, ph, tb, te - tb);
+            const unsigned char *unit = ring_wait(r);
+            if (!unit) { if (lane == 0) raise_abort(p, ERR_TIMEOUT); ok = false; break; }
+            float accA = 0.f, accB = 0.f;
+            compute_unit<TYPE, 1>(unit, 0, slot.xl, LIMB_STRIDE, slot.exps, 1, slot.gsums, 8, lane, accA, accB);
+            __syncwarp();
+            if (r.issued < r.n) ring_issue(r, lane);
+            const float yA = lane_total<1>(accA), yB = lane_total<1>(accB);
+            if (tig == 0) {
+                float *row = parts + (t * QG_WARPS + warp) * 16;
+                row[gid] += yA;
+                row[gid + 8] += yB;
+            }
+            // the ring is empty after this warp's last unit: the next phase's weights start now
+            if (r.consumed == r.n && !warp_aborted(p)) ring_next(p, ph, r, lane);
         }
+        // reducer threads (t * 8 + j) read their residual rows before the barrier
+        const unsigned i = threadIdx.x, t = i >> 3, j = i & 7;
+        const bool reducer = i < Tc * 8;
+        const bool resid = p.tp == 1 && (ph.kind == PH_DOWN || (ph.kind == PH_O && ph.layer > 0));
+        u64 ra = 0, rb = 0;
+        const u64 *rsrc = ph.kind == PH_O ? p.ll.xa : p.ll.xm;
+        const unsigned rA = (tb + c * CHUNK + t) * 16 + j;
+        if (reducer && resid) { ra = ll_get(rsrc + rA); rb = ll_get(rsrc + rA + 8); }
+        // every failure raised the abort word before this barrier
+        if (__syncthreads_or(!ok || aborted(p))) return false;
+        if (reducer) {
+            float yA = 0.f, yB = 0.f;
+#pragma unroll 4
+            for (unsigned w = 0; w < QG_WARPS; ++w) {
+                yA += parts[(t * QG_WARPS + w) * 16 + j];
+                yB += parts[(t * QG_WARPS + w) * 16 + j + 8];
+            }
+            if (norm) {
+                double ss = 0.0;
+                for (unsigned bb = 0; bb < nblk; ++bb) ss += bss[bb];
+                const float scale = (float)(1.0 / sqrt(ss / (double)ph.K + (double)p.eps));
+                yA = __fmul_rn(yA, scale);
+                yB = __fmul_rn(yB, scale);
+            }
+            if (resid) {
+                const unsigned rtag = ll_tag(step, ph.kind == PH_O ? (int)ph.layer - 1 : (int)ph.layer);
+                float xa_, xb_;
+                if (ll_ok(ra, rtag)) xa_ = ll_val(ra); else ll_wait1(p, rsrc + rA, rtag, xa_);
+                if (ll_ok(rb, rtag)) xb_ = ll_val(rb); else ll_wait1(p, rsrc + rA + 8, rtag, xb_);
+                yA = __fadd_rn(xa_, yA);
+                yB = __fadd_rn(xb_, yB);
+            }
+            // a failed wait raised the abort word; the next CTA barrier sees it
+            pair_output(p, ph, step, tb + c * CHUNK + t, j, yA, yB, key);
+        }
+        ++seq;
     }
-    wstamp(p, ph, 3, lane);
-    return ok;
+    return true;
 }
 
-FYB_DEV bool run_gemv(const DecodeParams &p, const Phase &ph, Ring &r, const XBuf &xb, unsigned lane,
-    PartSlot *parts, unsigned long long *keys)
+FYB_DEV bool run_gemv(const DecodeParams &p, const Phase &ph, unsigned step, Ring &r, const LimbSlot &slot,
+    const Cta &cta, unsigned lane, unsigned &seq, unsigned pseq, unsigned long long &key)
 {
-    return ph.w.type == T_Q4_K ? gemv_phase<T_Q4_K>(p, ph, r, xb, lane, parts, keys)
-                               : gemv_phase<T_Q6_K>(p, ph, r, xb, lane, parts, keys);
+    return ph.w.type == T_Q4_K ? gemv_phase<T_Q4_K>(p, ph, step, r, slot, cta, lane, seq, pseq, key)
+                               : gemv_phase<T_Q6_K>(p, ph, step, r, slot, cta, lane, seq, pseq, key);
 }
 
 // ------------------------------------------------------------ attention
 struct AttnSmem {
     float *wm, *wl;  // [warps][G] running max and sum of each warp
     float *wo;       // [warps][G][HD] unnormalized outputs
+    float *qkv;      // [G * HD + 2 * HD] the group's query rows, the new K and V rows
     unsigned *flag;
 };
 
 FYB_HOST_DEV size_t attn_smem_floats(unsigned G, unsigned hd)
 {
-    return 2 * (size_t)QG_WARPS * G + (size_t)QG_WARPS * G * hd;
+    return 2 * (size_t)QG_WARPS * G + (size_t)QG_WARPS * G * hd + (size_t)(G + 2) * hd;
 }
 
 // Partitions of the context per KV head for attended length L: one per
@@ -838,35 +739,50 @@ FYB_DEV void load_half_row(const __half *src, float (&out)[DPL])
 
 // One (KV head, partition) item with all warps of the CTA. Lane i owns head
 // dimensions [DPL*i, DPL*i + DPL); warp w takes positions c0 + w, c0 + w + 16,
-// ... in batches of PB, loading the q slices, and the K and V rows of a whole
-// batch, before using any of them, so a batch costs one round trip to
-// memory. Scores are lane partial dots reduced over the warp; an online
-// softmax per query head keeps (max, sum, unnormalized output) per warp, and
-// the warps merge in shared memory. The CTA's result goes to the item's slot;
-// the last partition of a KV head merges the slots in partition order and
-// publishes the head group (attention.cu does the same across launches).
+// ... in batches of PB, loading the K and V rows of a whole batch before
+// using any of them, so a batch costs one round trip to memory. The query
+// rows and the new position's K/V rows (tagged words of this layer) are
+// polled first; older positions come from the fp16 cache. Scores are lane
+// partial dots reduced over the warp; an online softmax per query head keeps
+// (max, sum, unnormalized output) per warp, and the warps merge in shared
+// memory. The CTA's result goes to the item's slot; the last partition of a
+// KV head merges the slots in partition order and stores the head group's
+// attention output as tagged words.
 template <int HD, int G>
-FYB_DEV void attention_item(const DecodeParams &p, unsigned l, unsigned kvh, unsigned sp, const AttnSmem &sm)
+FYB_DEV bool attention_item(const DecodeParams &p, unsigned step, unsigned l, unsigned kvh, unsigned sp,
+    const AttnSmem &sm)
 {
     constexpr int DPL = HD / 32, PB = G <= 2 ? 4 : G <= 4 ? 2 : 1;
     const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const unsigned L = __ldcg(p.request + 1) + 1;
+    const unsigned pos = __ldcg(p.request + 1), L = pos + 1;
     const unsigned S = attn_parts(p, L);
     const unsigned chunk = (L + S - 1) / S;
     const unsigned c0 = min(L, sp * chunk), c1 = min(L, c0 + chunk);
+    const unsigned tag = ll_tag(step, (int)l);
     const __half *K = kv_layer(p, l, false) + (size_t)kvh * p.capacity * HD + DPL * lane;
     const __half *V = kv_layer(p, l, true) + (size_t)kvh * p.capacity * HD + DPL * lane;
-    float qr[G][DPL];
+    // the query rows of the group and, in the partition holding it, the new
+    // position's K and V rows: one tagged word per thread, polled by the whole
+    // CTA into shared memory, then every warp reads them from there
+    const bool has_new = pos >= c0 && pos < c1;
+    bool ok = true;
+    for (unsigned i = threadIdx.x; i < G * HD + (has_new ? 2 * HD : 0); i += QG_THREADS) {
+        const u64 *src = i < G * HD ? p.ll.q + (size_t)kvh * G * HD + i
+                       : p.ll.kvnew + (size_t)(i < G * HD + HD ? kvh : p.Hkv + kvh) * HD + (i - G * HD) % HD;
+        float v = 0.f;
+        ok = ok && ll_wait1(p, src, tag, v);
+        sm.qkv[i] = v;
+    }
+    if (__syncthreads_or(!ok)) return false;
+    float qr[G][DPL], knew[DPL], vnew[DPL];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const float *qg = p.q + ((size_t)kvh * G + g) * HD + DPL * lane;
-        if constexpr (DPL == 4) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(qg));
-            qr[g][0] = v.x; qr[g][1] = v.y; qr[g][2] = v.z; qr[g][3] = v.w;
-        } else {
-            const float2 v = __ldcg(reinterpret_cast<const float2 *>(qg));
-            qr[g][0] = v.x; qr[g][1] = v.y;
-        }
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) qr[g][e] = sm.qkv[g * HD + DPL * lane + e];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+        knew[e] = has_new ? sm.qkv[G * HD + DPL * lane + e] : 0.f;
+        vnew[e] = has_new ? sm.qkv[G * HD + HD + DPL * lane + e] : 0.f;
     }
     float m[G], lsum[G], o[G][DPL];
 #pragma unroll
@@ -882,9 +798,14 @@ FYB_DEV void attention_item(const DecodeParams &p, unsigned l, unsigned kvh, uns
         for (int j = 0; j < PB; ++j) {
             const unsigned t = t0 + QG_WARPS * j;
             valid[j] = t < c1;
-            const size_t row = (size_t)(valid[j] ? t : t0) * HD;
-            load_half_row<DPL>(K + row, kf[j]);
-            load_half_row<DPL>(V + row, vf[j]);
+            if (valid[j] && t == pos) {
+#pragma unroll
+                for (int e = 0; e < DPL; ++e) { kf[j][e] = knew[e]; vf[j][e] = vnew[e]; }
+            } else {
+                const size_t row = (size_t)(valid[j] ? t : t0) * HD;
+                load_half_row<DPL>(K + row, kf[j]);
+                load_half_row<DPL>(V + row, vf[j]);
+            }
         }
         float sc[PB][G];
 #pragma unroll
@@ -930,7 +851,11 @@ FYB_DEV void attention_item(const DecodeParams &p, unsigned l, unsigned kvh, uns
     }
     __syncthreads();
     constexpr unsigned SLOT = G * (HD + 2);
-    float *slot = p.attn_partials + ((size_t)kvh * S + sp) * SLOT;
+    // partition slots alternate between layers; counters are per layer and
+    // reset by the merging CTA (read again only in the next step's launch)
+    float *const parts_l = p.attn_partials + (size_t)(l & 1) * p.Hkv * ATT_MAX_PARTS * SLOT;
+    unsigned *const counter = p.sync.attn_counters + (size_t)l * p.Hkv + kvh;
+    float *slot = parts_l + ((size_t)kvh * S + sp) * SLOT;
     for (unsigned i = threadIdx.x; i < G * HD; i += QG_THREADS) {
         const unsigned g = i / HD, dd = i % HD;
         float M = -INFINITY;
@@ -947,13 +872,14 @@ FYB_DEV void attention_item(const DecodeParams &p, unsigned l, unsigned kvh, uns
     }
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) *sm.flag = atomicAdd(p.sync.attn_counters + kvh, 1u) == S - 1;
+    if (threadIdx.x == 0) *sm.flag = atomicAdd(counter, 1u) == S - 1;
     __syncthreads();
-    if (!*sm.flag) return;
+    if (!*sm.flag) return true;
     __threadfence();
     // merge the S slots: their maxima and sums staged in shared memory (one
     // round of loads), then every output element loads its S values at once
-    const float *all = p.attn_partials + (size_t)kvh * S * SLOT;
+    const float *all = parts_l + (size_t)kvh * S * SLOT;
+    if (threadIdx.x == 0) *counter = 0;
     float *sM = sm.wo, *sD = sm.wo + ATT_MAX_PARTS * G;
     for (unsigned i = threadIdx.x; i < S * G; i += QG_THREADS) {
         const unsigned s2 = i / G, g = i % G;
@@ -979,99 +905,121 @@ FYB_DEV void attention_item(const DecodeParams &p, unsigned l, unsigned kvh, uns
                 den = fmaf(sD[s2 * G + g], f, den);
             }
         }
-        p.attn[((size_t)kvh * G + g) * HD + dd] = acc / den;
+        ll_put(p.ll.attn + ((size_t)kvh * G + g) * HD + dd, acc / den, tag);
     }
-    __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) {
-        p.sync.attn_counters[kvh] = 0;
-        __threadfence();
-        if (p.df.attn_kv) atomicAdd(p.df.attn_kv + l * p.Hkv + kvh, 1u);
-        else atomicAdd(p.sync.attn_done + l, 1u);
-    }
+    return true;
 }
 
 template <int HD, int G>
-FYB_DEV bool attention_phase(const DecodeParams &p, unsigned l, unsigned step, const AttnSmem &sm)
+FYB_DEV bool attention_phase(const DecodeParams &p, unsigned step, unsigned l, const AttnSmem &sm)
 {
     const unsigned S = attn_parts(p, __ldcg(p.request + 1) + 1);
     const unsigned items = p.Hkv * S;
-    const unsigned per_step = G * HD / 16 + 2 * HD / 16;
-    for (unsigned it = blockIdx.x; it < items; it += gridDim.x) {
-        const unsigned kvh = it / S, sp = it % S;
-        unsigned untraced = ~0u - 4;  // item counts differ between CTAs: not traced
-        if (!cta_wait(p, p.sync.qkv_done + l * p.Hkv + kvh, step * per_step, sm.flag, untraced)) return false;
-        attention_item<HD, G>(p, l, kvh, sp, sm);
-    }
+    for (unsigned it = blockIdx.x; it < items; it += gridDim.x)
+        if (!attention_item<HD, G>(p, step, l, it / S, it % S, sm)) return false;
     return true;
 }
 
 // ------------------------------------------------------------ the kernel
 struct SmemLayout {
-    size_t rings, bars, xbuf, exps, gsums, red, parts, misc, total;
+    size_t rings, bars, uni, parts, bss, keys, misc, total;
 };
 
-// Everything but the rings; the rings take what is left of the 227 KB.
-FYB_HOST_DEV SmemLayout smem_layout(unsigned d, unsigned ffn, unsigned H, unsigned Hkv, unsigned hd,
-    unsigned ring_bytes)
+// Everything but the rings; the rings take what is left of the 227 KB. The
+// limb slots and the attention scratch share one region (attention runs
+// between GEMV phases, behind CTA barriers).
+FYB_HOST_DEV SmemLayout smem_layout(unsigned H, unsigned Hkv, unsigned hd, unsigned ring_bytes)
 {
     SmemLayout s;
-    const unsigned kmax = ffn > d ? ffn : d, kin = H * hd > kmax ? H * hd : kmax;
-    const size_t xbytes = (size_t)4 * (kin + QG_XPAD);
+    const size_t limbs = (size_t)QG_WARPS * LIMB_SLOT;
     const size_t abytes = attn_smem_floats(H / Hkv, hd) * 4;
     s.rings = 0;
     s.bars = (size_t)QG_WARPS * ring_bytes;
-    s.xbuf = s.bars + (size_t)QG_WARPS * RING_BARS * 8;
-    s.exps = s.xbuf + ((xbytes > abytes ? xbytes : abytes) + 15) / 16 * 16;
-    s.gsums = s.exps + ((size_t)(kin / 256) * 4 + 15) / 16 * 16;
-    s.red = s.gsums + ((size_t)(kin / 32) * 4 + 15) / 16 * 16;
-    s.parts = s.red + QG_WARPS * sizeof(double);
-    s.misc = s.parts + PART_SLOTS_BYTES;
+    s.uni = s.bars + (size_t)QG_WARPS * RING_BARS * 8;
+    s.parts = s.uni + ((limbs > abytes ? limbs : abytes) + 15) / 16 * 16;
+    s.bss = s.parts + (size_t)2 * CHUNK * QG_WARPS * 16 * 4;
+    s.keys = s.bss + (size_t)2 * NORM_BLOCKS_MAX * 8;
+    s.misc = s.keys + (size_t)QG_WARPS * 8;
     s.total = s.misc + 16;
     return s;
 }
 
-// End of a step (every CTA): the last CTA out advances the step counter and,
-// for greedy steps, the request. Nothing happens after an abort: the plan is
-// failed and its sync words are not trusted again.
-FYB_DEV void end_step(const DecodeParams &p, unsigned *flag, unsigned &ts)
+// End of a step (every CTA): the logits argmax key of the CTA, then the last
+// CTA out advances the step counter and, for greedy steps, the request.
+// Nothing happens after an abort: the plan is failed and its sync words are
+// not trusted again.
+FYB_DEV void end_step(const DecodeParams &p, const Cta &cta, unsigned long long key, bool logits_done)
 {
     const bool tp = p.tp > 1;
-    if (!cta_wait(p, nullptr, 0, flag, ts)) return;
-    // the last CTA out advances the step (and, for greedy steps, the request)
-    if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd(p.sync.exit_count, 1u) == gridDim.x - 1) {
-            __threadfence();
-            p.sync.exit_count[0] = 0;
-            if (tp && p.logits_mode) {  // the token: the best of the ranks' keys
-                // keys move once per step with logits: request[4] counts those steps
-                const unsigned *kc = xctr(p, p.tp_rank) + 2 * p.nl;
-                const unsigned lstep = p.request[4] + 1;
-                bool got = false;
-                for (unsigned i = 0; i < WAIT_LIMIT && !aborted(p); ++i) {
-                    if (reached(ld_acquire_sys(kc), lstep * p.tp)) { got = true; break; }
-                    __nanosleep(32);
-                }
-                if (!got) { raise_abort(p, ERR_TIMEOUT); return; }
-                const unsigned long long *kk = reinterpret_cast<const unsigned long long *>(p.peers[p.tp_rank] + p.xl.keys);
-                unsigned long long best = 0ull;
-                for (unsigned j = 0; j < p.tp; ++j) {
-                    const unsigned long long v = __ldcg(kk + j);
-                    best = v > best ? v : best;
-                }
-                *p.argmax_token = 0xffffffffu - (unsigned)(best & 0xffffffffu);
-            }
-            if (p.logits_mode == 2) {
-                const unsigned t = __ldcg(p.argmax_token);
-                p.tokens_log[p.request[2]] = t;
-                p.request[0] = t;
-                p.request[1] += 1;
-                p.request[2] += 1;
-            }
-            p.request[3] += 1;
-            if (p.logits_mode) p.request[4] += 1;
+    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (logits_done) {
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+            key = other > key ? other : key;
         }
+        if (lane == 0) cta.keys[warp] = key;
+    }
+    if (__syncthreads_or(threadIdx.x == 0 && aborted(p))) return;
+    if (threadIdx.x != 0) return;
+    if (logits_done) {
+        unsigned tb, te;
+        const Phase lg = make_phase(p, PH_LOGITS, 0);
+        cta_tiles(lg, tb, te);
+        if (te > tb) {
+            unsigned long long best = 0ull;
+            for (unsigned w = 0; w < QG_WARPS; ++w) best = cta.keys[w] > best ? cta.keys[w] : best;
+            atomicMax(p.argmax_key, best);
+            __threadfence();
+            // the CTA that completes the last tile publishes the token (with
+            // tensor parallelism: this rank's best key, to every rank)
+            if (atomicAdd(p.sync.logit_tiles, te - tb) + (te - tb) == lg.w.tiles) {
+                __threadfence();
+                const unsigned long long k = atomicExch(p.argmax_key, 0ull);
+                atomicExch(p.sync.logit_tiles, 0u);
+                if (!tp) {
+                    *p.argmax_token = 0xffffffffu - (unsigned)(k & 0xffffffffu);
+                } else {
+                    for (unsigned j = 0; j < p.tp; ++j)
+                        reinterpret_cast<unsigned long long *>(p.peers[j] + p.xl.keys)[p.tp_rank] = k;
+                    __threadfence_system();
+                    for (unsigned j = 0; j < p.tp; ++j) atomicAdd_system(xctr(p, j) + 2 * p.nl, 1u);
+                }
+            }
+        }
+    }
+    __threadfence();
+    if (atomicAdd(p.sync.exit_count, 1u) == gridDim.x - 1) {
+        __threadfence();
+        p.sync.exit_count[0] = 0;
+        if (tp && p.logits_mode) {  // the token: the best of the ranks' keys
+            // keys move once per step with logits: request[4] counts those steps
+            const unsigned *kc = xctr(p, p.tp_rank) + 2 * p.nl;
+            const unsigned lstep = p.request[4] + 1;
+            bool got = false;
+            for (unsigned i = 0; i < WAIT_LIMIT && !aborted(p); ++i) {
+                if (reached(ld_acquire_sys(kc), lstep * p.tp)) { got = true; break; }
+                __nanosleep(32);
+            }
+            if (!got) { raise_abort(p, ERR_TIMEOUT); return; }
+            const unsigned long long *kk = reinterpret_cast<const unsigned long long *>(p.peers[p.tp_rank] + p.xl.keys);
+            unsigned long long best = 0ull;
+            for (unsigned j = 0; j < p.tp; ++j) {
+                const unsigned long long v = __ldcg(kk + j);
+                best = v > best ? v : best;
+            }
+            *p.argmax_token = 0xffffffffu - (unsigned)(best & 0xffffffffu);
+        }
+        if (p.logits_mode == 2) {
+            const unsigned t = __ldcg(p.argmax_token);
+            p.tokens_log[p.request[2]] = t;
+            p.request[0] = t;
+            p.request[1] += 1;
+            p.request[2] += 1;
+        }
+        p.request[3] += 1;
+        if (p.logits_mode) p.request[4] += 1;
     }
 }
 
@@ -1082,30 +1030,25 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
 {
     extern __shared__ __align__(128) unsigned char smem[];
     const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const SmemLayout lay = smem_layout(p.d, p.ffn, p.H, p.Hkv, p.hd, p.ring_bytes);
+    const SmemLayout lay = smem_layout(p.H, p.Hkv, p.hd, p.ring_bytes);
     Ring ring;
     ring.base = smem + lay.rings + (size_t)warp * p.ring_bytes;
     ring.bars = reinterpret_cast<uint64_t *>(smem + lay.bars) + warp * RING_BARS;
     ring.bytes = p.ring_bytes;
-    ring.pre = p.ring_pre;
     ring.par = 0;
     ring.issued = ring.consumed = ring.n = 0;
-    XBuf xb;
-    const unsigned kmax = p.ffn > p.d ? p.ffn : p.d;
-    xb.xstride = (p.H * p.hd > kmax ? p.H * p.hd : kmax) + QG_XPAD;
-    xb.xl = reinterpret_cast<signed char *>(smem + lay.xbuf);
-    xb.exps = reinterpret_cast<int *>(smem + lay.exps);
-    xb.gsums = reinterpret_cast<float *>(smem + lay.gsums);
-    double *red = reinterpret_cast<double *>(smem + lay.red);
-    PartSlot *parts = reinterpret_cast<PartSlot *>(smem + lay.parts);
-    unsigned long long *keys = reinterpret_cast<unsigned long long *>(smem + lay.parts + QG_WARPS * 2 * sizeof(PartSlot));
-    unsigned *flag = reinterpret_cast<unsigned *>(smem + lay.misc);
-    float *scale_smem = reinterpret_cast<float *>(flag + 1);
-    AttnSmem as;  // overlays the limb buffer, which is idle during attention
-    as.wm = reinterpret_cast<float *>(smem + lay.xbuf);
+    const LimbSlot slot = limb_slot(smem + lay.uni, warp);
+    Cta cta;
+    cta.parts = reinterpret_cast<float *>(smem + lay.parts);
+    cta.bss = reinterpret_cast<double *>(smem + lay.bss);
+    cta.keys = reinterpret_cast<unsigned long long *>(smem + lay.keys);
+    cta.flag = reinterpret_cast<unsigned *>(smem + lay.misc);
+    AttnSmem as;  // overlays the limb slots, idle during attention
+    as.wm = reinterpret_cast<float *>(smem + lay.uni);
     as.wl = as.wm + QG_WARPS * G;
     as.wo = as.wl + QG_WARPS * G;
-    as.flag = flag + 2;
+    as.qkv = as.wo + QG_WARPS * G * HD;
+    as.flag = cta.flag;
 
     if (lane == 0) {
         for (unsigned s = 0; s < RING_BARS; ++s) mbar_init(ring.bars + s, 1);
@@ -1114,70 +1057,36 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
     __syncwarp();
 
     const unsigned step = __ldcg(p.request + 3) + 1;
-    const unsigned dt = p.d / 16;
     bool ok = true;
-    unsigned ts = 0;
-    const bool tp = p.tp > 1;
-    // this rank's exchange region as floats (the partial rows all ranks wrote)
-    const float *xparts = tp ? reinterpret_cast<const float *>(p.peers[p.tp_rank]) : nullptr;
-    stamp(p, ts);
-    Phase cur = make_phase(p, PH_QKV, 0), nx0;
-    ring_begin(cur, ring, lane, phase_after(p, PH_QKV, 0, nx0) ? &nx0 : nullptr, p.l2_prefetch);
+    unsigned seq = 0, pseq = 0, ts = 0;
+    unsigned long long key = 0ull;
+    stamp(p, ts++);
+    Phase cur = make_phase(p, PH_QKV, 0);
+    ring_begin(cur, ring, lane);
     for (unsigned l = 0; l < p.nl && ok; ++l) {
-        // Q/K/V + RoPE + KV append
-        if (tp) {  // x = x_mid + the ranks' down rows (or the embedding row); written to xa
-            ok = cta_wait(p, l ? xctr(p, p.tp_rank) + p.nl + l - 1 : nullptr, step * p.tp * dt, flag, ts, true);
-            if (!ok) break;
-            prep_tp(p, l == 0, p.xm, xparts + p.xl.xd / 4, p.xa, p.layers[l].attn_norm, xb, red);
-        } else {
-            ok = cta_wait(p, l ? p.sync.down_done + (l - 1) : nullptr, step * dt, flag, ts);
-            if (!ok) break;
-            if (l == 0) prep_input(p, true, nullptr, nullptr, 0, p.layers[0].attn_norm, p.d, xb, red, scale_smem);
-            else prep_input(p, false, p.xa, p.ss_d, dt, p.layers[l].attn_norm, p.d, xb, red, scale_smem);
+        for (unsigned k = 0; k < 5 && ok; ++k) {
+            if (k == 1) {  // attention; its scratch overlays the limb slots, so all warps leave it together
+                ok = attention_phase<HD, G>(p, step, l, as);
+                ok = __syncthreads_or(!ok || aborted(p)) == 0;
+            } else {
+                ok = run_gemv(p, cur, step, ring, slot, cta, lane, seq, pseq++, key);
+                Phase nx;
+                if (phase_after(p, cur.kind, cur.layer, nx)) cur = nx;
+            }
+            stamp(p, ts++);
         }
-        stamp(p, ts);
-        run_gemv(p, cur, ring, xb, lane, parts, keys); advance(p, cur);  // now the O projection
-        // attention (its scratch overlays the limb buffer, idle now)
-        ok = cta_wait(p, nullptr, 0, flag, ts) && attention_phase<HD, G>(p, l, step, as);
-        stamp(p, ts);
-        if (!ok) break;
-        // output projection; residual add in the tile outputs
-        ok = cta_wait(p, p.sync.attn_done + l, step * p.Hkv, flag, ts);
-        if (!ok) break;
-        prep_input(p, false, p.attn, nullptr, 0, nullptr, p.H * p.hd, xb, red, scale_smem);
-        stamp(p, ts);
-        run_gemv(p, cur, ring, xb, lane, parts, keys); advance(p, cur);  // gate/up
-        // gate/up + SwiGLU
-        if (tp) {  // x_mid = x + the ranks' O rows; written to xm
-            ok = cta_wait(p, xctr(p, p.tp_rank) + l, step * p.tp * dt, flag, ts, true);
-            if (!ok) break;
-            prep_tp(p, false, p.xa, xparts + p.xl.xo / 4, p.xm, p.layers[l].ffn_norm, xb, red);
-        } else {
-            ok = cta_wait(p, p.sync.o_done + l, step * dt, flag, ts);
-            if (!ok) break;
-            prep_input(p, false, p.xm, p.ss_o, dt, p.layers[l].ffn_norm, p.d, xb, red, scale_smem);
-        }
-        stamp(p, ts);
-        run_gemv(p, cur, ring, xb, lane, parts, keys); advance(p, cur);  // down
-        // down; residual add in the tile outputs
-        ok = cta_wait(p, p.sync.gu_done + l, step * (p.ffn / 8), flag, ts);
-        if (!ok) break;
-        prep_input(p, false, p.h, nullptr, 0, nullptr, p.ffn, xb, red, scale_smem);
-        stamp(p, ts);
-        run_gemv(p, cur, ring, xb, lane, parts, keys); advance(p, cur);  // the next layer's QKV, or the logits
     }
+    bool logits_done = false;
     if (ok && p.logits_mode) {
-        if (tp) ok = cta_wait(p, xctr(p, p.tp_rank) + 2 * p.nl - 1, step * p.tp * dt, flag, ts, true);
-        else ok = cta_wait(p, p.sync.down_done + (p.nl - 1), step * dt, flag, ts);
-        if (ok) {
-            if (tp) prep_tp(p, false, p.xm, xparts + p.xl.xd / 4, nullptr, p.out_norm, xb, red);
-            else prep_input(p, false, p.xa, p.ss_d, dt, p.out_norm, p.d, xb, red, scale_smem);
-            stamp(p, ts);
-            run_gemv(p, cur, ring, xb, lane, parts, keys);
-        }
+        ok = run_gemv(p, cur, step, ring, slot, cta, lane, seq, pseq++, key);
+        logits_done = ok;
     }
+    stamp(p, 1 + 5 * p.nl);
     ring_drain(ring);
-    end_step(p, flag, ts);
+    if (ok) {
+        end_step(p, cta, key, logits_done);
+        stamp(p, 2 + 5 * p.nl);
+    }
 }
 
 using DecodeKernel = void (*)(const DecodeParams);

@@ -101,10 +101,10 @@ int launch_attention(const AttentionLaunch &L, cudaStream_t s);
 
 // ---------------------------------------------------------------- decode.cu
 // Tensor-parallel exchange region of a plan (byte offsets). Every rank has
-// one; rank j writes its partial O and down rows into [xo|xd] + j*d floats of
-// every rank's region, its vocabulary slice of the logits into `logits`, its
-// best argmax key into keys[j], and bumps the counters: o_x[l] (index l),
-// d_x[l] (nl + l), keys (2 nl); 2 nl + 1 is the shared abort word.
+// one; rank j writes its partial O and down rows as tagged 8-byte words into
+// [xo|xd] + j*d words of every rank's region, its vocabulary slice of the
+// logits into `logits`, its best argmax key into keys[j]; counters: keys at
+// 2 nl, the shared abort word at 2 nl + 1.
 struct XchgLayout {
     size_t xo = 0, xd = 0, logits = 0, keys = 0, ctr = 0, bytes = 0;
 };
@@ -113,8 +113,8 @@ inline XchgLayout xchg_layout(unsigned tp, unsigned d, unsigned V, unsigned nl)
     auto up = [](size_t b) { return (b + 255) / 256 * 256; };
     XchgLayout x;
     size_t o = 0;
-    x.xo = o; o += up((size_t)tp * d * 4);
-    x.xd = o; o += up((size_t)tp * d * 4);
+    x.xo = o; o += up((size_t)tp * d * 8);
+    x.xd = o; o += up((size_t)tp * d * 8);
     x.logits = o; o += up((size_t)V * 4);
     x.keys = o; o += up((size_t)tp * 8);
     x.ctr = o; o += up(((size_t)2 * nl + 4) * 4);
@@ -126,34 +126,31 @@ inline XchgLayout xchg_layout(unsigned tp, unsigned d, unsigned V, unsigned nl)
 struct DecodeLayer {
     QWeights qkv, o, gateup, down;  // repacked as for the stand-alone GEMV
     const float *attn_norm = nullptr, *ffn_norm = nullptr;
-    __half *kcache = nullptr, *vcache = nullptr;  // [kv_heads][capacity][hd]
 };
 struct DecodeGeometry {
     unsigned nl = 0, d = 0, H = 0, Hkv = 0, hd = 0, ffn = 0, V = 0, capacity = 0;
 };
+// Vectors handed from phase to phase as tagged 8-byte words {float, tag}
+// (zero at plan creation; decode_kernel.cuh describes the tags).
+struct DecodeLL {
+    unsigned long long *xa = nullptr;     // [d] x after down (tp > 1: the exchange base before O)
+    unsigned long long *xm = nullptr;     // [d] x after O (tp > 1: the exchange base before down)
+    unsigned long long *q = nullptr;      // [H * hd] q after RoPE
+    unsigned long long *kvnew = nullptr;  // [2][Hkv * hd] this position's K (after RoPE) and V, fp16-rounded
+    unsigned long long *attn = nullptr;   // [H * hd] attention output
+    unsigned long long *h = nullptr;      // [ffn] SwiGLU output
+};
+inline size_t decode_ll_words(const DecodeGeometry &g)
+{
+    return (size_t)2 * g.d + (size_t)2 * g.H * g.hd + (size_t)2 * g.Hkv * g.hd + g.ffn;
+}
 // Device-side synchronization words of a plan (all zero at creation; the
 // kernel keeps them consistent from step to step).
 struct DecodeSync {
-    unsigned *qkv_done = nullptr;   // [nl][kv_heads]
-    unsigned *attn_done = nullptr;  // [nl]
-    unsigned *o_done = nullptr, *gu_done = nullptr, *down_done = nullptr;  // [nl]
-    unsigned *tile_counters = nullptr;  // [max tiles of a phase]
-    unsigned *attn_counters = nullptr;  // [kv_heads]
+    unsigned *attn_counters = nullptr;  // [nl][kv_heads] finished attention partitions
     unsigned *exit_count = nullptr, *abort_flag = nullptr;
     unsigned *logit_tiles = nullptr;
 };
-// Readiness counters of the dataflow decode kernel (zero at plan creation,
-// never reset: each step adds a fixed amount, targets are step multiples).
-struct DecodeDfSync {
-    unsigned *bo = nullptr;       // [nl][d/256] attention-output tiles done per 256-row block (16 per step)
-    unsigned *bgu = nullptr;      // [nl][ffn/256] gate/up tiles done per 256-row block of h (32 per step)
-    unsigned *bdn = nullptr;      // [nl][d/256] down tiles done per 256-row block (16 per step)
-    unsigned *attn_kv = nullptr;  // [nl][kv_heads] attention outputs done per KV head (1 per step)
-};
-inline size_t decode_df_counters(unsigned nl, unsigned d, unsigned ffn, unsigned Hkv)
-{
-    return (size_t)nl * (2 * (d / 256) + ffn / 256 + Hkv);
-}
 struct DecodeLaunch {
     DecodeGeometry g;
     const DecodeLayer *layers = nullptr;  // device array [nl]
@@ -165,11 +162,10 @@ struct DecodeLaunch {
     float eps = 1e-5f, attn_scale = 0.f;
     const float *rope_cos = nullptr, *rope_sin = nullptr;
     unsigned *request = nullptr;  // {token, position, tokens logged, steps, steps with logits}
-    float *xa = nullptr, *xm = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
-    double *ss_o = nullptr, *ss_d = nullptr;  // [d/16] per-tile sums of squares
+    DecodeLL ll;
+    float *logits = nullptr;
     DecodeSync sync;
-    float *partials = nullptr;       // decode_partials_bytes()
-    float *attn_partials = nullptr;  // kv_heads * splits * G * (hd + 2) floats
+    float *attn_partials = nullptr;  // decode_attn_partials_floats()
     unsigned attn_splits = 1;
     unsigned long long *argmax_key = nullptr;
     unsigned *argmax_token = nullptr, *tokens_log = nullptr;
@@ -178,30 +174,24 @@ struct DecodeLaunch {
     int grid = 0;
     unsigned long long *trace = nullptr;  // profiling: [decode_trace_points()][grid] globaltimer ns
     unsigned trace_slots = 0;
-    unsigned long long *wtrace = nullptr;  // profiling: [layers*5 + 1][grid*16][WTRACE_POINTS] per-warp GEMV records
     unsigned ring_bytes = 0;  // per-warp weight ring (0: as much as shared memory allows)
-    int l2_prefetch = 1;      // L2 prefetch of weights: 0 none, 1 the phase after next, 2 the rest of the next phase
-    unsigned ring_pre = 0;    // units requested when a phase's ring starts (0: the whole ring)
     // tensor parallelism (tp > 1): g holds this rank's heads, FFN rows and
     // vocabulary rows (g.V), the d-row phases exchange partial sums
     unsigned tp = 1, tp_rank = 0, vocab0 = 0;
     unsigned char *const *peers = nullptr;  // device array [tp] of exchange regions
     XchgLayout xl;
-    // dataflow kernel (single GPU): set to run it instead of the barrier form
-    DecodeDfSync df;
-    // K and V caches of all layers, layer l at l*kv_heads*capacity*head_dim (optional)
+    // K and V caches of all layers, layer l at l*kv_heads*capacity*head_dim
     __half *kcache = nullptr, *vcache = nullptr;
 };
-// Trace points per CTA of one step: start, per layer 5 x (idle, ready) + 4
-// preparations + attention end, logits (idle, ready, prepared), exit (idle, ready).
-constexpr unsigned WTRACE_POINTS = 8;  // words per warp and GEMV phase of the warp trace
-inline unsigned decode_trace_points(unsigned layers) { return 1 + 15 * layers + 3 + 2; }
+// Trace points per CTA of one step: start, per layer the ends of QKV,
+// attention, O, gate/up and down, the end of the logits, exit.
+inline unsigned decode_trace_points(unsigned layers) { return 1 + 5 * layers + 1 + 1; }
+inline size_t decode_attn_partials_floats(const DecodeGeometry &g)
+{
+    return (size_t)2 * g.Hkv * 16 * (g.H / g.Hkv) * (g.hd + 2);  // two layers' slots, 16 partitions
+}
 int decode_supported(const DecodeGeometry &g, unsigned type_out);
-size_t decode_partials_bytes(const DecodeGeometry &g, int grid);
-unsigned decode_max_tiles(const DecodeGeometry &g);
 int decode_grid(int sms, const DecodeGeometry &g);
-// Whether the dataflow form runs this geometry on `grid` CTAs (single GPU).
-int decode_df_supported(const DecodeGeometry &g, unsigned type_out, int grid);
 int launch_decode(const DecodeLaunch &L, cudaStream_t s);
 
 }  // namespace fyb

@@ -335,14 +335,11 @@ struct Plan {
     int dec_grid = 0;
     DecodeLayer *dec_layers = nullptr;
     DecodeSync dec_sync;
-    float *dec_xm = nullptr, *dec_partials = nullptr, *dec_attn = nullptr;
-    double *dec_ss = nullptr;  // [2][d/16]: per-tile sums of squares after O and after down
+    DecodeLL dec_ll;
+    float *dec_attn = nullptr;
     unsigned dec_splits = 1;
     size_t dec_bytes = 0;
-    unsigned dec_ring_bytes = 6720;  // per-warp weight ring; NYA_CUDA_RING_BYTES (0 = largest)
-    int dec_l2_prefetch = 0;         // NYA_CUDA_L2_PREFETCH: 1 the phase after next into L2, 2 the rest of the next
-    DecodeDfSync dec_df;             // NYA_CUDA_DATAFLOW=1: the dataflow form of the kernel
-    unsigned dec_ring_pre = 0;       // NYA_CUDA_RING_PRE: units requested early per warp (0: whole ring)
+    unsigned dec_ring_bytes = 0;  // per-warp weight ring; NYA_CUDA_RING_BYTES (0 = as much as fits)
     // tensor parallelism: this plan holds rank tp_rank's shard of tp_size
     // (H, Hkv and ffn above are this rank's; V is the whole vocabulary)
     unsigned tp_size = 1, tp_rank = 0, vocab_rows = 0, vocab0 = 0;
@@ -524,20 +521,16 @@ static DecodeLaunch persistent_launch(const Plan *p, StepMode mode)
     L.eps = p->eps; L.attn_scale = 1.0f / std::sqrt((float)p->hd);
     L.rope_cos = p->rope_cos; L.rope_sin = p->rope_sin;
     L.request = p->request;
-    L.xa = p->x[0]; L.xm = p->dec_xm; L.q = p->q; L.attn = p->attn; L.h = p->h; L.logits = p->logits;
-    L.ss_o = p->dec_ss; L.ss_d = p->dec_ss + p->d / 16;
+    L.ll = p->dec_ll;
+    L.logits = p->logits;
     L.sync = p->dec_sync;
-    L.partials = p->dec_partials;
     L.attn_partials = p->dec_attn; L.attn_splits = p->dec_splits;
     L.argmax_key = p->argmax_key; L.argmax_token = p->argmax_token; L.tokens_log = p->tokens_log;
     L.error = p->err_dev;
     L.logits_mode = mode == STEP_NO_LOGITS ? 0 : mode == STEP_GREEDY ? 2 : 1;
     L.grid = p->dec_grid;
     L.ring_bytes = p->dec_ring_bytes;
-    L.l2_prefetch = p->dec_l2_prefetch;
-    L.ring_pre = p->dec_ring_pre;
     L.kcache = p->kcache; L.vcache = p->vcache;
-    L.df = p->dec_df;
     if (p->tp_size > 1) {  // partial sums and logits go through the ranks' exchange regions
         L.tp = p->tp_size; L.tp_rank = p->tp_rank; L.vocab0 = p->vocab0;
         L.peers = p->peers_dev; L.xl = p->xl;
@@ -705,9 +698,6 @@ static bool setup_persistent(Plan *p)
     if (env && !std::strcmp(env, "0")) return true;
     size_t v;
     if (env_size("NYA_CUDA_RING_BYTES", &v)) p->dec_ring_bytes = (unsigned)std::min<size_t>(v, 1u << 20);
-    const char *pf = std::getenv("NYA_CUDA_L2_PREFETCH");
-    if (pf && (!std::strcmp(pf, "1") || !std::strcmp(pf, "2"))) p->dec_l2_prefetch = pf[0] - '0';
-    if (env_size("NYA_CUDA_RING_PRE", &v)) p->dec_ring_pre = (unsigned)std::min<size_t>(v, 64);  // the kernel clamps to the ring
     DecodeGeometry g;
     g.nl = p->nl; g.d = p->d; g.H = p->H; g.Hkv = p->Hkv; g.hd = p->hd; g.ffn = p->ffn; g.V = p->vocab_rows;
     g.capacity = (unsigned)p->capacity;
@@ -722,45 +712,32 @@ static bool setup_persistent(Plan *p)
         p->dec_bytes += bytes;
         return x;
     };
-    const unsigned G = p->H / p->Hkv, dt = p->d / 16;
-    const size_t words = (size_t)p->nl * p->Hkv + 4 * (size_t)p->nl + decode_max_tiles(g) + p->Hkv + 3;
+    const size_t words = (size_t)p->nl * p->Hkv + 3;
     unsigned *w = (unsigned *)A(words * 4);
     std::vector<DecodeLayer> layers(p->nl);
     for (unsigned l = 0; l < p->nl; ++l) {
         DecodeLayer &L = layers[l];
         L.qkv = p->layers[l].qkv; L.o = p->layers[l].o; L.gateup = p->layers[l].gateup; L.down = p->layers[l].down;
         L.attn_norm = p->layers[l].attn_norm; L.ffn_norm = p->layers[l].ffn_norm;
-        L.kcache = p->kcache + (size_t)l * p->Hkv * p->capacity * p->hd;
-        L.vcache = p->vcache + (size_t)l * p->Hkv * p->capacity * p->hd;
     }
     p->dec_layers = (DecodeLayer *)A(layers.size() * sizeof(DecodeLayer));
-    p->dec_xm = (float *)A((size_t)p->d * 4);
-    p->dec_ss = (double *)A((size_t)2 * dt * 8);
-    p->dec_partials = (float *)A(decode_partials_bytes(g, grid));
-    p->dec_splits = (unsigned)std::max(1, std::min(16, grid / (int)p->Hkv));  // decode.cu ATT_MAX_PARTS
-    p->dec_attn = (float *)A((size_t)p->Hkv * p->dec_splits * G * (p->hd + 2) * 4);
+    const size_t llw = decode_ll_words(g);
+    unsigned long long *ll = (unsigned long long *)A(llw * 8);
+    p->dec_splits = (unsigned)std::max(1, std::min(16, grid / (int)p->Hkv));  // decode_kernel.cuh ATT_MAX_PARTS
+    p->dec_attn = (float *)A(decode_attn_partials_floats(g) * 4);
     if (!ok) return false;
     DecodeSync &y = p->dec_sync;
-    y.qkv_done = w; w += (size_t)p->nl * p->Hkv;
-    y.attn_done = w; w += p->nl;
-    y.o_done = w; w += p->nl;
-    y.gu_done = w; w += p->nl;
-    y.down_done = w; w += p->nl;
-    y.tile_counters = w; w += decode_max_tiles(g);
-    y.attn_counters = w; w += p->Hkv;
+    y.attn_counters = w; w += (size_t)p->nl * p->Hkv;
     y.exit_count = w++; y.abort_flag = w++; y.logit_tiles = w++;
-    const char *dfe = std::getenv("NYA_CUDA_DATAFLOW");
-    if (dfe && !std::strcmp(dfe, "1") && p->tp_size == 1 && decode_df_supported(g, p->out_head.type, grid)) {
-        const size_t n = decode_df_counters(p->nl, p->d, p->ffn, p->Hkv);
-        unsigned *c = (unsigned *)A(n * 4);
-        if (!ok || cudaMemsetAsync(c, 0, n * 4, s) != cudaSuccess) return false;
-        DecodeDfSync &f = p->dec_df;
-        f.bo = c; c += (size_t)p->nl * (p->d / 256);
-        f.bdn = c; c += (size_t)p->nl * (p->d / 256);
-        f.bgu = c; c += (size_t)p->nl * (p->ffn / 256);
-        f.attn_kv = c;
-    }
-    if (cudaMemsetAsync(y.qkv_done, 0, words * 4, s) != cudaSuccess ||
+    DecodeLL &b = p->dec_ll;
+    b.xa = ll; ll += p->d;
+    b.xm = ll; ll += p->d;
+    b.q = ll; ll += (size_t)p->H * p->hd;
+    b.kvnew = ll; ll += (size_t)2 * p->Hkv * p->hd;
+    b.attn = ll; ll += (size_t)p->H * p->hd;
+    b.h = ll;
+    if (cudaMemsetAsync(y.attn_counters, 0, words * 4, s) != cudaSuccess ||
+        cudaMemsetAsync(p->dec_ll.xa, 0, llw * 8, s) != cudaSuccess ||
         !upload(p->dec_layers, layers.data(), layers.size() * sizeof(DecodeLayer), s) ||
         cudaStreamSynchronize(s) != cudaSuccess)
         return false;
@@ -1278,7 +1255,7 @@ extern "C" int fyb_plan_decode_form(const void *opaque)
 {
     const Plan *p = (const Plan *)opaque;
     if (!p) return -1;
-    return !p->dec_grid ? 0 : p->dec_df.bo ? 2 : 1;
+    return !p->dec_grid ? 0 : 1;
 }
 
 extern "C" int fyb_plan_tp_info(const void *opaque, unsigned *rank, unsigned *size)
@@ -1345,23 +1322,18 @@ extern "C" long fyb_plan_trace(void *opaque, uint32_t token, size_t position, un
     const unsigned points = decode_trace_points(p->nl);
     const size_t n = (size_t)points * p->dec_grid;
     if (out_count < n) return -1;
+    (void)warp_out; (void)warp_count;  // per-warp records are not kept by this kernel
     DeviceScope scope(p->ctx->device);
     cudaStream_t s = p->ctx->stream;
-    const size_t wn = ((size_t)p->nl * 5 + 1) * p->dec_grid * 16 * WTRACE_POINTS;
-    if (warp_out && warp_count < wn) return -1;
-    unsigned long long *buf = nullptr, *wbuf = nullptr;
+    unsigned long long *buf = nullptr;
     if (cudaMalloc(&buf, n * 8) != cudaSuccess) { cudaGetLastError(); return -1; }
-    if (warp_out && cudaMalloc(&wbuf, wn * 8) != cudaSuccess) { cudaGetLastError(); cudaFree(buf); return -1; }
     DecodeLaunch L = persistent_launch(p, STEP_LOGITS);
-    L.trace = buf; L.trace_slots = points; L.wtrace = wbuf;
+    L.trace = buf; L.trace_slots = points;
     int r = cudaMemsetAsync(buf, 0, n * 8, s) == cudaSuccess &&
-            (!wbuf || cudaMemsetAsync(wbuf, 0, wn * 8, s) == cudaSuccess) &&
             set_request(p, token, (unsigned)position) == 0 &&
             launch_decode(L, s) == 0 && cudaMemcpyAsync(out, buf, n * 8, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
-            (!wbuf || cudaMemcpyAsync(warp_out, wbuf, wn * 8, cudaMemcpyDeviceToHost, s) == cudaSuccess) &&
             cudaStreamSynchronize(s) == cudaSuccess && !*(volatile unsigned *)p->err_host ? 0 : -1;
     cudaFree(buf);
-    if (wbuf) cudaFree(wbuf);
     if (r) return plan_fail(p, position);
     p->valid = std::max(p->valid, position + 1);
     if (grid_out) *grid_out = (unsigned)p->dec_grid;
