@@ -541,11 +541,13 @@ def run_trace_mode(args):
         raise SystemExit("8B plan or prefill failed")
     tr = None
     for i in range(args.trace_step):  # the last traced step is reported (earlier ones warm up)
-        tr = plan.trace(17 + i, PROMPT + i)
-        if tr is None:
+        res = plan.trace(17 + i, PROMPT + i, detail=bool(args.trace_raw))
+        if res is None:
             raise SystemExit("trace failed (persistent kernel not in use?)")
+        tr = res[0] if args.trace_raw else res
     if args.trace_raw:
         np.save(args.trace_raw, tr)
+        np.save(args.trace_raw.replace(".npy", "") + "_detail.npy", res[1])
     res = summarize_trace(tr, model.config.layers)
     step = res.pop("step_us")
     print(json.dumps({"trace_us": res, "step_us": step, "grid": int(tr.shape[1]), "points": int(tr.shape[0])}))

@@ -16,7 +16,7 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libfyodor_b200.so")
+LIB_PATH = os.environ.get("FYB_LIBRARY") or os.path.join(HERE, "libfyodor_b200.so")  # override: another build
 
 # GGML storage ids (backend/core/llm_internal.h:11-19)
 F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 2, 8, 12, 14, 30
@@ -341,20 +341,27 @@ class Plan:
         """Decline every later step without launching (another rank failed)."""
         return lib.fyb_plan_tp_disconnect(C.c_void_p(self.ptr))
 
-    def trace(self, token, position):
+    def trace(self, token, position, detail=False):
         """Per-CTA trace points of one persistent decode step: array
         [points][grid] of globaltimer nanoseconds (start, then per layer the
         ends of QKV, attention, O, gate/up and down, the end of the logits,
-        exit), or None."""
+        exit), or None. With detail=True, a pair (that array, per-warp
+        records of layer layers // 2 [grid][16][32], decode_kernel.cuh)."""
         grid = C.c_uint(0)
         L = self.model.config.layers
         points = 1 + 5 * L + 2
         n = points * 1024
         out = np.zeros(n, np.uint64)
-        r = lib.fyb_plan_trace(C.c_void_p(self.ptr), token, position, _ptr(out), n, C.byref(grid), None, 0)
+        wn = 1024 * 16 * 32
+        wout = np.zeros(wn, np.uint64) if detail else None
+        r = lib.fyb_plan_trace(C.c_void_p(self.ptr), token, position, _ptr(out), n, C.byref(grid),
+                               _ptr(wout) if detail else None, wn if detail else 0)
         if r < 0:
             return None
-        return out[: r * grid.value].reshape(r, grid.value)
+        cta = out[: r * grid.value].reshape(r, grid.value)
+        if not detail:
+            return cta
+        return cta, wout[: grid.value * 16 * 32].reshape(grid.value, 16, 32)
 
     def profile(self, token, position, steps):
         """Per-class milliseconds of one decode step: matrix, attention, other."""

@@ -95,7 +95,7 @@ int launch_decode(const DecodeLaunch &L, cudaStream_t s)
     p.logits_mode = L.logits_mode;
     p.ring_bytes = ring_bytes_for(L.g, L.ring_bytes);
     p.kcache = L.kcache; p.vcache = L.vcache;
-    p.trace = L.trace; p.trace_slots = L.trace_slots;
+    p.trace = L.trace; p.trace_slots = L.trace_slots; p.dtrace = L.dtrace;
     p.tp = L.tp; p.tp_rank = L.tp_rank; p.vocab0 = L.vocab0; p.peers = L.peers; p.xl = L.xl;
     if (p.ring_bytes < 2 * Q6_UNIT || !p.kcache || !p.vcache) return -1;  // every unit size needs two ring slots
     const size_t smem = decode_smem_bytes(L.g, L.ring_bytes);

@@ -47,11 +47,16 @@
 namespace fyb {
 
 constexpr unsigned WAIT_LIMIT = 1u << 22;  // polls (with a short sleep) before ERR_TIMEOUT
+constexpr unsigned POLL_NS_MAX = 256;      // poll back-off: sleeps double from 16 ns up to this
 constexpr unsigned RING_BARS = 8;          // mbarriers (max units in flight) per warp
 constexpr unsigned CHUNK = 8;              // tiles per reduction chunk
 constexpr unsigned LIMB_STRIDE = 256 + QG_XPAD;  // limb-row stride of a one-block slot (64 mod 128)
 constexpr unsigned LIMB_SLOT = 4 * LIMB_STRIDE + 16 + 32 + 16;  // 4 limb rows | exponent | 8 group sums | pad
 constexpr unsigned NORM_BLOCKS_MAX = 64;   // 256-value blocks of a normalized input (d <= 16384)
+constexpr unsigned DTRACE_POINTS = 32;     // per-warp detail records (profiling)
+#ifndef FYB_PAIR_UNITS
+#define FYB_PAIR_UNITS 0                    // two units of one block per step (build flag for comparisons)
+#endif
 
 typedef unsigned long long u64;
 
@@ -78,6 +83,8 @@ struct DecodeParams {
     unsigned ring_bytes;        // per warp, a multiple of 16
     unsigned long long *trace;  // optional [point][CTA] globaltimer values
     unsigned trace_slots;
+    unsigned long long *dtrace; // optional [CTA][warp][DTRACE_POINTS] records of layer nl / 2
+
     // tensor parallelism (tp > 1): H, Hkv, ffn and V above are this rank's
     unsigned tp, tp_rank, vocab0;
     unsigned char *const *peers;  // [tp] exchange regions, this rank's at tp_rank
@@ -148,10 +155,12 @@ FYB_DEV bool reached(unsigned value, unsigned target) { return (int)(value - tar
 FYB_DEV bool ll_wait1(const DecodeParams &p, const u64 *src, unsigned tag, float &v)
 {
     u64 w = ll_get(src);
+    unsigned ns = 16;
     for (unsigned i = 0; !ll_ok(w, tag); ++i) {
         if (i >= WAIT_LIMIT) { raise_abort(p, ERR_TIMEOUT); return false; }
         if (aborted(p)) return false;
-        __nanosleep(20);
+        __nanosleep(ns);
+        ns = min(ns * 2, POLL_NS_MAX);
         w = ll_get(src);
     }
     v = ll_val(w);
@@ -166,6 +175,7 @@ FYB_DEV bool ll_wait8(const DecodeParams &p, const u64 *src, unsigned tag, float
     u64 r[8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) ll_get2(src + 2 * i, r[2 * i], r[2 * i + 1]);
+    unsigned ns = 16;
     for (unsigned it = 0;; ++it) {
         bool ok = true;
 #pragma unroll
@@ -176,7 +186,8 @@ FYB_DEV bool ll_wait8(const DecodeParams &p, const u64 *src, unsigned tag, float
             return false;
         }
         if (warp_aborted(p)) return false;
-        __nanosleep(20);
+        __nanosleep(ns);
+        ns = min(ns * 2, POLL_NS_MAX);
         if (!ok) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) ll_get2(src + 2 * i, r[2 * i], r[2 * i + 1]);
@@ -199,6 +210,22 @@ FYB_DEV unsigned long long globaltimer()
 FYB_DEV void stamp(const DecodeParams &p, unsigned ts)
 {
     if (p.trace && threadIdx.x == 0 && ts < p.trace_slots) p.trace[(size_t)ts * gridDim.x + blockIdx.x] = globaltimer();
+}
+
+// Profiling detail of one layer (nl / 2), lane 0 of every warp: per GEMV
+// phase kind k (QKV, O, gate/up, down) at 6k: entry (ns), first input block
+// prepared (ns), SM cycles waiting for weights, SM cycles preparing inputs,
+// units done (ns), outputs done (ns); attention (warp 0) at 24: entry, first
+// item's inputs polled, first item published, merge done (ns, 0 if none),
+// phase end.
+#ifndef FYB_DETAIL_TRACE
+#define FYB_DETAIL_TRACE 0  // build flag: per-warp detail records (registers and branches in the unit loop)
+#endif
+FYB_DEV bool dtraced(const DecodeParams &p, unsigned l) { return FYB_DETAIL_TRACE && p.dtrace && l == p.nl / 2; }
+FYB_DEV void drecord(const DecodeParams &p, unsigned point, unsigned long long v)
+{
+    if ((threadIdx.x & 31) == 0)
+        p.dtrace[((size_t)blockIdx.x * QG_WARPS + (threadIdx.x >> 5)) * DTRACE_POINTS + point] = v;
 }
 
 // ------------------------------------------------------------ phases
@@ -241,7 +268,7 @@ FYB_DEV void cta_tiles(const Phase &ph, unsigned &tb, unsigned &te)
 // A warp's units of one phase: chunk by chunk, and inside chunk c (Tc tiles)
 // the units u = b * Tc + t in [Uc * w / W, Uc * (w + 1) / W), Uc = nblk * Tc.
 struct Walk {
-    unsigned T, nblk, c, k, e, Tc;
+    unsigned T, nblk, c, k, e, Tc, b, t;  // (b, t): block and chunk-local tile of unit k
 };
 
 FYB_DEV void walk_chunk(Walk &wk, unsigned warp)
@@ -250,12 +277,14 @@ FYB_DEV void walk_chunk(Walk &wk, unsigned warp)
     const unsigned Uc = wk.Tc * wk.nblk;
     wk.k = Uc * warp / QG_WARPS;
     wk.e = Uc * (warp + 1) / QG_WARPS;
+    wk.b = wk.k / wk.Tc;
+    wk.t = wk.k - wk.b * wk.Tc;
 }
 
 FYB_DEV void walk_begin(Walk &wk, unsigned T, unsigned nblk, unsigned warp)
 {
     wk.T = T; wk.nblk = nblk; wk.c = 0;
-    wk.k = wk.e = wk.Tc = 0;
+    wk.k = wk.e = wk.Tc = wk.b = wk.t = 0;
     if (T) walk_chunk(wk, warp);
 }
 
@@ -267,9 +296,10 @@ FYB_DEV bool walk_next(Walk &wk, unsigned warp, unsigned &t, unsigned &b)
         ++wk.c;
         walk_chunk(wk, warp);
     }
-    b = wk.k / wk.Tc;
-    t = wk.c * CHUNK + (wk.k - b * wk.Tc);
+    b = wk.b;
+    t = wk.c * CHUNK + wk.t;
     ++wk.k;
+    if (++wk.t == wk.Tc) { wk.t = 0; ++wk.b; }
     return true;
 }
 
@@ -288,54 +318,66 @@ FYB_DEV unsigned walk_count(unsigned T, unsigned nblk, unsigned warp)
 // units; unit k of the phase goes to slot k % S. Bit s of `par` is the
 // parity the next wait on mbarrier s expects. The ring is empty between
 // phases, so each phase may use its own unit size.
+// The issue side of a warp's ring, kept in shared memory: only lane 0 forms
+// copy addresses, so these words take no registers in the unit loop.
+struct RingIssue {
+    const unsigned char *src;
+    unsigned tb, nblk, ub;
+    Walk iw;  // issue cursor
+};
+
 struct Ring {
     unsigned char *base;
     uint64_t *bars;
+    RingIssue *is;    // this warp's issue state (shared memory)
     unsigned bytes, par;
-    unsigned S, ub, issued, consumed, n, tb;
-    const unsigned char *src;
-    unsigned nblk;
-    Walk iw;  // issue cursor
+    unsigned S, ub, issued, consumed, n;
+    unsigned si, sc;  // slots of the next issue and the next consumption (issued % S, consumed % S)
 };
 
 FYB_DEV void ring_issue(Ring &r, unsigned lane)
 {
-    unsigned t = 0, b = 0;
-    walk_next(r.iw, threadIdx.x >> 5, t, b);
-    const unsigned slot = r.issued % r.S;
+    const unsigned slot = r.si;
     if (lane == 0) {
-        fence_proxy_async();
-        mbar_expect_tx(r.bars + slot, r.ub);
-        bulk_copy_g2s(r.base + slot * r.ub, r.src + ((unsigned long long)(r.tb + t) * r.nblk + b) * r.ub, r.ub,
+        RingIssue &q = *r.is;
+        unsigned t = 0, b = 0;
+        walk_next(q.iw, threadIdx.x >> 5, t, b);
+        mbar_expect_tx(r.bars + slot, q.ub);
+        bulk_copy_g2s(r.base + slot * q.ub, q.src + ((unsigned long long)(q.tb + t) * q.nblk + b) * q.ub, q.ub,
                       r.bars + slot);
     }
     ++r.issued;
+    if (++r.si == r.S) r.si = 0;
 }
 
 // Start a phase on an empty ring: this warp's units and its first S copies.
 FYB_DEV void ring_begin(const Phase &ph, Ring &r, unsigned lane)
 {
-    unsigned te;
-    cta_tiles(ph, r.tb, te);
+    unsigned tb, te;
+    cta_tiles(ph, tb, te);
     const unsigned warp = threadIdx.x >> 5;
-    r.nblk = ph.nblk;
-    r.n = walk_count(te - r.tb, ph.nblk, warp);
-    walk_begin(r.iw, te - r.tb, ph.nblk, warp);
+    r.n = walk_count(te - tb, ph.nblk, warp);
     r.ub = unit_bytes(ph.w.type);
     r.S = min(RING_BARS, r.bytes / r.ub);
-    r.src = ph.w.units;
+    if (lane == 0) {
+        RingIssue &q = *r.is;
+        q.src = ph.w.units; q.tb = tb; q.nblk = ph.nblk; q.ub = r.ub;
+        walk_begin(q.iw, te - tb, ph.nblk, warp);
+    }
     r.issued = r.consumed = 0;
+    r.si = r.sc = 0;
     while (r.issued < r.n && r.issued < r.S) ring_issue(r, lane);
 }
 
 // Wait for the next unit; its shared-memory address, or null on timeout.
 FYB_DEV const unsigned char *ring_wait(Ring &r)
 {
-    const unsigned slot = r.consumed % r.S;
+    const unsigned slot = r.sc;
     const bool landed = mbar_wait_bounded(r.bars + slot, (r.par >> slot) & 1u);
     if (!__all_sync(0xffffffffu, landed)) return nullptr;
     r.par ^= 1u << slot;
     ++r.consumed;
+    if (++r.sc == r.S) r.sc = 0;
     return r.base + slot * r.ub;
 }
 
@@ -616,6 +658,11 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, R
     double *bss = cta.bss + (pseq & 1) * NORM_BLOCKS_MAX;
     bool ok = true;
     unsigned cur_b = ~0u;
+    BlockConst bc;
+    const bool dt = dtraced(p, ph.layer) && ph.kind != PH_LOGITS;
+    const unsigned dbase = ph.kind * 6;
+    long long wait_cycles = 0, prep_cycles = 0;
+    if (dt) drecord(p, dbase, globaltimer());
     if (r.n == 0 && !warp_aborted(p)) ring_next(p, ph, r, lane);  // no units here: only the next ring
     if (T == 0) return __syncthreads_or(aborted(p)) == 0;  // keeps the CTA's phases in step (bss, parts)
     for (unsigned c = 0; c * CHUNK < T; ++c) {
@@ -624,30 +671,69 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, R
         walk_chunk(wk, warp);
         const unsigned Tc = wk.Tc;
         float *parts = cta.parts + (size_t)(seq & 1) * CHUNK * QG_WARPS * 16;
+        // the abort word is read here and used at the chunk barrier, so its
+        // load is not in front of the barrier (a failure of this thread since
+        // the last barrier raised it, and this thread sees its own store)
+        const bool abort_seen = lane == 0 && aborted(p);
         // this warp's partial rows of the chunk's tiles start at zero
         for (unsigned i = lane; i < Tc * 16; i += 32) parts[((i >> 4) * QG_WARPS + warp) * 16 + (i & 15)] = 0.f;
         __syncwarp();
-        for (unsigned k = wk.k; k < wk.e && ok; ++k) {
-            const unsigned b = k / Tc, t = k - b * Tc;
+        {
+        unsigned b = wk.b, t = wk.t;
+        for (unsigned k = wk.k; k < wk.e && ok;) {
             if (b != cur_b) {
+                const long long c0 = dt ? clock64() : 0;
                 ok = prep_block(p, ph, b, step, slot, bss, lane);
+                if (dt) {
+                    prep_cycles += clock64() - c0;
+                    if (cur_b == ~0u) drecord(p, dbase + 1, globaltimer());
+                }
                 cur_b = b;
                 if (!ok) break;
+                bc = block_const(slot.exps, slot.gsums, lane);
             }
-            const unsigned char *unit = ring_wait(r);
-            if (!unit) { if (lane == 0) raise_abort(p, ERR_TIMEOUT); ok = false; break; }
-            float accA = 0.f, accB = 0.f;
-            compute_unit<TYPE, 1>(unit, 0, slot.xl, LIMB_STRIDE, slot.exps, 1, slot.gsums, 8, lane, accA, accB);
+            // two units of the same block share the x fragments
+            const bool two = FYB_PAIR_UNITS && k + 1 < wk.e && t + 1 < Tc;
+            const long long w0 = dt ? clock64() : 0;
+            const unsigned char *u0 = ring_wait(r);
+            const unsigned char *u1 = two && u0 ? ring_wait(r) : u0;
+            if (dt) wait_cycles += clock64() - w0;
+            if (!u0 || !u1) { if (lane == 0) raise_abort(p, ERR_TIMEOUT); ok = false; break; }
+            float acc[2][2];
+            if (two) {
+                const unsigned char *const uu[2] = {u0, u1};
+                compute_units<TYPE, 2>(uu, slot.xl, LIMB_STRIDE, bc, lane, acc);
+            } else {
+                const unsigned char *const uu[1] = {u0};
+                float a1[1][2];
+                compute_units<TYPE, 1>(uu, slot.xl, LIMB_STRIDE, bc, lane, a1);
+                acc[0][0] = a1[0][0]; acc[0][1] = a1[0][1];
+            }
             __syncwarp();
             if (r.issued < r.n) ring_issue(r, lane);
-            const float yA = lane_total<1>(accA), yB = lane_total<1>(accB);
-            if (tig == 0) {
-                float *row = parts + (t * QG_WARPS + warp) * 16;
-                row[gid] += yA;
-                row[gid + 8] += yB;
+            if (two && r.issued < r.n) ring_issue(r, lane);
+#pragma unroll
+            for (int n = 0; n < 2; ++n) {
+                if (n == 1 && !two) break;
+                const float yA = lane_total<1>(acc[n][0]), yB = lane_total<1>(acc[n][1]);
+                if (tig == 0) {
+                    float *row = parts + ((t + n) * QG_WARPS + warp) * 16;
+                    row[gid] += yA;
+                    row[gid + 8] += yB;
+                }
             }
+            const unsigned adv = two ? 2u : 1u;
+            k += adv;
+            t += adv;
+            if (t == Tc) { t = 0; ++b; }
             // the ring is empty after this warp's last unit: the next phase's weights start now
             if (r.consumed == r.n && !warp_aborted(p)) ring_next(p, ph, r, lane);
+        }
+        }
+        if (dt && (c + 1) * CHUNK >= T) {
+            drecord(p, dbase + 2, (unsigned long long)wait_cycles);
+            drecord(p, dbase + 3, (unsigned long long)prep_cycles);
+            drecord(p, dbase + 4, globaltimer());
         }
         // reducer threads (t * 8 + j) read their residual rows before the barrier
         const unsigned i = threadIdx.x, t = i >> 3, j = i & 7;
@@ -658,7 +744,7 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, R
         const unsigned rA = (tb + c * CHUNK + t) * 16 + j;
         if (reducer && resid) { ra = ll_get(rsrc + rA); rb = ll_get(rsrc + rA + 8); }
         // every failure raised the abort word before this barrier
-        if (__syncthreads_or(!ok || aborted(p))) return false;
+        if (__syncthreads_or(!ok || abort_seen)) return false;
         if (reducer) {
             float yA = 0.f, yB = 0.f;
 #pragma unroll 4
@@ -686,6 +772,7 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, R
         }
         ++seq;
     }
+    if (dt) drecord(p, dbase + 5, globaltimer());
     return true;
 }
 
@@ -774,6 +861,8 @@ FYB_DEV bool attention_item(const DecodeParams &p, unsigned step, unsigned l, un
         sm.qkv[i] = v;
     }
     if (__syncthreads_or(!ok)) return false;
+    const bool dt = dtraced(p, l) && warp == 0 && sp + kvh * S == blockIdx.x;  // the CTA's first item
+    if (dt) drecord(p, 25, globaltimer());
     float qr[G][DPL], knew[DPL], vnew[DPL];
 #pragma unroll
     for (int g = 0; g < G; ++g)
@@ -850,65 +939,99 @@ FYB_DEV bool attention_item(const DecodeParams &p, unsigned step, unsigned l, un
         for (int e = 0; e < DPL; ++e) sm.wo[(warp * G + g) * HD + lane * DPL + e] = o[g][e];
     }
     __syncthreads();
+    // the CTA's partial result: per query head its maximum, sum and
+    // unnormalized output, merged over the warps in warp order; thread i
+    // owns output elements i + r * QG_THREADS
     constexpr unsigned SLOT = G * (HD + 2);
-    // partition slots alternate between layers; counters are per layer and
-    // reset by the merging CTA (read again only in the next step's launch)
-    float *const parts_l = p.attn_partials + (size_t)(l & 1) * p.Hkv * ATT_MAX_PARTS * SLOT;
-    unsigned *const counter = p.sync.attn_counters + (size_t)l * p.Hkv + kvh;
-    float *slot = parts_l + ((size_t)kvh * S + sp) * SLOT;
-    for (unsigned i = threadIdx.x; i < G * HD; i += QG_THREADS) {
-        const unsigned g = i / HD, dd = i % HD;
-        float M = -INFINITY;
-        for (int w = 0; w < QG_WARPS; ++w) M = fmaxf(M, sm.wm[w * G + g]);
-        float acc = 0.f, den = 0.f;
-        for (int w = 0; w < QG_WARPS; ++w) {
-            const float wmv = sm.wm[w * G + g];
-            const float f = wmv == -INFINITY ? 0.f : expf(wmv - M);
-            acc = fmaf(sm.wo[(w * G + g) * HD + dd], f, acc);
-            den = fmaf(sm.wl[w * G + g], f, den);
-        }
-        slot[g * (HD + 2) + dd] = acc;
-        if (dd == 0) { slot[g * (HD + 2) + HD] = M; slot[g * (HD + 2) + HD + 1] = den; }
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) *sm.flag = atomicAdd(counter, 1u) == S - 1;
-    __syncthreads();
-    if (!*sm.flag) return true;
-    __threadfence();
-    // merge the S slots: their maxima and sums staged in shared memory (one
-    // round of loads), then every output element loads its S values at once
-    const float *all = parts_l + (size_t)kvh * S * SLOT;
-    if (threadIdx.x == 0) *counter = 0;
-    float *sM = sm.wo, *sD = sm.wo + ATT_MAX_PARTS * G;
-    for (unsigned i = threadIdx.x; i < S * G; i += QG_THREADS) {
-        const unsigned s2 = i / G, g = i % G;
-        sM[i] = __ldcg(all + s2 * SLOT + g * (HD + 2) + HD);
-        sD[i] = __ldcg(all + s2 * SLOT + g * (HD + 2) + HD + 1);
-    }
-    __syncthreads();
-    for (unsigned i = threadIdx.x; i < G * HD; i += QG_THREADS) {
-        const unsigned g = i / HD, dd = i % HD;
-        float v[ATT_MAX_PARTS];
+    constexpr unsigned EPT = (G * HD + QG_THREADS - 1) / QG_THREADS;  // elements per thread (1 or 2)
+    u64 *const parts_all = reinterpret_cast<u64 *>(p.attn_partials) + (size_t)kvh * ATT_MAX_PARTS * SLOT;
+    float acc0[EPT], M0[EPT], den0[EPT];
 #pragma unroll
-        for (unsigned s2 = 0; s2 < ATT_MAX_PARTS; ++s2)
-            v[s2] = s2 < S ? __ldcg(all + s2 * SLOT + g * (HD + 2) + dd) : 0.f;
+    for (unsigned r = 0; r < EPT; ++r) {
+        const unsigned e = threadIdx.x + r * QG_THREADS, g = e / HD, dd = e % HD;
+        acc0[r] = 0.f; M0[r] = -INFINITY; den0[r] = 0.f;
+        if (e < G * HD) {
+            for (int w = 0; w < QG_WARPS; ++w) M0[r] = fmaxf(M0[r], sm.wm[w * G + g]);
+            for (int w = 0; w < QG_WARPS; ++w) {
+                const float wmv = sm.wm[w * G + g];
+                const float f = wmv == -INFINITY ? 0.f : expf(wmv - M0[r]);
+                acc0[r] = fmaf(sm.wo[(w * G + g) * HD + dd], f, acc0[r]);
+                den0[r] = fmaf(sm.wl[w * G + g], f, den0[r]);
+            }
+        }
+    }
+    if (sp != 0) {
+        // partitions after the first publish their result as tagged words;
+        // the first partition's CTA merges them
+        u64 *slot = parts_all + (size_t)sp * SLOT;
+#pragma unroll
+        for (unsigned r = 0; r < EPT; ++r) {
+            const unsigned e = threadIdx.x + r * QG_THREADS, g = e / HD, dd = e % HD;
+            if (e < G * HD) {
+                ll_put(slot + g * (HD + 2) + dd, acc0[r], tag);
+                if (dd == 0) {
+                    ll_put(slot + g * (HD + 2) + HD, M0[r], tag);
+                    ll_put(slot + g * (HD + 2) + HD + 1, den0[r], tag);
+                }
+            }
+        }
+        if (dt) drecord(p, 26, globaltimer());
+        __syncthreads();  // the shared scratch is free again
+        return true;
+    }
+    if (dt) drecord(p, 26, globaltimer());
+    // merge: the partitions' maxima and sums polled into shared memory (one
+    // word per thread), then every output element polls its S - 1 values;
+    // the sums run in partition order
+    __syncthreads();  // every thread has read the warps' outputs
+    float *sM = sm.wo, *sD = sm.wo + ATT_MAX_PARTS * G;
+    bool mok = true;
+#pragma unroll
+    for (unsigned r = 0; r < EPT; ++r) {
+        const unsigned e = threadIdx.x + r * QG_THREADS, g = e / HD, dd = e % HD;
+        if (e < G * HD && dd == 0) { sM[g] = M0[r]; sD[g] = den0[r]; }
+    }
+    for (unsigned i = threadIdx.x; i < (S - 1) * G * 2; i += QG_THREADS) {
+        const unsigned s2 = 1 + i / (2 * G), gg = (i / 2) % G, w2 = i & 1;
+        float v = 0.f;
+        mok = mok && ll_wait1(p, parts_all + (size_t)s2 * SLOT + gg * (HD + 2) + HD + w2, tag, v);
+        (w2 ? sD : sM)[s2 * G + gg] = v;
+    }
+    if (__syncthreads_or(!mok)) return false;
+#pragma unroll
+    for (unsigned r = 0; r < EPT; ++r) {
+        const unsigned e = threadIdx.x + r * QG_THREADS, g = e / HD, dd = e % HD;
+        if (e >= G * HD) continue;
         float M = -INFINITY;
         for (unsigned s2 = 0; s2 < S; ++s2) M = fmaxf(M, sM[s2 * G + g]);
         float acc = 0.f, den = 0.f;
+        // partitions in order, four loads in flight at a time
+        for (unsigned s0 = 0; s0 < S; s0 += 4) {
+            u64 w[4];
 #pragma unroll
-        for (unsigned s2 = 0; s2 < ATT_MAX_PARTS; ++s2) {
-            if (s2 < S) {
+            for (unsigned j = 0; j < 4; ++j) {
+                const unsigned s2 = s0 + j;
+                w[j] = s2 == 0 ? ll_pack(acc0[r], tag)
+                     : s2 < S ? ll_get(parts_all + (size_t)s2 * SLOT + g * (HD + 2) + dd) : ll_pack(0.f, tag);
+            }
+#pragma unroll
+            for (unsigned j = 0; j < 4; ++j) {
+                const unsigned s2 = s0 + j;
+                if (s2 >= S) break;
+                float v;
+                if (ll_ok(w[j], tag)) v = ll_val(w[j]);
+                else if (!ll_wait1(p, parts_all + (size_t)s2 * SLOT + g * (HD + 2) + dd, tag, v)) mok = false;
                 const float ms = sM[s2 * G + g];
                 const float f = ms == -INFINITY ? 0.f : expf(ms - M);
-                acc = fmaf(v[s2], f, acc);
+                acc = fmaf(v, f, acc);
                 den = fmaf(sD[s2 * G + g], f, den);
             }
         }
         ll_put(p.ll.attn + ((size_t)kvh * G + g) * HD + dd, acc / den, tag);
     }
-    __syncthreads();
-    return true;
+    if (dt) drecord(p, 27, globaltimer());
+    // a failed wait raised the abort word; the caller's barrier sees it
+    return __syncthreads_or(!mok) == 0;
 }
 
 template <int HD, int G>
@@ -923,7 +1046,7 @@ FYB_DEV bool attention_phase(const DecodeParams &p, unsigned step, unsigned l, c
 
 // ------------------------------------------------------------ the kernel
 struct SmemLayout {
-    size_t rings, bars, uni, parts, bss, keys, misc, total;
+    size_t rings, bars, uni, parts, bss, keys, issue, misc, total;
 };
 
 // Everything but the rings; the rings take what is left of the 227 KB. The
@@ -940,7 +1063,8 @@ FYB_HOST_DEV SmemLayout smem_layout(unsigned H, unsigned Hkv, unsigned hd, unsig
     s.parts = s.uni + ((limbs > abytes ? limbs : abytes) + 15) / 16 * 16;
     s.bss = s.parts + (size_t)2 * CHUNK * QG_WARPS * 16 * 4;
     s.keys = s.bss + (size_t)2 * NORM_BLOCKS_MAX * 8;
-    s.misc = s.keys + (size_t)QG_WARPS * 8;
+    s.issue = s.keys + (size_t)QG_WARPS * 8;
+    s.misc = s.issue + ((size_t)QG_WARPS * sizeof(RingIssue) + 15) / 16 * 16;
     s.total = s.misc + 16;
     return s;
 }
@@ -1035,6 +1159,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
     ring.base = smem + lay.rings + (size_t)warp * p.ring_bytes;
     ring.bars = reinterpret_cast<uint64_t *>(smem + lay.bars) + warp * RING_BARS;
     ring.bytes = p.ring_bytes;
+    ring.is = reinterpret_cast<RingIssue *>(smem + lay.issue) + warp;
     ring.par = 0;
     ring.issued = ring.consumed = ring.n = 0;
     const LimbSlot slot = limb_slot(smem + lay.uni, warp);
@@ -1066,8 +1191,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
     for (unsigned l = 0; l < p.nl && ok; ++l) {
         for (unsigned k = 0; k < 5 && ok; ++k) {
             if (k == 1) {  // attention; its scratch overlays the limb slots, so all warps leave it together
+                if (dtraced(p, l) && warp == 0) drecord(p, 24, globaltimer());
                 ok = attention_phase<HD, G>(p, step, l, as);
                 ok = __syncthreads_or(!ok || aborted(p)) == 0;
+                if (dtraced(p, l) && warp == 0) drecord(p, 28, globaltimer());
             } else {
                 ok = run_gemv(p, cur, step, ring, slot, cta, lane, seq, pseq++, key);
                 Phase nx;

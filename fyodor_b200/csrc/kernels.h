@@ -147,7 +147,6 @@ inline size_t decode_ll_words(const DecodeGeometry &g)
 // Device-side synchronization words of a plan (all zero at creation; the
 // kernel keeps them consistent from step to step).
 struct DecodeSync {
-    unsigned *attn_counters = nullptr;  // [nl][kv_heads] finished attention partitions
     unsigned *exit_count = nullptr, *abort_flag = nullptr;
     unsigned *logit_tiles = nullptr;
 };
@@ -174,6 +173,7 @@ struct DecodeLaunch {
     int grid = 0;
     unsigned long long *trace = nullptr;  // profiling: [decode_trace_points()][grid] globaltimer ns
     unsigned trace_slots = 0;
+    unsigned long long *dtrace = nullptr;  // profiling: [grid][16 warps][decode_dtrace_points()] of layer nl / 2
     unsigned ring_bytes = 0;  // per-warp weight ring (0: as much as shared memory allows)
     // tensor parallelism (tp > 1): g holds this rank's heads, FFN rows and
     // vocabulary rows (g.V), the d-row phases exchange partial sums
@@ -186,9 +186,13 @@ struct DecodeLaunch {
 // Trace points per CTA of one step: start, per layer the ends of QKV,
 // attention, O, gate/up and down, the end of the logits, exit.
 inline unsigned decode_trace_points(unsigned layers) { return 1 + 5 * layers + 1 + 1; }
+inline unsigned decode_dtrace_points() { return 32; }
+inline size_t decode_dtrace_words(int grid) { return (size_t)grid * 16 * decode_dtrace_points(); }  // 16 warps per CTA
+// Attention partition results: kv_heads x 16 partitions x G x (hd + 2)
+// tagged 8-byte words (two floats each).
 inline size_t decode_attn_partials_floats(const DecodeGeometry &g)
 {
-    return (size_t)2 * g.Hkv * 16 * (g.H / g.Hkv) * (g.hd + 2);  // two layers' slots, 16 partitions
+    return (size_t)2 * g.Hkv * 16 * (g.H / g.Hkv) * (g.hd + 2);
 }
 int decode_supported(const DecodeGeometry &g, unsigned type_out);
 int decode_grid(int sms, const DecodeGeometry &g);

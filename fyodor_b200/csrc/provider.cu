@@ -712,7 +712,7 @@ static bool setup_persistent(Plan *p)
         p->dec_bytes += bytes;
         return x;
     };
-    const size_t words = (size_t)p->nl * p->Hkv + 3;
+    const size_t words = 3;
     unsigned *w = (unsigned *)A(words * 4);
     std::vector<DecodeLayer> layers(p->nl);
     for (unsigned l = 0; l < p->nl; ++l) {
@@ -727,7 +727,6 @@ static bool setup_persistent(Plan *p)
     p->dec_attn = (float *)A(decode_attn_partials_floats(g) * 4);
     if (!ok) return false;
     DecodeSync &y = p->dec_sync;
-    y.attn_counters = w; w += (size_t)p->nl * p->Hkv;
     y.exit_count = w++; y.abort_flag = w++; y.logit_tiles = w++;
     DecodeLL &b = p->dec_ll;
     b.xa = ll; ll += p->d;
@@ -736,8 +735,9 @@ static bool setup_persistent(Plan *p)
     b.kvnew = ll; ll += (size_t)2 * p->Hkv * p->hd;
     b.attn = ll; ll += (size_t)p->H * p->hd;
     b.h = ll;
-    if (cudaMemsetAsync(y.attn_counters, 0, words * 4, s) != cudaSuccess ||
+    if (cudaMemsetAsync(y.exit_count, 0, words * 4, s) != cudaSuccess ||
         cudaMemsetAsync(p->dec_ll.xa, 0, llw * 8, s) != cudaSuccess ||
+        cudaMemsetAsync(p->dec_attn, 0, decode_attn_partials_floats(g) * 4, s) != cudaSuccess ||
         !upload(p->dec_layers, layers.data(), layers.size() * sizeof(DecodeLayer), s) ||
         cudaStreamSynchronize(s) != cudaSuccess)
         return false;
@@ -1322,17 +1322,22 @@ extern "C" long fyb_plan_trace(void *opaque, uint32_t token, size_t position, un
     const unsigned points = decode_trace_points(p->nl);
     const size_t n = (size_t)points * p->dec_grid;
     if (out_count < n) return -1;
-    (void)warp_out; (void)warp_count;  // per-warp records are not kept by this kernel
+    const size_t wn = decode_dtrace_words(p->dec_grid);
+    if (warp_out && warp_count < wn) return -1;
     DeviceScope scope(p->ctx->device);
     cudaStream_t s = p->ctx->stream;
-    unsigned long long *buf = nullptr;
+    unsigned long long *buf = nullptr, *wbuf = nullptr;
     if (cudaMalloc(&buf, n * 8) != cudaSuccess) { cudaGetLastError(); return -1; }
+    if (warp_out && cudaMalloc(&wbuf, wn * 8) != cudaSuccess) { cudaGetLastError(); cudaFree(buf); return -1; }
     DecodeLaunch L = persistent_launch(p, STEP_LOGITS);
-    L.trace = buf; L.trace_slots = points;
+    L.trace = buf; L.trace_slots = points; L.dtrace = wbuf;
     int r = cudaMemsetAsync(buf, 0, n * 8, s) == cudaSuccess &&
+            (!wbuf || cudaMemsetAsync(wbuf, 0, wn * 8, s) == cudaSuccess) &&
             set_request(p, token, (unsigned)position) == 0 &&
             launch_decode(L, s) == 0 && cudaMemcpyAsync(out, buf, n * 8, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+            (!wbuf || cudaMemcpyAsync(warp_out, wbuf, wn * 8, cudaMemcpyDeviceToHost, s) == cudaSuccess) &&
             cudaStreamSynchronize(s) == cudaSuccess && !*(volatile unsigned *)p->err_host ? 0 : -1;
+    if (wbuf) cudaFree(wbuf);
     cudaFree(buf);
     if (r) return plan_fail(p, position);
     p->valid = std::max(p->valid, position + 1);

@@ -192,6 +192,155 @@ FYB_DEV void compute_unit(const unsigned char *u, unsigned blk, const signed cha
     }
 }
 
+// NT units of the same 256-column block (one input vector): the x-limb
+// fragments and the block's exponent and group sums are loaded once and
+// reused for every unit, and the units' MMA chains are independent, so a
+// warp keeps NT chains in flight. acc[n][0] / acc[n][1] are unit n's row gid
+// / gid + 8 partial sums as in compute_unit<TYPE, 1>.
+// The per-lane constants of one prepared block: the limb weights of the
+// lane's two MMA columns and (Q4_K) the lane's two group sums.
+struct BlockConst {
+    float f0, f1;
+    float2 g2;
+};
+FYB_DEV BlockConst block_const(const int *exps, const float *gsums, unsigned lane)
+{
+    const unsigned tig = lane & 3;
+    const int l0 = 2 * (tig & 1);
+    const int E = tig < 2 ? exps[0] : 0;
+    BlockConst c;
+    c.f0 = pow2f(E - 6 - 7 * l0);
+    c.f1 = pow2f(E - 6 - 7 * (l0 + 1));
+    c.g2 = *reinterpret_cast<const float2 *>(gsums + 2 * tig);
+    return c;
+}
+
+template <unsigned TYPE, int NT>
+FYB_DEV void compute_units(const unsigned char *const (&u)[NT], const signed char *xl, unsigned xstride,
+    const BlockConst &bc, unsigned lane, float (&acc)[NT][2])
+{
+    const unsigned gid = lane >> 2, tig = lane & 3;
+    const bool brow_ok = gid < 4u;
+    const signed char *xrow = xl + (size_t)(brow_ok ? gid : 0) * xstride + tig * 16u;
+    const float f0 = bc.f0, f1 = bc.f1;
+    if constexpr (TYPE == T_Q4_K) {
+        int T[NT][4], Uh[NT][4];
+        unsigned sc[NT][4];  // scales of rows A (groups 0-3, 4-7) and B (0-3, 4-7)
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            const uint4 hA = *reinterpret_cast<const uint4 *>(u[n] + 2048 + gid * 16);
+            const uint4 hB = *reinterpret_cast<const uint4 *>(u[n] + 2048 + (gid + 8) * 16);
+            sc[n][0] = hA.y & 0x3F3F3F3Fu; sc[n][1] = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
+            sc[n][2] = hB.y & 0x3F3F3F3Fu; sc[n][3] = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { T[n][i] = 0; Uh[n][i] = 0; }
+        }
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) {
+            uint4 bw = make_uint4(0u, 0u, 0u, 0u);
+            if (brow_ok) bw = *reinterpret_cast<const uint4 *>(xrow + 64 * pr);
+            const int b0 = (2 * pr) & 3, b1 = b0 + 1;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                unsigned q[4];
+                load_frag(q, u[n] + pr * 512, lane);
+                const unsigned alo[4] = {q[0] & 0x0F0F0F0Fu, q[1] & 0x0F0F0F0Fu, q[2] & 0x0F0F0F0Fu, q[3] & 0x0F0F0F0Fu};
+                const unsigned ahi[4] = {q[0] & 0xF0F0F0F0u, q[1] & 0xF0F0F0F0u, q[2] & 0xF0F0F0F0u, q[3] & 0xF0F0F0F0u};
+                int dlo[4] = {0, 0, 0, 0}, dhi[4] = {0, 0, 0, 0};
+                mma_u8s8_k32(dlo, alo, bw.x, bw.y);
+                mma_u8s8_k32(dhi, ahi, bw.z, bw.w);
+                const unsigned wA = pr < 2 ? sc[n][0] : sc[n][1], wB = pr < 2 ? sc[n][2] : sc[n][3];
+                const int sAl = (int)__byte_perm(wA, 0u, 0x4440 + b0), sAh = (int)__byte_perm(wA, 0u, 0x4440 + b1);
+                const int sBl = (int)__byte_perm(wB, 0u, 0x4440 + b0), sBh = (int)__byte_perm(wB, 0u, 0x4440 + b1);
+                T[n][0] += sAl * dlo[0]; Uh[n][0] += sAh * dhi[0];
+                T[n][1] += sAl * dlo[1]; Uh[n][1] += sAh * dhi[1];
+                T[n][2] += sBl * dlo[2]; Uh[n][2] += sBh * dhi[2];
+                T[n][3] += sBl * dlo[3]; Uh[n][3] += sBh * dhi[3];
+            }
+        }
+        const float2 g2 = bc.g2;
+        const unsigned o = (2 * tig) & 3;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            const uint4 hA = *reinterpret_cast<const uint4 *>(u[n] + 2048 + gid * 16);
+            const uint4 hB = *reinterpret_cast<const uint4 *>(u[n] + 2048 + (gid + 8) * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) T[n][i] += Uh[n][i] >> 4;  // exact: Uh is a multiple of 16
+            const float dA = half_bits_to_float((unsigned short)(hA.x & 0xffffu));
+            const float dB = half_bits_to_float((unsigned short)(hB.x & 0xffffu));
+            float aA = dA * fmaf((float)T[n][0], f0, (float)T[n][1] * f1);
+            float aB = dB * fmaf((float)T[n][2], f0, (float)T[n][3] * f1);
+            // minimum term -dmin * sum_g m_g * sum(x_g): lane tig takes groups 2tig, 2tig+1
+            const unsigned mA0 = hA.z & 0x3F3F3F3Fu, mA1 = ((hA.w >> 4) & 0x0F0F0F0Fu) | ((hA.z >> 2) & 0x30303030u);
+            const unsigned mB0 = hB.z & 0x3F3F3F3Fu, mB1 = ((hB.w >> 4) & 0x0F0F0F0Fu) | ((hB.z >> 2) & 0x30303030u);
+            const float dmA = half_bits_to_float((unsigned short)(hA.x >> 16));
+            const float dmB = half_bits_to_float((unsigned short)(hB.x >> 16));
+            const unsigned wA = tig < 2 ? mA0 : mA1, wB = tig < 2 ? mB0 : mB1;
+            const float bA = fmaf((float)__byte_perm(wA, 0u, 0x4440 + o + 1), g2.y, (float)__byte_perm(wA, 0u, 0x4440 + o) * g2.x);
+            const float bB = fmaf((float)__byte_perm(wB, 0u, 0x4440 + o + 1), g2.y, (float)__byte_perm(wB, 0u, 0x4440 + o) * g2.x);
+            acc[n][0] = fmaf(-dmA, bA, aA);
+            acc[n][1] = fmaf(-dmB, bB, aB);
+        }
+    } else {
+        int T[NT][4];
+        uint4 sA[NT], sB[NT];
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            sA[n] = *reinterpret_cast<const uint4 *>(u[n] + 3072 + gid * 16);
+            sB[n] = *reinterpret_cast<const uint4 *>(u[n] + 3072 + (gid + 8) * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) T[n][i] = 0;
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            unsigned qh[NT][4];
+#pragma unroll
+            for (int n = 0; n < NT; ++n) load_frag(qh[n], u[n] + 2048 + h * 512, lane);
+#pragma unroll
+            for (int c2 = 0; c2 < 2; ++c2) {
+                unsigned ql[NT][4];
+#pragma unroll
+                for (int n = 0; n < NT; ++n) load_frag(ql[n], u[n] + (2 * h + c2) * 512, lane);
+#pragma unroll
+                for (int hiq = 0; hiq < 2; ++hiq) {
+                    const int Q = c2 + 2 * hiq;  // quarter: ql chunk c2, nibble hiq
+                    uint2 bw = make_uint2(0u, 0u);
+                    if (brow_ok) bw = *reinterpret_cast<const uint2 *>(xrow + (2 * h + (Q >> 1)) * 64 + 8 * (Q & 1));
+                    const int g = h * 8 + Q * 2;  // first of the two 16-value scale groups
+#pragma unroll
+                    for (int n = 0; n < NT; ++n) {
+                        unsigned a[4];
+#define FYB_Q6(QQ) for (int i = 0; i < 4; ++i) a[i] = q6_signed<QQ>(ql[n][i], qh[n][i]);
+                        if (Q == 0) { FYB_Q6(0) } else if (Q == 1) { FYB_Q6(1) } else if (Q == 2) { FYB_Q6(2) } else { FYB_Q6(3) }
+#undef FYB_Q6
+                        int d1[4] = {0, 0, 0, 0}, d2[4] = {0, 0, 0, 0};
+                        asm volatile(
+                            "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                            : "+r"(d1[0]), "+r"(d1[1]), "+r"(d1[2]), "+r"(d1[3]) : "r"(a[0]), "r"(a[1]), "r"(bw.x));
+                        asm volatile(
+                            "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                            : "+r"(d2[0]), "+r"(d2[1]), "+r"(d2[2]), "+r"(d2[3]) : "r"(a[2]), "r"(a[3]), "r"(bw.y));
+                        const unsigned wA = (&sA[n].x)[g >> 2], wB = (&sB[n].x)[g >> 2];
+                        const int s1A = sbyte(wA, g & 3), s2A = sbyte(wA, (g & 3) + 1);
+                        const int s1B = sbyte(wB, g & 3), s2B = sbyte(wB, (g & 3) + 1);
+                        T[n][0] += s1A * d1[0] + s2A * d2[0];
+                        T[n][1] += s1A * d1[1] + s2A * d2[1];
+                        T[n][2] += s1B * d1[2] + s2B * d2[2];
+                        T[n][3] += s1B * d1[3] + s2B * d2[3];
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            const float dA = half_bits_to_float(*reinterpret_cast<const unsigned short *>(u[n] + 3328 + gid * 2));
+            const float dB = half_bits_to_float(*reinterpret_cast<const unsigned short *>(u[n] + 3328 + (gid + 8) * 2));
+            acc[n][0] = dA * fmaf((float)T[n][0], f0, (float)T[n][1] * f1);
+            acc[n][1] = dB * fmaf((float)T[n][2], f0, (float)T[n][3] * f1);
+        }
+    }
+}
+
 // Sum of a lane's tile accumulator over the lanes that share its vector.
 template <int NV>
 FYB_DEV float lane_total(float acc)
