@@ -79,7 +79,8 @@ class SynthConfig(C.Structure):
                 ("kv_heads", C.c_uint32), ("feed_forward", C.c_uint32), ("vocabulary", C.c_uint32),
                 ("context", C.c_uint32), ("matrix_type", C.c_uint32), ("embed_type", C.c_uint32),
                 ("output_type", C.c_uint32), ("rope_base", C.c_float), ("epsilon", C.c_float),
-                ("seed", C.c_uint64), ("norm_mode", C.c_int), ("threads", C.c_int), ("centered", C.c_int)]
+                ("seed", C.c_uint64), ("norm_mode", C.c_int), ("threads", C.c_int), ("centered", C.c_int),
+                ("path", C.c_char_p)]
 
 
 def _load():
@@ -154,9 +155,10 @@ class SynthModel:
 
     def __init__(self, layers=2, embedding=512, heads=4, kv_heads=2, feed_forward=1024, vocabulary=1024,
                  context=512, matrix_type=Q4_K, embed_type=Q6_K, output_type=Q6_K, rope_base=500000.0,
-                 epsilon=1e-5, seed=1234, norm_mode=2, threads=0, centered=0):
+                 epsilon=1e-5, seed=1234, norm_mode=2, threads=0, centered=0, path=None):
         cfg = SynthConfig(layers, embedding, heads, kv_heads, feed_forward, vocabulary, context, matrix_type,
-                          embed_type, output_type, rope_base, epsilon, seed, norm_mode, threads, centered)
+                          embed_type, output_type, rope_base, epsilon, seed, norm_mode, threads, centered,
+                          path.encode() if path else None)
         self.config = cfg
         self.ptr = lib.fyb_synth_create(C.byref(cfg))
         if not self.ptr:

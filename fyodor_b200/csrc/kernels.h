@@ -78,6 +78,14 @@ size_t qgemv_partials_bytes(const QgemvLaunch &L, int grid);
 int qgemv_supported(unsigned type, size_t cols, size_t nvec);
 int launch_qgemv(const QgemvLaunch &L, cudaStream_t s);
 
+// ---------------------------------------------------------------- qgemm.cu
+// Small-batch GEMM (3..16 vectors) reading every weight unit once: x [nv][cols],
+// y [nv][out_stride]. Workspace: qgemm_workspace_bytes (zero before the first
+// launch; launches leave it so).
+size_t qgemm_workspace_bytes(unsigned type, size_t rows, size_t cols, size_t nv, int sms);
+int launch_qgemm(const QWeights &w, unsigned rows, const float *x, float *y, size_t out_stride, unsigned nv,
+    void *workspace, size_t workspace_bytes, unsigned *error, int sms, cudaStream_t s);
+
 // ---------------------------------------------------------------- attention.cu
 struct AttentionLaunch {
     const float *q = nullptr;       // [nseq][heads][hd]

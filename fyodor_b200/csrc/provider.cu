@@ -99,6 +99,8 @@ struct Context {
     size_t counters_bytes = 0;
     float *partials = nullptr;
     size_t partials_bytes = 0;
+    void *gemm = nullptr;  // small-batch GEMM workspace, kept zero between launches
+    size_t gemm_bytes = 0;
     int sms = 148;
 };
 
@@ -111,7 +113,7 @@ static void context_free(Context *c)
         DeviceScope scope(c->device);
         if (c->stream) cudaStreamSynchronize(c->stream);
         for (auto &w : c->weights) cudaFree(w.dev);
-        cudaFree(c->dx); cudaFree(c->dy); cudaFree(c->counters); cudaFree(c->partials);
+        cudaFree(c->dx); cudaFree(c->dy); cudaFree(c->counters); cudaFree(c->partials); cudaFree(c->gemm);
         if (c->stream) cudaStreamDestroy(c->stream);
     }
     delete c;
@@ -215,21 +217,37 @@ struct Scratch {
     size_t *counters_bytes;
     float **partials;
     size_t *partials_bytes;
+    void **gemm;          // small-batch GEMM workspace (zero between launches)
+    size_t *gemm_bytes;
 };
 
-// Y[b] = W X[b] on resident data; K-quants run the tensor-core GEMV two
-// vectors per launch, every other type the generic kernel.
+// Y[b] = W X[b] on resident data. K-quants: batches of 3 or more run the
+// weight-reusing small-batch GEMM in groups of up to 16 vectors (each weight
+// read once per group); one or two vectors (and a remainder of one or two)
+// run the tensor-core GEMV. Every other type runs the generic kernel.
 static int device_matmul(const QWeights *qw, const void *raw, size_t row_bytes, size_t rows, size_t cols,
     unsigned type, const float *x, float *y, size_t batch, const Scratch &sc, cudaStream_t s, int sms)
 {
     if (qw && qw->units) {
-        for (size_t b0 = 0; b0 < batch; b0 += 2) {
-            if (!qgemv_supported(type, cols, std::min<size_t>(2, batch - b0))) return -1;
+        for (size_t b0 = 0; b0 < batch;) {
+            const size_t left = batch - b0;
+            if (left >= 3) {
+                const unsigned nv = (unsigned)std::min<size_t>(16, left);
+                const size_t need = qgemm_workspace_bytes(type, rows, cols, nv, sms);
+                if (!need || grow(sc.gemm, sc.gemm_bytes, need, true)) return -2;
+                const int r = launch_qgemm(*qw, (unsigned)rows, x + b0 * cols, y + b0 * rows, rows, nv, *sc.gemm,
+                                           *sc.gemm_bytes, nullptr, sms, s);
+                if (r) return r;
+                b0 += nv;
+                continue;
+            }
+            const int nvec = (int)std::min<size_t>(2, left);
+            if (!qgemv_supported(type, cols, nvec)) return -1;
             QgemvLaunch L;
             L.epilogue = EPI_STORE;
             L.w = *qw;
             L.seg_rows[0] = (unsigned)rows;
-            L.nvec = (int)std::min<size_t>(2, batch - b0);
+            L.nvec = nvec;
             L.x = x + b0 * cols;
             L.out[0] = y + b0 * rows;
             L.out_stride = rows;
@@ -241,6 +259,7 @@ static int device_matmul(const QWeights *qw, const void *raw, size_t row_bytes, 
             L.partials = *sc.partials; L.partials_bytes = *sc.partials_bytes;
             const int r = launch_qgemv(L, s);
             if (r) return r;
+            b0 += (size_t)nvec;
         }
         return 0;
     }
@@ -267,7 +286,7 @@ static int context_matmul(Context *c, const void *w, size_t rows, size_t cols, u
             grow((void **)&c->dy, &c->dy_bytes, rows * batch * sizeof(float), false))
             break;
         if (cudaMemcpyAsync(c->dx, x, cols * batch * sizeof(float), cudaMemcpyHostToDevice, c->stream) != cudaSuccess) break;
-        const Scratch sc{&c->counters, &c->counters_bytes, &c->partials, &c->partials_bytes};
+        const Scratch sc{&c->counters, &c->counters_bytes, &c->partials, &c->partials_bytes, &c->gemm, &c->gemm_bytes};
         if (device_matmul(e->qw.units ? &e->qw : nullptr, e->dev, row_bytes, rows, cols, type, c->dx, c->dy, batch,
                           sc, c->stream, c->sms) != 0)
             break;
@@ -1077,14 +1096,20 @@ extern "C" int fyb_dequantize(const void *w, size_t count, unsigned type, float 
 }
 
 // Workspace of fyb_quant_matmul for one shape: [tile counters][partials][units].
-static void qm_layout(size_t rows, size_t cols, unsigned type, int sms, size_t *counters, size_t *partials, size_t *units)
+// Workspace of fyb_quant_matmul*: [stream-K counters][GEMV partials][units]
+// [small-batch GEMM scratch for `batch` vectors, at most 16 per group].
+static void qm_layout(size_t rows, size_t cols, unsigned type, int sms, size_t batch, size_t *counters,
+    size_t *partials, size_t *units, size_t *gemm)
 {
     QgemvLaunch L;
     L.w.type = type; L.w.cols = (unsigned)cols; L.w.tiles = (unsigned)((rows + 15) / 16);
     L.seg_rows[0] = (unsigned)rows;
     *counters = ((size_t)L.w.tiles * 4 + 255) / 256 * 256;
     *partials = (qgemv_partials_bytes(L, sms) + 255) / 256 * 256;
-    *units = qunits_bytes(type, L.w.tiles, cols);
+    *units = (qunits_bytes(type, L.w.tiles, cols) + 255) / 256 * 256;
+    *gemm = 0;
+    for (size_t nv = 3; nv <= std::min<size_t>(batch, 16); ++nv)
+        *gemm = std::max(*gemm, qgemm_workspace_bytes(type, rows, cols, nv, sms));
 }
 
 static int current_sms()
@@ -1097,11 +1122,10 @@ static int current_sms()
 
 extern "C" size_t fyb_quant_matmul_workspace(size_t rows, size_t cols, unsigned type, size_t batch)
 {
-    (void)batch;
     if (!qgemv_supported(type, cols, 1) || rows == 0) return 0;
-    size_t a, b, u;
-    qm_layout(rows, cols, type, current_sms(), &a, &b, &u);
-    return a + b + u;
+    size_t a, b, u, g;
+    qm_layout(rows, cols, type, current_sms(), batch, &a, &b, &u, &g);
+    return a + b + u + g;
 }
 
 extern "C" int fyb_quant_matmul(const void *w, size_t rows, size_t cols, unsigned type, const float *x, float *y,
@@ -1116,17 +1140,18 @@ extern "C" int fyb_quant_matmul(const void *w, size_t rows, size_t cols, unsigne
     const size_t row_bytes = cols / block * bbytes;
     if (!qgemv_supported(type, cols, 1))
         return launch_generic_matmul(w, row_bytes, rows, cols, type, x, cols, y, rows, batch, s);
-    size_t cb, pb, ub;
-    qm_layout(rows, cols, type, sms, &cb, &pb, &ub);
-    if (!workspace || workspace_bytes < cb + pb + ub) return -1;
+    size_t cb, pb, ub, gb;
+    qm_layout(rows, cols, type, sms, batch, &cb, &pb, &ub, &gb);
+    if (!workspace || workspace_bytes < cb + pb + ub + gb) return -1;
     unsigned char *ws = (unsigned char *)workspace;
     QWeights qw;
     qw.units = ws + cb + pb; qw.type = type; qw.cols = (unsigned)cols; qw.tiles = (unsigned)((rows + 15) / 16);
     if (repack_units(w, nullptr, rows, cols, type, REPACK_PLAIN, ws + cb + pb, qw.tiles, s)) return -2;
     unsigned *counters = (unsigned *)ws;
     float *partials = (float *)(ws + cb);
-    size_t cbytes = cb, pbytes = pb;
-    const Scratch sc{&counters, &cbytes, &partials, &pbytes};
+    void *gemm = ws + cb + pb + ub;
+    size_t cbytes = cb, pbytes = pb, gbytes = gb;
+    const Scratch sc{&counters, &cbytes, &partials, &pbytes, &gemm, &gbytes};
     return device_matmul(&qw, w, row_bytes, rows, cols, type, x, y, batch, sc, s, sms) ? -2 : 0;
 }
 
@@ -1139,8 +1164,8 @@ extern "C" int fyb_quant_repack(const void *w, size_t rows, size_t cols, unsigne
     if (!w || !rows || !cols || rows > 0x7fffffffu || !type_geometry(type, &block, &bbytes) || cols % block ||
         !qgemv_supported(type, cols, 1) || !workspace)
         return -1;
-    size_t cb, pb, ub;
-    qm_layout(rows, cols, type, current_sms(), &cb, &pb, &ub);
+    size_t cb, pb, ub, gb;
+    qm_layout(rows, cols, type, current_sms(), 1, &cb, &pb, &ub, &gb);
     if (workspace_bytes < cb + pb + ub) return -1;
     unsigned char *ws = (unsigned char *)workspace;
     return repack_units(w, nullptr, rows, cols, type, REPACK_PLAIN, ws + cb + pb, (unsigned)((rows + 15) / 16),
@@ -1153,16 +1178,17 @@ extern "C" int fyb_quant_matmul_prepared(size_t rows, size_t cols, unsigned type
     if (!x || !y || !rows || !cols || !batch || rows > 0x7fffffffu || !qgemv_supported(type, cols, 1) || !workspace)
         return -1;
     const int sms = current_sms();
-    size_t cb, pb, ub;
-    qm_layout(rows, cols, type, sms, &cb, &pb, &ub);
-    if (workspace_bytes < cb + pb + ub) return -1;
+    size_t cb, pb, ub, gb;
+    qm_layout(rows, cols, type, sms, batch, &cb, &pb, &ub, &gb);
+    if (workspace_bytes < cb + pb + ub + gb) return -1;
     unsigned char *ws = (unsigned char *)workspace;
     QWeights qw;
     qw.units = ws + cb + pb; qw.type = type; qw.cols = (unsigned)cols; qw.tiles = (unsigned)((rows + 15) / 16);
     unsigned *counters = (unsigned *)ws;
     float *partials = (float *)(ws + cb);
-    size_t cbytes = cb, pbytes = pb;
-    const Scratch sc{&counters, &cbytes, &partials, &pbytes};
+    void *gemm = ws + cb + pb + ub;
+    size_t cbytes = cb, pbytes = pb, gbytes = gb;
+    const Scratch sc{&counters, &cbytes, &partials, &pbytes, &gemm, &gbytes};
     return device_matmul(&qw, nullptr, 0, rows, cols, type, x, y, batch, sc, (cudaStream_t)stream, sms) ? -2 : 0;
 }
 

@@ -341,6 +341,139 @@ FYB_DEV void compute_units(const unsigned char *const (&u)[NT], const signed cha
     }
 }
 
+// One unit against NPP vector pairs (vectors 2pp, 2pp + 1 of pair pp; their
+// limb rows are pair * 8 + limb of xl, as compute_unit<TYPE, 2> reads one
+// pair): the weight fragments, masks and scale bytes are formed once per
+// 32-column chunk and used by every pair's MMAs. Pair pp's exponents and
+// group sums are at exps + pp * 2 * nblk and gsums + pp * 2 * ngroups.
+// acc[pp][0] / acc[pp][1] accumulate as compute_unit<TYPE, 2>'s accA / accB.
+template <unsigned TYPE, int NPP>
+FYB_DEV void compute_pairs(const unsigned char *u, unsigned blk, const signed char *xl, unsigned xstride,
+    const int *exps, unsigned nblk, const float *gsums, unsigned ngroups, unsigned lane, float (&acc)[NPP][2])
+{
+    const unsigned gid = lane >> 2, tig = lane & 3, vec = tig >> 1;
+    const int l0 = 2 * (tig & 1);
+    const signed char *xrow = xl + (size_t)gid * xstride + blk * 256u + tig * 16u;
+    int T[NPP][4];
+#pragma unroll
+    for (int n = 0; n < NPP; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) T[n][i] = 0;
+    if constexpr (TYPE == T_Q4_K) {
+        const uint4 hA = *reinterpret_cast<const uint4 *>(u + 2048 + gid * 16);
+        const uint4 hB = *reinterpret_cast<const uint4 *>(u + 2048 + (gid + 8) * 16);
+        const unsigned scA0 = hA.y & 0x3F3F3F3Fu, scA1 = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
+        const unsigned scB0 = hB.y & 0x3F3F3F3Fu, scB1 = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
+        int Uh[NPP][4];
+#pragma unroll
+        for (int n = 0; n < NPP; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) Uh[n][i] = 0;
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) {
+            unsigned q[4];
+            load_frag(q, u + pr * 512, lane);
+            const unsigned alo[4] = {q[0] & 0x0F0F0F0Fu, q[1] & 0x0F0F0F0Fu, q[2] & 0x0F0F0F0Fu, q[3] & 0x0F0F0F0Fu};
+            const unsigned ahi[4] = {q[0] & 0xF0F0F0F0u, q[1] & 0xF0F0F0F0u, q[2] & 0xF0F0F0F0u, q[3] & 0xF0F0F0F0u};
+            const unsigned wA = pr < 2 ? scA0 : scA1, wB = pr < 2 ? scB0 : scB1;
+            const int b0 = (2 * pr) & 3, b1 = b0 + 1;
+            const int sAl = (int)__byte_perm(wA, 0u, 0x4440 + b0), sAh = (int)__byte_perm(wA, 0u, 0x4440 + b1);
+            const int sBl = (int)__byte_perm(wB, 0u, 0x4440 + b0), sBh = (int)__byte_perm(wB, 0u, 0x4440 + b1);
+#pragma unroll
+            for (int n = 0; n < NPP; ++n) {
+                const uint4 bw = *reinterpret_cast<const uint4 *>(xrow + (size_t)n * 8 * xstride + 64 * pr);
+                int dlo[4] = {0, 0, 0, 0}, dhi[4] = {0, 0, 0, 0};
+                mma_u8s8_k32(dlo, alo, bw.x, bw.y);
+                mma_u8s8_k32(dhi, ahi, bw.z, bw.w);
+                T[n][0] += sAl * dlo[0]; Uh[n][0] += sAh * dhi[0];
+                T[n][1] += sAl * dlo[1]; Uh[n][1] += sAh * dhi[1];
+                T[n][2] += sBl * dlo[2]; Uh[n][2] += sBh * dhi[2];
+                T[n][3] += sBl * dlo[3]; Uh[n][3] += sBh * dhi[3];
+            }
+        }
+        const float dA = half_bits_to_float((unsigned short)(hA.x & 0xffffu));
+        const float dB = half_bits_to_float((unsigned short)(hB.x & 0xffffu));
+        const float dmA = half_bits_to_float((unsigned short)(hA.x >> 16));
+        const float dmB = half_bits_to_float((unsigned short)(hB.x >> 16));
+        const unsigned mA0 = hA.z & 0x3F3F3F3Fu, mA1 = ((hA.w >> 4) & 0x0F0F0F0Fu) | ((hA.z >> 2) & 0x30303030u);
+        const unsigned mB0 = hB.z & 0x3F3F3F3Fu, mB1 = ((hB.w >> 4) & 0x0F0F0F0Fu) | ((hB.z >> 2) & 0x30303030u);
+        const unsigned wmA = (tig & 1) ? mA1 : mA0, wmB = (tig & 1) ? mB1 : mB0;
+        const float mA[4] = {(float)__byte_perm(wmA, 0u, 0x4440), (float)__byte_perm(wmA, 0u, 0x4441),
+                             (float)__byte_perm(wmA, 0u, 0x4442), (float)__byte_perm(wmA, 0u, 0x4443)};
+        const float mB[4] = {(float)__byte_perm(wmB, 0u, 0x4440), (float)__byte_perm(wmB, 0u, 0x4441),
+                             (float)__byte_perm(wmB, 0u, 0x4442), (float)__byte_perm(wmB, 0u, 0x4443)};
+#pragma unroll
+        for (int n = 0; n < NPP; ++n) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) T[n][i] += Uh[n][i] >> 4;  // exact: Uh is a multiple of 16
+            const int E = exps[n * 2 * nblk + vec * nblk + blk];
+            const float f0 = pow2f(E - 6 - 7 * l0), f1 = pow2f(E - 6 - 7 * (l0 + 1));
+            acc[n][0] = fmaf(dA, fmaf((float)T[n][0], f0, (float)T[n][1] * f1), acc[n][0]);
+            acc[n][1] = fmaf(dB, fmaf((float)T[n][2], f0, (float)T[n][3] * f1), acc[n][1]);
+            // minimum term: the two lanes of a vector take groups 4(tig&1)..+3
+            const float4 g4 = *reinterpret_cast<const float4 *>(gsums + (size_t)n * 2 * ngroups + vec * ngroups +
+                                                                 blk * 8 + 4 * (tig & 1));
+            float bA = mA[0] * g4.x, bB = mB[0] * g4.x;
+            bA = fmaf(mA[1], g4.y, bA); bB = fmaf(mB[1], g4.y, bB);
+            bA = fmaf(mA[2], g4.z, bA); bB = fmaf(mB[2], g4.z, bB);
+            bA = fmaf(mA[3], g4.w, bA); bB = fmaf(mB[3], g4.w, bB);
+            acc[n][0] = fmaf(-dmA, bA, acc[n][0]);
+            acc[n][1] = fmaf(-dmB, bB, acc[n][1]);
+        }
+    } else {
+        const uint4 sA = *reinterpret_cast<const uint4 *>(u + 3072 + gid * 16);
+        const uint4 sB = *reinterpret_cast<const uint4 *>(u + 3072 + (gid + 8) * 16);
+        const float dA = half_bits_to_float(*reinterpret_cast<const unsigned short *>(u + 3328 + gid * 2));
+        const float dB = half_bits_to_float(*reinterpret_cast<const unsigned short *>(u + 3328 + (gid + 8) * 2));
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            unsigned qh[4];
+            load_frag(qh, u + 2048 + h * 512, lane);
+#pragma unroll
+            for (int c2 = 0; c2 < 2; ++c2) {
+                unsigned ql[4];
+                load_frag(ql, u + (2 * h + c2) * 512, lane);
+#pragma unroll
+                for (int hiq = 0; hiq < 2; ++hiq) {
+                    const int Q = c2 + 2 * hiq;
+                    unsigned a[4];
+#define FYB_Q6(QQ) for (int i = 0; i < 4; ++i) a[i] = q6_signed<QQ>(ql[i], qh[i]);
+                    if (Q == 0) { FYB_Q6(0) } else if (Q == 1) { FYB_Q6(1) } else if (Q == 2) { FYB_Q6(2) } else { FYB_Q6(3) }
+#undef FYB_Q6
+                    const int g = h * 8 + Q * 2;
+                    const unsigned wA = (&sA.x)[g >> 2], wB = (&sB.x)[g >> 2];
+                    const int s1A = sbyte(wA, g & 3), s2A = sbyte(wA, (g & 3) + 1);
+                    const int s1B = sbyte(wB, g & 3), s2B = sbyte(wB, (g & 3) + 1);
+#pragma unroll
+                    for (int n = 0; n < NPP; ++n) {
+                        const uint2 bw = *reinterpret_cast<const uint2 *>(xrow + (size_t)n * 8 * xstride +
+                                                                          (2 * h + (Q >> 1)) * 64 + 8 * (Q & 1));
+                        int d1[4] = {0, 0, 0, 0}, d2[4] = {0, 0, 0, 0};
+                        asm volatile(
+                            "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                            : "+r"(d1[0]), "+r"(d1[1]), "+r"(d1[2]), "+r"(d1[3]) : "r"(a[0]), "r"(a[1]), "r"(bw.x));
+                        asm volatile(
+                            "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                            : "+r"(d2[0]), "+r"(d2[1]), "+r"(d2[2]), "+r"(d2[3]) : "r"(a[2]), "r"(a[3]), "r"(bw.y));
+                        T[n][0] += s1A * d1[0] + s2A * d2[0];
+                        T[n][1] += s1A * d1[1] + s2A * d2[1];
+                        T[n][2] += s1B * d1[2] + s2B * d2[2];
+                        T[n][3] += s1B * d1[3] + s2B * d2[3];
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < NPP; ++n) {
+            const int E = exps[n * 2 * nblk + vec * nblk + blk];
+            const float f0 = pow2f(E - 6 - 7 * l0), f1 = pow2f(E - 6 - 7 * (l0 + 1));
+            acc[n][0] = fmaf(dA, fmaf((float)T[n][0], f0, (float)T[n][1] * f1), acc[n][0]);
+            acc[n][1] = fmaf(dB, fmaf((float)T[n][2], f0, (float)T[n][3] * f1), acc[n][1]);
+        }
+        (void)gsums; (void)ngroups;
+    }
+}
+
 // Sum of a lane's tile accumulator over the lanes that share its vector.
 template <int NV>
 FYB_DEV float lane_total(float acc)

@@ -24,6 +24,11 @@
 #include <cstring>
 #include <thread>
 #include <vector>
+#include <chrono>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 namespace {
 
@@ -189,6 +194,20 @@ struct SynthOwner {  // stored in mapping.data so fyb_synth_free can release eve
     unsigned char *arena;
 };
 
+constexpr uint64_t SYNTH_MAGIC = 0x4659425359544831ull;  // "FYBSYTH1"
+
+// Digest of everything that determines a model's bytes (a shared file made
+// for another configuration is not used).
+uint64_t config_digest(const fyb_synth_config &c, size_t total)
+{
+    uint64_t h = splitmix(total);
+    const uint64_t f[] = {c.layers, c.embedding, c.heads, c.kv_heads, c.feed_forward, c.vocabulary, c.context,
+                          c.matrix_type, c.embed_type, c.output_type, (uint64_t)(uint32_t)c.norm_mode,
+                          (uint64_t)(uint32_t)c.centered, c.seed};
+    for (uint64_t v : f) h = splitmix(h ^ v);
+    return h;
+}
+
 }  // namespace
 
 extern "C" void fyb_synth_fill(void *data, size_t rows, size_t columns, uint32_t type, uint64_t seed, uint64_t stream_id)
@@ -239,10 +258,44 @@ extern "C" nya_llm_context *fyb_synth_create(const fyb_synth_config *cfg)
         size_t bytes = (size_t)specs[i].rows * (specs[i].cols / block_values(specs[i].type)) * block_bytes(specs[i].type);
         total += (bytes + 255) / 256 * 256;
     }
-    unsigned char *arena = (unsigned char *)std::aligned_alloc(256, total ? total : 256);
-    if (!arena) { fyb_synth_free(c); return nullptr; }
-    c->mapping.data = arena;
-    c->mapping.size = total;
+    unsigned char *arena = nullptr;
+    bool fill = true;
+    if (cfg->path) {
+        // header page: magic, configuration digest, byte count, complete flag
+        const uint64_t digest = config_digest(*cfg, total);
+        const size_t head = 4096, bytes = head + total;
+        int fd = ::open(cfg->path, O_RDWR | O_CREAT | O_EXCL, 0600);
+        const bool creator = fd >= 0;
+        if (!creator) fd = ::open(cfg->path, O_RDONLY);
+        if (fd < 0) { fyb_synth_free(c); return nullptr; }
+        if (creator && ::ftruncate(fd, (off_t)bytes) != 0) { ::close(fd); ::unlink(cfg->path); fyb_synth_free(c); return nullptr; }
+        if (!creator) {  // wait (bounded) for the creator to size and complete it
+            bool ready = false;
+            for (int i = 0; i < 6000 && !ready; ++i) {
+                struct stat st;
+                if (::fstat(fd, &st) == 0 && (size_t)st.st_size == bytes) {
+                    uint64_t hdr[4] = {0, 0, 0, 0};
+                    ready = ::pread(fd, hdr, sizeof(hdr), 0) == (ssize_t)sizeof(hdr) && hdr[0] == SYNTH_MAGIC &&
+                            hdr[1] == digest && hdr[2] == total && hdr[3] == 1;
+                }
+                if (!ready) std::this_thread::sleep_for(std::chrono::milliseconds(100));
+            }
+            if (!ready) { ::close(fd); fyb_synth_free(c); return nullptr; }
+        }
+        void *m = ::mmap(nullptr, bytes, creator ? PROT_READ | PROT_WRITE : PROT_READ, MAP_SHARED, fd, 0);
+        ::close(fd);
+        if (m == MAP_FAILED) { if (creator) ::unlink(cfg->path); fyb_synth_free(c); return nullptr; }
+        arena = (unsigned char *)m + head;
+        c->mapping.data = (unsigned char *)m;
+        c->mapping.size = bytes;
+        c->mapping.mapping_handle = 1;  // a shared-file mapping: fyb_synth_free unmaps it
+        fill = creator;
+    } else {
+        arena = (unsigned char *)std::aligned_alloc(256, total ? total : 256);
+        if (!arena) { fyb_synth_free(c); return nullptr; }
+        c->mapping.data = arena;
+        c->mapping.size = total;
+    }
     for (size_t i = 0; i < specs.size(); ++i) {
         nya_llm_tensor *t = &c->tensors[i];
         const Spec &s = specs[i];
@@ -257,6 +310,7 @@ extern "C" nya_llm_context *fyb_synth_create(const fyb_synth_config *cfg)
         t->data_size = (size_t)s.rows * (s.cols / block_values(s.type)) * block_bytes(s.type);
         t->bound = 1;
         unsigned char *dst = arena + offsets[i];
+        if (!fill) continue;
         if (s.rows == 1) {  // norm vector
             Rng g(cfg->seed, i, 0);
             for (uint32_t k = 0; k < s.cols; ++k) {
@@ -266,6 +320,11 @@ extern "C" nya_llm_context *fyb_synth_create(const fyb_synth_config *cfg)
         } else {
             fill_parallel(dst, s.rows, s.cols, s.type, cfg->seed, i, threads, cfg->centered);
         }
+    }
+    if (cfg->path && fill) {  // the file is complete: later processes may map it
+        uint64_t *hdr = (uint64_t *)c->mapping.data;
+        hdr[0] = SYNTH_MAGIC; hdr[1] = config_digest(*cfg, total); hdr[2] = total;
+        __atomic_store_n(&hdr[3], (uint64_t)1, __ATOMIC_RELEASE);
     }
     c->token_embedding = &c->tensors[0];
     c->output_norm = &c->tensors[1];
@@ -304,7 +363,8 @@ extern "C" nya_llm_context *fyb_synth_create(const fyb_synth_config *cfg)
 extern "C" void fyb_synth_free(nya_llm_context *c)
 {
     if (!c) return;
-    std::free(c->mapping.data);
+    if (c->mapping.mapping_handle == 1) ::munmap(c->mapping.data, c->mapping.size);
+    else std::free(c->mapping.data);
     std::free(c->tensors);
     std::free(c->layers);
     std::free(c);

@@ -220,6 +220,12 @@ typedef struct fyb_synth_config {
     int threads;            /* host threads for filling; 0 = all cores */
     int centered;           /* Q4_K only: choose each group's min so its mean
                                weight is near zero (mins then are not uniform) */
+    const char *path;       /* null: private memory. Otherwise the tensor bytes
+                               live in this file, mapped shared: the first
+                               process to create it fills it, later ones (same
+                               configuration) wait until it is complete and map
+                               it read-only, so ranks on one host share one copy,
+                               as processes mapping one GGUF file do. */
 } fyb_synth_config;
 nya_llm_context *fyb_synth_create(const fyb_synth_config *config);
 void fyb_synth_free(nya_llm_context *model);

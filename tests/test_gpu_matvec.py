@@ -183,3 +183,35 @@ def test_prepared_matches_one_call(type_id):
         torch.cuda.synchronize()
         assert torch.equal(y1, y2), batch
     assert F.lib.fyb_quant_matmul_prepared(rows, cols, F.Q8_0, P(x), P(y2), 1, P(ws2), wsb, None) == -1
+
+
+@pytest.mark.parametrize("type_id", [F.Q4_K, F.Q6_K])
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (1024, 14336), (3000, 4096)])
+def test_prepared_small_batch_gemm(type_id, rows, cols):
+    """Batches of 3..17 through fyb_quant_matmul_prepared (the weight-reusing
+    small-batch GEMM for groups of 3..16 vectors, the GEMV for a remainder of
+    one or two) against the double reference, with the forward-error bound of
+    the GEMV tests. K = 14336 needs several K-slices at 16 vectors (their
+    partial rows are added in slice order); 3000 rows end in a partial tile."""
+    import torch
+    P = lambda t: C.c_void_p(t.data_ptr())
+    nbytes = rows * F.row_bytes(type_id, cols)
+    data = np.empty(nbytes, np.uint8)
+    F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, type_id, 77, rows * 3 + cols)
+    rng = np.random.default_rng(rows * 31 + cols)
+    xs = rng.standard_normal((17, cols)).astype(np.float32)
+    s, mag = double_reference(data, type_id, xs, cols, rows)
+    wsb = F.lib.fyb_quant_matmul_workspace(rows, cols, type_id, 17)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    dw = torch.from_numpy(data).cuda()
+    assert F.lib.fyb_quant_repack(P(dw), rows, cols, type_id, P(ws), wsb, None) == 0
+    x = torch.from_numpy(xs).cuda()
+    for batch in (3, 8, 16, 17):
+        y = torch.full((batch, rows), float("nan"), device="cuda")
+        for rep in range(2):  # twice: the scratch counters must be back at zero
+            assert F.lib.fyb_quant_matmul_prepared(rows, cols, type_id, P(x), P(y), batch, P(ws), wsb, None) == 0
+            torch.cuda.synchronize()
+            got = y.cpu().numpy().astype(np.float64)
+            for b in range(batch):
+                err = np.abs(got[b] - s[b])
+                assert np.all(err <= 1e-6 * (1 + mag[b])), (batch, rep, b, float((err / (1 + mag[b])).max()))
