@@ -326,6 +326,115 @@ def run_provider(args):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- 70B tensor parallel
+CFG70B = dict(layers=80, embedding=8192, heads=64, kv_heads=8, feed_forward=28672, vocabulary=128256, context=8192,
+              rope_base=500000.0, epsilon=1e-5, seed=4321, norm_mode=1)
+CAPACITY_70B = 8192  # fp16 KV cache sized for the 8192-token context
+
+
+def bytes_per_token_70b(world, positions):
+    """Algorithmic bytes one GPU streams per token of the 70B configuration at
+    the given attention positions: its 1/world of the projection and output
+    weights (Q4_K), the replicated norms and one Q6_K embedding row, and its
+    KV heads' fp16 rows at each position (mean over `positions`)."""
+    L, d, ffn, V, hd, kvh = 80, 8192, 28672, 128256, 128, 8
+    q4 = lambda r, c: r * c // 256 * 144
+    layer = q4(d, d) + 2 * q4(kvh * hd, d) + q4(d, d) + 3 * q4(ffn, d)
+    weights = (L * layer + q4(V, d)) / world + L * 2 * d * 4 + d * 4 + d // 256 * 210
+    kv = sum(L * (kvh // world) * hd * 2 * 2 * (p + 1) for p in positions) / len(positions)
+    return weights + kv
+
+
+def run_provider_70b(args):
+    """The 70B-class configuration (80 layers, d 8192, 64 / 8 heads of 128,
+    FFN 28672, vocabulary 128256; Q4_K projections and output head, Q6_K
+    embedding; fp16 KV cache for 8192 positions), tensor parallel over the
+    launch's ranks (one process per GPU; 1 = a single GPU). All ranks map one
+    copy of the model in /dev/shm (the first creates it), as processes on a
+    host map one GGUF file. Prompt 512 then 256 greedy tokens per step, batch
+    1 (batched decode is not built)."""
+    import torch
+    import fyodor_b200 as F
+    from tests.patterns import bench_tokens
+    rank, world, local = dist_env()
+    os.environ["NYA_CUDA_DEVICE"] = str(local)
+    if world > 1:
+        os.environ["NYA_CUDA_TP_SIZE"] = str(world)
+        os.environ["NYA_CUDA_TP_RANK"] = str(rank)
+    torch.cuda.set_device(local)
+    dist = init_dist(world)
+    t_setup = time.perf_counter()
+    path = "/dev/shm/fyb_bench_70b_%d.bin" % CFG70B["seed"]
+    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q4_K, path=path, **CFG70B)
+    provider = F.Provider()
+    plan = provider.plan(model, CAPACITY_70B)
+    if plan is None:
+        raise SystemExit("the provider declined the 70B plan")
+    barrier(dist)
+    if rank == 0 and os.path.exists(path):
+        os.unlink(path)  # every rank holds its mapping; the file goes with the last one
+    if world > 1 and not F.tp_connect_all(plan):
+        raise SystemExit("connecting the tensor-parallel ranks failed")
+    barrier(dist)
+    prompt = bench_tokens(PROMPT, model.vocabulary)
+    if plan.prefill(prompt, 0) != 0:
+        raise SystemExit("prefill failed")
+    first = int(np.argmax(plan.logits))
+    setup_s = time.perf_counter() - t_setup
+    for _ in range(args.warmup):
+        if plan.time_greedy(first, PROMPT, DECODE) < 0:
+            raise SystemExit("warm-up failed")
+    barrier(dist)
+    torch.cuda.synchronize()
+    launches_before = plan.stats()["kernel_launches"]
+    with ClockSampler(local) as clocks:
+        total_ms = 0.0
+        for _ in range(args.steps):
+            ms = plan.time_greedy(first, PROMPT, DECODE)
+            if ms < 0:
+                raise SystemExit("timed step failed")
+            total_ms += ms
+    torch.cuda.synchronize()
+    launches = plan.stats()["kernel_launches"] - launches_before
+    digest_tokens = plan.decode_greedy(first, PROMPT, 64)
+    barrier(dist)
+    total_ms = max_over_ranks(dist, total_ms)
+    value = args.steps * DECODE / (total_ms / 1000.0)
+    peaks, peak_kind = measured_peaks()
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    bpt = bytes_per_token_70b(world, range(PROMPT, PROMPT + DECODE))
+    per_launch_ms = total_ms / (args.steps * DECODE)
+    achieved = bpt / (per_launch_ms / 1000.0) / 1e9
+    line = {
+        "metric": "70B Q4_K decode tok/s (bs1)", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q4_k weights, s8 limb x u8/s8 int MMA, fp32 accumulate, fp16 KV",
+        "data": "synthetic (seeded random-init weights, random prompt ids)",
+        "config": {"workload": "70B-class Llama decode: prompt 512 then 256 greedy tokens per step, batch 1",
+                   "layers": 80, "d_model": 8192, "heads": "64/8", "ffn": 28672, "vocab": 128256,
+                   "weights": "Q4_K projections and output, Q6_K embedding", "kv": "fp16, 8192 positions",
+                   "parallelism": "tp%d" % world if world > 1 else "single-gpu",
+                   "l2": "inputs larger than L2 (%.1f GB of weights per GPU per token)" % (bpt / 1e9)},
+        "greedy_digest": {"tokens": 64, "first8": [int(x) for x in digest_tokens[:8]],
+                          "sha1": hashlib.sha1(np.asarray(digest_tokens, np.uint32).tobytes()).hexdigest()[:16]},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "kernel": "decode_kernel (persistent, one launch per token; %d B per launch per GPU)" % int(bpt),
+                     "us_per_launch": round(per_launch_ms * 1000, 2), "peak_source": peak_kind,
+                     "tok_s_at_peak": round(hbm * 1e9 / bpt, 1)},
+        "gpu_launches": int(launches), "clocks": clocks.summary(), "setup_s": round(setup_s, 1),
+        "cpu_baseline": None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    plan.close()
+    provider.close()
+    model.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
     """The engine's own CPU path on this host's cores: the bench model's bytes
@@ -565,6 +674,7 @@ def main():
     ap.add_argument("--attention", action="store_true", help="time the ragged-batch attention configuration only")
     ap.add_argument("--matvec", action="store_true", help="time the matvec / small-batch GEMM sweep only")
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--model", default="8b", choices=["8b", "70b"], help="70b: the tensor-parallel 70B configuration")
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="fyodor", choices=["fyodor", "reference"])
@@ -584,6 +694,8 @@ def main():
         run_trace_mode(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.model == "70b":
+        run_provider_70b(args)
     else:
         run_provider(args)
 

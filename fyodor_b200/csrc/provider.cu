@@ -653,10 +653,13 @@ static int set_request(Plan *p, unsigned token, unsigned position)
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+// A K-quant matrix of the expected shape. The persistent decode kernel takes
+// any multiple of 256 columns; the per-operation step's GEMV has its own
+// limit (qgemv_supported), checked when a plan runs that step.
 static bool supported_matrix(const nya_llm_tensor *t, size_t cols, size_t rows)
 {
     return t && (t->type == T_Q4_K || t->type == T_Q6_K) && t->dimension_count == 2 && t->dimensions[0] == cols &&
-           t->dimensions[1] == rows && qgemv_supported(t->type, cols, 1);
+           t->dimensions[1] == rows && cols % 256 == 0;
 }
 
 // Upload the raw GGUF bytes of up to three tensors and repack them, tile
@@ -929,6 +932,15 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
                      cudaMemsetAsync(p->attn_ws, 0, p->attn_ws_bytes, c->stream) == cudaSuccess;
     }
     if (ok) ok = setup_persistent(p);
+    if (ok && !p->dec_grid) {  // the per-operation step: every projection within the GEMV's limits
+        const size_t ks[3] = {d, (size_t)H * hd, ffn};
+        for (size_t k : ks)
+            if (!qgemv_supported(m->layers[0].query->type, k, 1) || !qgemv_supported(m->output->type, d, 1) ||
+                !qgemv_supported(m->layers[0].feed_forward_down->type, k, 1)) {
+                plan_free(p);
+                return plan_decline("geometry beyond the per-operation step's GEMV");
+            }
+    }
     if (ok && p->tp_size > 1) {
         if (!p->dec_grid) {  // only the persistent kernel exchanges partial sums
             debug("tensor parallelism needs the persistent decode kernel", cudaSuccess);

@@ -275,8 +275,17 @@ extern "C" nya_llm_context *fyb_synth_create(const fyb_synth_config *cfg)
                 struct stat st;
                 if (::fstat(fd, &st) == 0 && (size_t)st.st_size == bytes) {
                     uint64_t hdr[4] = {0, 0, 0, 0};
-                    ready = ::pread(fd, hdr, sizeof(hdr), 0) == (ssize_t)sizeof(hdr) && hdr[0] == SYNTH_MAGIC &&
-                            hdr[1] == digest && hdr[2] == total && hdr[3] == 1;
+                    const bool read = ::pread(fd, hdr, sizeof(hdr), 0) == (ssize_t)sizeof(hdr);
+                    if (read && hdr[3] == 1 && (hdr[0] != SYNTH_MAGIC || hdr[1] != digest || hdr[2] != total))
+                        break;  // complete, but made for another configuration
+                    ready = read && hdr[0] == SYNTH_MAGIC && hdr[1] == digest && hdr[2] == total && hdr[3] == 1;
+                }
+                else {
+                    struct stat st2;
+                    if (::fstat(fd, &st2) == 0 && (size_t)st2.st_size != bytes && st2.st_size != 0) {
+                        uint64_t hdr[4] = {0, 0, 0, 0};
+                        if (::pread(fd, hdr, sizeof(hdr), 0) == (ssize_t)sizeof(hdr) && hdr[3] == 1) break;
+                    }
                 }
                 if (!ready) std::this_thread::sleep_for(std::chrono::milliseconds(100));
             }

@@ -49,3 +49,40 @@ def test_provider_declines_without_device():
     if F.lib.fyb_device_count() > 0:
         return
     assert not F.api().create()
+
+
+def _shared_model_worker(path, out):
+    import numpy as np
+
+    import fyodor_b200 as F
+    m = F.SynthModel(layers=2, embedding=512, heads=4, kv_heads=2, feed_forward=1024, vocabulary=1024, context=64,
+                     seed=9, path=path)
+    np.save(out, np.concatenate([m.tensor_bytes(i) for i in (0, 4, 10)]))
+    m.close()
+
+
+def test_shared_file_model(tmp_path):
+    """A model created with `path` lives in one shared file: the first
+    process fills it, the others wait for it and map it; every process sees
+    the bytes the private-memory generator makes."""
+    import multiprocessing as mp
+
+    import numpy as np
+    path = str(tmp_path / "model.bin")
+    ctx = mp.get_context("spawn")
+    outs = [str(tmp_path / ("w%d.npy" % i)) for i in range(3)]
+    procs = [ctx.Process(target=_shared_model_worker, args=(path, o)) for o in outs]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    ref = F.SynthModel(layers=2, embedding=512, heads=4, kv_heads=2, feed_forward=1024, vocabulary=1024, context=64,
+                       seed=9)
+    expect = np.concatenate([ref.tensor_bytes(i) for i in (0, 4, 10)])
+    for o in outs:
+        assert (np.load(o) == expect).all()
+    # a file made for another configuration is not used
+    other = F.SynthModel(layers=2, embedding=512, heads=4, kv_heads=2, feed_forward=1024, vocabulary=1024,
+                         context=64, seed=10, path=None)
+    assert not (other.tensor_bytes(4) == ref.tensor_bytes(4)).all()
