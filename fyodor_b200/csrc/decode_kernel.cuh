@@ -49,14 +49,12 @@ namespace fyb {
 constexpr unsigned WAIT_LIMIT = 1u << 22;  // polls (with a short sleep) before ERR_TIMEOUT
 constexpr unsigned POLL_NS_MAX = 256;      // poll back-off: sleeps double from 16 ns up to this
 constexpr unsigned RING_BARS = 8;          // mbarriers (max units in flight) per warp
-constexpr unsigned CHUNK = 8;              // tiles per reduction chunk
+constexpr unsigned CHUNK = 16;             // tiles per reduction chunk
 constexpr unsigned LIMB_STRIDE = 256 + QG_XPAD;  // limb-row stride of a one-block slot (64 mod 128)
 constexpr unsigned LIMB_SLOT = 4 * LIMB_STRIDE + 16 + 32 + 16;  // 4 limb rows | exponent | 8 group sums | pad
+constexpr unsigned LIMB_SLOTS = 1;                 // per warp: the input block of its current units
 constexpr unsigned NORM_BLOCKS_MAX = 64;   // 256-value blocks of a normalized input (d <= 16384)
 constexpr unsigned DTRACE_POINTS = 32;     // per-warp detail records (profiling)
-#ifndef FYB_PAIR_UNITS
-#define FYB_PAIR_UNITS 0                    // two units of one block per step (build flag for comparisons)
-#endif
 
 typedef unsigned long long u64;
 
@@ -170,11 +168,23 @@ FYB_DEV bool ll_wait1(const DecodeParams &p, const u64 *src, unsigned tag, float
 // Eight consecutive words per lane (src is this lane's first word, 16-byte
 // aligned), warp-uniform: returns when every lane's words carry `tag`; false
 // for the whole warp on abort or timeout.
-FYB_DEV bool ll_wait8(const DecodeParams &p, const u64 *src, unsigned tag, float (&v)[8])
+FYB_DEV void ll_load8(const u64 *src, u64 (&r)[8])
 {
-    u64 r[8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) ll_get2(src + 2 * i, r[2 * i], r[2 * i + 1]);
+}
+
+// `pre`: the words already requested from src (so that two blocks' loads
+// are in flight together), or null.
+FYB_DEV bool ll_wait8(const DecodeParams &p, const u64 *src, unsigned tag, float (&v)[8], const u64 *pre = nullptr)
+{
+    u64 r[8];
+    if (pre) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = pre[i];
+    } else {
+        ll_load8(src, r);
+    }
     unsigned ns = 16;
     for (unsigned it = 0;; ++it) {
         bool ok = true;
@@ -408,10 +418,11 @@ struct Cta {
     unsigned *flag;
 };
 
-FYB_DEV LimbSlot limb_slot(unsigned char *base, unsigned warp)
+// Slot `which` of the limb slots starting at `base` (a warp's first slot).
+FYB_DEV LimbSlot limb_slot(unsigned char *base, unsigned which)
 {
     LimbSlot s;
-    unsigned char *b = base + (size_t)warp * LIMB_SLOT;
+    unsigned char *b = base + (size_t)which * LIMB_SLOT;
     s.xl = reinterpret_cast<signed char *>(b);
     s.exps = reinterpret_cast<int *>(b + 4 * LIMB_STRIDE);
     s.gsums = reinterpret_cast<float *>(b + 4 * LIMB_STRIDE + 16);
@@ -481,8 +492,20 @@ FYB_DEV void split_block(float (&x)[8], unsigned lane, const LimbSlot &s, unsign
 // layer. With tensor parallelism the d-row inputs are a base vector plus the
 // ranks' partial rows, added in rank order (every rank computes the same x),
 // and the last CTA stores the summed x for the next exchange's base.
+// The lane's first word of block b for phases with one tagged source (O,
+// down, and without tensor parallelism QKV after layer 0, gate/up and the
+// logits); null for the others.
+FYB_DEV const u64 *single_source(const DecodeParams &p, const Phase &ph, unsigned b, unsigned lane)
+{
+    const unsigned i0 = b * 256 + lane * 8;
+    if (ph.kind == PH_O) return p.ll.attn + i0;
+    if (ph.kind == PH_DOWN) return p.ll.h + i0;
+    if (p.tp > 1 || (ph.kind == PH_QKV && ph.layer == 0)) return nullptr;
+    return (ph.kind == PH_GATEUP ? p.ll.xm : p.ll.xa) + i0;
+}
+
 FYB_DEV bool prep_block(const DecodeParams &p, const Phase &ph, unsigned b, unsigned step, const LimbSlot &s,
-    double *bss, unsigned lane)
+    double *bss, unsigned lane, const u64 *pre = nullptr)
 {
     const unsigned i0 = b * 256 + lane * 8;
     const int l = (int)ph.layer;
@@ -497,14 +520,11 @@ FYB_DEV bool prep_block(const DecodeParams &p, const Phase &ph, unsigned b, unsi
 #pragma unroll
             for (int j = 0; j < 8; ++j) ll_put(p.ll.xa + i0 + j, x[j], ll_tag(step, -1));
         }
-    } else if (ph.kind == PH_O) {
-        if (!ll_wait8(p, p.ll.attn + i0, ll_tag(step, l), x)) return false;
-    } else if (ph.kind == PH_DOWN) {
-        if (!ll_wait8(p, p.ll.h + i0, ll_tag(step, l), x)) return false;
+    } else if (ph.kind == PH_O || ph.kind == PH_DOWN) {
+        if (!ll_wait8(p, single_source(p, ph, b, lane), ll_tag(step, l), x, pre)) return false;
     } else if (p.tp == 1) {
-        const u64 *src = ph.kind == PH_GATEUP ? p.ll.xm : p.ll.xa;
         const unsigned tag = ll_tag(step, ph.kind == PH_GATEUP ? l : prev);
-        if (!ll_wait8(p, src + i0, tag, x)) return false;
+        if (!ll_wait8(p, single_source(p, ph, b, lane), tag, x, pre)) return false;
     } else {
         // x = base + the ranks' partial rows: QKV / logits: x after O plus the
         // down rows; gate/up: x after the previous exchange plus the O rows
@@ -647,7 +667,7 @@ FYB_DEV bool pair_output(const DecodeParams &p, const Phase &ph, unsigned step, 
 // phases (it picks the block sums of squares). False for every thread on
 // abort.
 template <unsigned TYPE>
-FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, Ring &r, const LimbSlot &slot,
+FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, Ring &r, unsigned char *slots,
     const Cta &cta, unsigned lane, unsigned &seq, unsigned pseq, unsigned long long &key)
 {
     const unsigned warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
@@ -657,7 +677,7 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, R
     const bool norm = ph.kind == PH_QKV || ph.kind == PH_GATEUP || ph.kind == PH_LOGITS;
     double *bss = cta.bss + (pseq & 1) * NORM_BLOCKS_MAX;
     bool ok = true;
-    unsigned cur_b = ~0u;
+    unsigned plo = ~0u, cur_b = ~0u;  // plo: the block in the limb slot; cur_b: the block of bc
     BlockConst bc;
     const bool dt = dtraced(p, ph.layer) && ph.kind != PH_LOGITS;
     const unsigned dbase = ph.kind * 6;
@@ -675,25 +695,31 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, R
         // load is not in front of the barrier (a failure of this thread since
         // the last barrier raised it, and this thread sees its own store)
         const bool abort_seen = lane == 0 && aborted(p);
-        // this warp's partial rows of the chunk's tiles start at zero
-        for (unsigned i = lane; i < Tc * 16; i += 32) parts[((i >> 4) * QG_WARPS + warp) * 16 + (i & 15)] = 0.f;
-        __syncwarp();
+        // a warp whose units are exactly one block column of the chunk writes
+        // each of its partial rows once; any other warp starts them at zero
+        // and adds to them
+        const bool column = wk.e - wk.k == Tc && wk.t == 0;
+        if (!column) {
+            for (unsigned i = lane; i < Tc * 16; i += 32) parts[((i >> 4) * QG_WARPS + warp) * 16 + (i & 15)] = 0.f;
+            __syncwarp();
+        }
         {
         unsigned b = wk.b, t = wk.t;
         for (unsigned k = wk.k; k < wk.e && ok;) {
-            if (b != cur_b) {
+            if (b != plo) {  // prepare block b into the limb slot
                 const long long c0 = dt ? clock64() : 0;
-                ok = prep_block(p, ph, b, step, slot, bss, lane);
+                ok = prep_block(p, ph, b, step, limb_slot(slots, 0), bss, lane);
                 if (dt) {
                     prep_cycles += clock64() - c0;
-                    if (cur_b == ~0u) drecord(p, dbase + 1, globaltimer());
+                    if (plo == ~0u) drecord(p, dbase + 1, globaltimer());
                 }
-                cur_b = b;
+                plo = b;
                 if (!ok) break;
-                bc = block_const(slot.exps, slot.gsums, lane);
             }
-            // two units of the same block share the x fragments
-            const bool two = FYB_PAIR_UNITS && k + 1 < wk.e && t + 1 < Tc;
+            const LimbSlot slot = limb_slot(slots, 0);
+            if (b != cur_b) { bc = block_const(slot.exps, slot.gsums, lane); cur_b = b; }
+            // two units of the same block run as two independent MMA chains
+            const bool two = k + 1 < wk.e && t + 1 < Tc;
             const long long w0 = dt ? clock64() : 0;
             const unsigned char *u0 = ring_wait(r);
             const unsigned char *u1 = two && u0 ? ring_wait(r) : u0;
@@ -718,8 +744,8 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, R
                 const float yA = lane_total<1>(acc[n][0]), yB = lane_total<1>(acc[n][1]);
                 if (tig == 0) {
                     float *row = parts + ((t + n) * QG_WARPS + warp) * 16;
-                    row[gid] += yA;
-                    row[gid + 8] += yB;
+                    if (column) { row[gid] = yA; row[gid + 8] = yB; }
+                    else { row[gid] += yA; row[gid + 8] += yB; }
                 }
             }
             const unsigned adv = two ? 2u : 1u;
@@ -776,11 +802,11 @@ FYB_DEV bool gemv_phase(const DecodeParams &p, const Phase &ph, unsigned step, R
     return true;
 }
 
-FYB_DEV bool run_gemv(const DecodeParams &p, const Phase &ph, unsigned step, Ring &r, const LimbSlot &slot,
+FYB_DEV bool run_gemv(const DecodeParams &p, const Phase &ph, unsigned step, Ring &r, unsigned char *slots,
     const Cta &cta, unsigned lane, unsigned &seq, unsigned pseq, unsigned long long &key)
 {
-    return ph.w.type == T_Q4_K ? gemv_phase<T_Q4_K>(p, ph, step, r, slot, cta, lane, seq, pseq, key)
-                               : gemv_phase<T_Q6_K>(p, ph, step, r, slot, cta, lane, seq, pseq, key);
+    return ph.w.type == T_Q4_K ? gemv_phase<T_Q4_K>(p, ph, step, r, slots, cta, lane, seq, pseq, key)
+                               : gemv_phase<T_Q6_K>(p, ph, step, r, slots, cta, lane, seq, pseq, key);
 }
 
 // ------------------------------------------------------------ attention
@@ -1055,7 +1081,7 @@ struct SmemLayout {
 FYB_HOST_DEV SmemLayout smem_layout(unsigned H, unsigned Hkv, unsigned hd, unsigned ring_bytes)
 {
     SmemLayout s;
-    const size_t limbs = (size_t)QG_WARPS * LIMB_SLOT;
+    const size_t limbs = (size_t)QG_WARPS * LIMB_SLOTS * LIMB_SLOT;
     const size_t abytes = attn_smem_floats(H / Hkv, hd) * 4;
     s.rings = 0;
     s.bars = (size_t)QG_WARPS * ring_bytes;
@@ -1162,7 +1188,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
     ring.is = reinterpret_cast<RingIssue *>(smem + lay.issue) + warp;
     ring.par = 0;
     ring.issued = ring.consumed = ring.n = 0;
-    const LimbSlot slot = limb_slot(smem + lay.uni, warp);
+    unsigned char *const slots = smem + lay.uni + (size_t)warp * LIMB_SLOTS * LIMB_SLOT;  // this warp's limb slots
     Cta cta;
     cta.parts = reinterpret_cast<float *>(smem + lay.parts);
     cta.bss = reinterpret_cast<double *>(smem + lay.bss);
@@ -1196,7 +1222,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
                 ok = __syncthreads_or(!ok || aborted(p)) == 0;
                 if (dtraced(p, l) && warp == 0) drecord(p, 28, globaltimer());
             } else {
-                ok = run_gemv(p, cur, step, ring, slot, cta, lane, seq, pseq++, key);
+                ok = run_gemv(p, cur, step, ring, slots, cta, lane, seq, pseq++, key);
                 Phase nx;
                 if (phase_after(p, cur.kind, cur.layer, nx)) cur = nx;
             }
@@ -1205,7 +1231,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) decode_kernel(const DecodeParam
     }
     bool logits_done = false;
     if (ok && p.logits_mode) {
-        ok = run_gemv(p, cur, step, ring, slot, cta, lane, seq, pseq++, key);
+        ok = run_gemv(p, cur, step, ring, slots, cta, lane, seq, pseq++, key);
         logits_done = ok;
     }
     stamp(p, 1 + 5 * p.nl);
