@@ -279,7 +279,9 @@ def run_provider(args):
                          "engine's CPU provider (nya_llm_session_run, NYA_CPU_THREADS=%d), after the same "
                          "512-token prompt prefilled by its batched CPU prefill" % (n, threads)}
     attn_c4 = attention_c4() if rank == 0 and world == 1 else None
-    mv_c2 = matvec_c2() if rank == 0 and world == 1 else None
+    with_cpu = not args.no_cpu_baseline
+    mv_c2 = matvec_c2(cpu=with_cpu) if rank == 0 and world == 1 else None
+    mv_c1 = matvec_c1(cpu=with_cpu) if rank == 0 and world == 1 else None
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -312,6 +314,7 @@ def run_provider(args):
                     "units": "stand-alone GEMV launches (matvec/matmul path): [us per launch, GB/s]"},
         "attention_c4": attn_c4,
         "matvec_c2": mv_c2,
+        "matvec_c1": mv_c1,
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
@@ -522,22 +525,52 @@ def attention_c4(reps=20, warmup=3, splits_decode=16, splits_verify=4):
     return res
 
 
-def matvec_c2(reps=10, warmup=3):
+def _cpu_compute():
+    """The engine's "cpu" compute provider on all host threads, or None when
+    oracle/_ref was not built."""
+    import oracle as O
+    if not O.reference_available():
+        return None, 0
+    threads = os.cpu_count() or 1
+    os.environ["NYA_CPU_THREADS"] = str(threads)
+    return O.RefCompute(), threads
+
+
+def _time_device(call, copies, reps, warmup):
+    """Milliseconds per call(copy) over CUDA events, rotating over `copies`."""
+    import torch
+    for i in range(warmup):
+        assert call(copies[i % len(copies)]) == 0
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(reps):
+        assert call(copies[i % len(copies)]) == 0
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def matvec_c2(reps=10, warmup=3, cpu=False):
     """The matvec / small-batch GEMM sweep: Q4_K and Q6_K weights of the four
     projection shapes (out x in) at batches 1, 2, 4, 8, 16, repacked once
     (fyb_quant_repack) and multiplied with fyb_quant_matmul_prepared. Consecutive
     timed launches rotate over copies of the weights totalling at least 512 MB
     (more than L2). Values: {shape: {type: {batch: [us, GB/s]}}}, GB/s =
-    (GGUF weight bytes once + 4 B x batch x (in + out)) / time."""
+    (GGUF weight bytes once + 4 B x batch x (in + out)) / time. With cpu=True
+    the same weights (host copies) also go through the engine's CPU provider
+    at batches 1 and 16 (nya_compute_matvec_typed / matmul_typed on a "cpu"
+    context): values under "cpu"."""
     import ctypes as C
     import torch
     import fyodor_b200 as F
     P = lambda t: C.c_void_p(t.data_ptr())
     stream = lambda: C.c_void_p(torch.cuda.current_stream().cuda_stream)
-    out = {}
+    ref, threads = _cpu_compute() if cpu else (None, 0)
+    out, cpu_out = {}, {}
     for rows, cols in ((4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)):
         shape = "%dx%d" % (rows, cols)
-        out[shape] = {}
+        out[shape], cpu_out[shape] = {}, {}
         for tname, t in (("q4_k", F.Q4_K), ("q6_k", F.Q6_K)):
             nbytes = rows * F.row_bytes(t, cols)
             data = np.empty(nbytes, np.uint8)
@@ -552,24 +585,64 @@ def matvec_c2(reps=10, warmup=3):
             y = torch.empty((16, rows), device="cuda")
             res = {}
             for batch in (1, 2, 4, 8, 16):
-                for i in range(warmup):
-                    F.lib.fyb_quant_matmul_prepared(rows, cols, t, P(x), P(y), batch, P(copies[i % len(copies)]),
-                                                    wsb, stream())
-                torch.cuda.synchronize()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                for i in range(reps):
-                    r = F.lib.fyb_quant_matmul_prepared(rows, cols, t, P(x), P(y), batch,
-                                                        P(copies[i % len(copies)]), wsb, stream())
-                    assert r == 0
-                e1.record()
-                torch.cuda.synchronize()
-                ms = e0.elapsed_time(e1) / reps
+                ms = _time_device(lambda ws: F.lib.fyb_quant_matmul_prepared(rows, cols, t, P(x), P(y), batch, P(ws),
+                                                                             wsb, stream()), copies, reps, warmup)
                 res[batch] = [round(ms * 1e3, 2), round((nbytes + 4 * batch * (rows + cols)) / ms / 1e6, 1)]
             out[shape][tname] = res
             del copies, ws0
             torch.cuda.empty_cache()
-    out["units"] = "[us per call, GB/s of GGUF weight bytes once + x + y]; batches > 2 run ceil(batch/2) passes"
+            if ref is not None:
+                xs = x.cpu().numpy()
+                cres = {}
+                for batch in (1, 16):
+                    us = ref.time(data, rows, cols, t, xs[:batch], batch)
+                    cres[batch] = [round(us, 1), round((nbytes + 4 * batch * (rows + cols)) / us / 1e3, 1)]
+                cpu_out[shape][tname] = cres
+    out["units"] = "[us per call, GB/s of GGUF weight bytes once + x + y]; batches of 3..16 run the small-batch GEMM (every weight unit read once)"
+    if ref is not None:
+        cpu_out["units"] = ("[us per call, GB/s] through the Fyodor engine's CPU provider (nya_compute_matvec_typed / "
+                            "nya_compute_matmul_typed on a \"cpu\" context, NYA_CPU_THREADS=%d), weights in host memory"
+                            % threads)
+        out["cpu"] = cpu_out
+        ref.close()
+    return out
+
+
+def matvec_c1(reps=200, warmup=5, cpu=False):
+    """C1: Q8_0 4096x4096 (int8 uniform in [-127, 127], d = |N(0,1)| * 0.01,
+    seeded) times an fp32 N(0,1) vector, through fyb_quant_matmul (the
+    bulk-staged Q8_0 kernel; batch 8 as well), rotating over copies of the
+    weights totalling at least 512 MB. With cpu=True the engine's CPU provider
+    times the same product from host memory."""
+    import ctypes as C
+    import torch
+    import fyodor_b200 as F
+    rows = cols = 4096
+    P = lambda t: C.c_void_p(t.data_ptr())
+    stream = lambda: C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    nbytes = rows * F.row_bytes(F.Q8_0, cols)
+    data = np.empty(nbytes, np.uint8)
+    F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, F.Q8_0, 2024, rows * 7 + cols)
+    dw = torch.from_numpy(data).cuda()
+    copies = [dw] + [dw.clone() for _ in range(-(-(512 << 20) // nbytes) - 1)]
+    x = torch.randn((8, cols), device="cuda")
+    y = torch.empty((8, rows), device="cuda")
+    res = {}
+    for batch in (1, 8):
+        ms = _time_device(lambda w: F.lib.fyb_quant_matmul(P(w), rows, cols, F.Q8_0, P(x), P(y), batch, None, 0,
+                                                           stream()), copies, reps, warmup)
+        res[batch] = [round(ms * 1e3, 2), round((nbytes + 4 * batch * (rows + cols)) / ms / 1e6, 1)]
+    del copies, dw
+    torch.cuda.empty_cache()
+    out = {"q8_0_4096x4096": res,
+           "units": "[us per call, GB/s of GGUF weight bytes once + x + y]"}
+    ref, threads = _cpu_compute() if cpu else (None, 0)
+    if ref is not None:
+        us = ref.time(data, rows, cols, F.Q8_0, x[:1].cpu().numpy(), 1, seconds=1.0, max_calls=2000)
+        out["cpu"] = {"1": [round(us, 1), round((nbytes + 4 * (rows + cols)) / us / 1e3, 1)],
+                      "threads": threads, "kind": "reference",
+                      "sample": "nya_compute_matvec_typed on a \"cpu\" context, weights in host memory"}
+        ref.close()
     return out
 
 
@@ -685,7 +758,8 @@ def main():
     if args.kernel:
         run_kernel_mode(args)
     elif args.matvec:
-        print(json.dumps({"matvec_c2": matvec_c2()}))
+        print(json.dumps({"matvec_c1": matvec_c1(cpu=not args.no_cpu_baseline),
+                          "matvec_c2": matvec_c2(cpu=not args.no_cpu_baseline)}))
     elif args.attention:
         print(json.dumps({"attention_c4": attention_c4(reps=args.reps, warmup=3)}))
     elif args.eager_steps:

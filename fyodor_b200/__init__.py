@@ -109,6 +109,8 @@ def _load():
     lib.fyb_plan_tp_handle.argtypes = [_P, _P, C.c_size_t]
     lib.fyb_plan_tp_connect.argtypes = [_P, _P, C.c_size_t]
     lib.fyb_plan_tp_disconnect.argtypes = [_P]
+    lib.fyb_plan_tp_connect_local.argtypes = [_P, C.POINTER(C.c_void_p), C.c_size_t]
+    lib.fyb_plan_error.argtypes = [_P]
     lib.fyb_plan_trace.restype = C.c_long
     lib.fyb_plan_trace.argtypes = [_P, C.c_uint32, C.c_size_t, _P, C.c_size_t, _P, _P, C.c_size_t]
     lib.fyb_plan_decode_greedy.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t, _P]
@@ -136,7 +138,8 @@ EXPORTS = ["nya_cuda_backend", "fyb_version", "fyb_device_count", "fyb_dequantiz
            "fyb_attention_decode", "fyb_attention_verify",
            "fyb_attention_decode_static", "fyb_plan_decode_greedy",
            "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_decode_form", "fyb_plan_profile", "fyb_plan_trace",
-           "fyb_plan_tp_info", "fyb_plan_tp_handle", "fyb_plan_tp_connect", "fyb_plan_tp_disconnect", "fyb_plan_time_projection",
+           "fyb_plan_tp_info", "fyb_plan_tp_handle", "fyb_plan_tp_connect", "fyb_plan_tp_disconnect",
+           "fyb_plan_tp_connect_local", "fyb_plan_error", "fyb_plan_time_projection",
            "fyb_synth_create",
            "fyb_synth_free", "fyb_synth_fill"]
 
@@ -342,6 +345,17 @@ class Plan:
     def tp_disconnect(self):
         """Decline every later step without launching (another rank failed)."""
         return lib.fyb_plan_tp_disconnect(C.c_void_p(self.ptr))
+
+    def tp_connect_local(self, plans):
+        """Connect this plan to the other shard plans of this process
+        (plans: every rank's Plan, in rank order)."""
+        arr = (C.c_void_p * len(plans))(*[q.ptr for q in plans])
+        return lib.fyb_plan_tp_connect_local(C.c_void_p(self.ptr), arr, len(plans))
+
+    def error(self):
+        """The device error word: 0 none, 1 a bounded wait ran out, 2 non-finite
+        logits, 4 an index out of range."""
+        return lib.fyb_plan_error(C.c_void_p(self.ptr))
 
     def trace(self, token, position, detail=False):
         """Per-CTA trace points of one persistent decode step: array

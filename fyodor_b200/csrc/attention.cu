@@ -263,6 +263,292 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
     if (threadIdx.x == 0) p.counters[pair] = 0;
 }
 
+// ---------------------------------------------------------------------------
+// Speculative verification on tensor cores. One CTA per (partition, KV head,
+// KV sequence) takes all M = queries x G query rows of that KV head (row
+// r = j * G + g: draft query j, head g of the group), so each K/V tile
+// crosses HBM once for all draft rows (the per-row kernel above reads it
+// once per row). Warp w owns rows 16w..16w+15. Per 32-position tile, staged
+// in shared memory through a three-stage cp.async ring and shared by all
+// warps:
+//   S = Q K^T   (mma.sync m16n8k16, fp16 operands, fp32 accumulation; the
+//                fp32 query is split into q_hi = fp16(q) and
+//                q_lo = fp16(q - q_hi), two MMAs, so the products keep about
+//                22 bits of the query)
+//   online softmax per row (rows of a thread: gid and gid + 8 of the
+//                fragment; row max / sum over the quad with shuffles)
+//   O += P V    (P split into fp16 hi + lo the same way; V through ldmatrix.trans)
+// Causality inside the draft: row j attends positions [0, L - (Q-1-j)).
+// Tiles in shared memory are XOR-swizzled in 16-byte chunks (chunk c of row
+// r at c ^ (r % 8)), so every ldmatrix reads eight distinct bank groups.
+// The partials go to the same slots as the per-row kernel's and the last CTA
+// of a (KV sequence, KV head) merges them in partition order.
+constexpr int VT_TILE = 32;    // positions per tile
+constexpr int VT_STAGES = 3;
+constexpr unsigned VT_MAX_ROWS = 64;  // queries x G handled by this kernel
+
+template <int HD>
+constexpr size_t vt_smem_bytes(int rw)
+{
+    return (size_t)rw * 16 * HD * 2 * sizeof(__half) + (size_t)VT_STAGES * 2 * VT_TILE * HD * sizeof(__half);
+}
+
+template <int HD>
+FYB_DEV unsigned vt_swz(unsigned r, unsigned d)  // half index of element (r, d), d % 8 == 0 for chunk starts
+{
+    return r * HD + ((((d >> 3) ^ (r & 7))) << 3) + (d & 7);
+}
+
+FYB_DEV void ldmatrix_x4_trans(unsigned (&r)[4], const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
+}
+
+// D(16x8, f32) += A(16x16, f16, row) * B(16x8, f16, col)
+FYB_DEV void mma_f16_k16(float (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+FYB_DEV void split_pack(float x0, float x1, unsigned &hi, unsigned &lo)
+{
+    const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+    const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
+    const __half2 H = __halves2half2(h0, h1), Lo = __halves2half2(l0, l1);
+    hi = *reinterpret_cast<const unsigned *>(&H);
+    lo = *reinterpret_cast<const unsigned *>(&Lo);
+}
+
+// K and V rows of positions [base, base + VT_TILE) into a stage (rows at or
+// past `end` are zero, so masked positions multiply zeros in P V).
+template <int HD, int NT>
+FYB_DEV void vt_stage_tile(__half *Ks, __half *Vs, const __half *K, const __half *V, unsigned base, unsigned end)
+{
+    constexpr int CH = HD / 8;
+    const unsigned rows = end > base ? min((unsigned)VT_TILE, end - base) : 0u;
+    for (unsigned q = threadIdx.x; q < VT_TILE * CH; q += NT) {
+        const unsigned r = q / CH, c = q % CH;
+        __half *kd = Ks + vt_swz<HD>(r, c * 8), *vd = Vs + vt_swz<HD>(r, c * 8);
+        if (r < rows) {
+            cp_async16(kd, K + (size_t)(base + r) * HD + c * 8);
+            cp_async16(vd, V + (size_t)(base + r) * HD + c * 8);
+        } else {
+            *reinterpret_cast<uint4 *>(kd) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4 *>(vd) = make_uint4(0, 0, 0, 0);
+        }
+    }
+}
+
+template <int HD, int RW>
+__global__ void __launch_bounds__(RW * 32) verify_mma_kernel(const AtParams p)
+{
+    constexpr int NT = RW * 32, NB = HD / 8;  // threads; 8-wide dimension blocks of the output
+    extern __shared__ __align__(128) unsigned char vt_smem[];
+    __half *qh = reinterpret_cast<__half *>(vt_smem);
+    __half *ql = qh + RW * 16 * HD;
+    __half *stages = ql + RW * 16 * HD;
+    __shared__ unsigned last_flag;
+
+    const unsigned sp = blockIdx.x, kh = blockIdx.y, kvs = blockIdx.z;
+    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
+    const unsigned G = p.heads / p.kv_heads, Q = p.queries, M = G * Q;
+
+    pdl_launch_dependents();
+    pdl_wait();
+    unsigned L = p.length;
+    if (p.lengths) L = p.lengths[kvs];
+    else if (p.request) L = p.request[1] + 1;
+    const unsigned chunk = (L + p.splits - 1) / p.splits;
+    const unsigned c0 = min(L, sp * chunk), c1 = min(L, c0 + chunk);
+
+    const __half *K = p.k + kvs * p.seq_stride + (size_t)kh * p.capacity * HD;
+    const __half *V = p.v + kvs * p.seq_stride + (size_t)kh * p.capacity * HD;
+    const unsigned ntiles = c1 > c0 ? (c1 - c0 + VT_TILE - 1) / VT_TILE : 0;
+    auto stage = [&](unsigned t) { return stages + (size_t)(t % VT_STAGES) * 2 * VT_TILE * HD; };
+    auto issue = [&](unsigned t) {
+        __half *Ks = stage(t);
+        vt_stage_tile<HD, NT>(Ks, Ks + VT_TILE * HD, K, V, c0 + t * VT_TILE, c1);
+        cp_async_commit();
+    };
+    for (unsigned t = 0; t + 1 < VT_STAGES && t < ntiles; ++t) issue(t);
+
+    // query rows as fp16 hi + lo (rows past M are zero)
+    for (unsigned i = threadIdx.x; i < RW * 16 * HD; i += NT) {
+        const unsigned r = i / HD, d = i % HD;
+        float x = 0.f;
+        if (r < M) {
+            const unsigned j = r / G, g = r - j * G;
+            x = p.q[(((size_t)kvs * Q + j) * p.heads + (size_t)kh * G + g) * HD + d];
+        }
+        const __half h = __float2half_rn(x);
+        qh[vt_swz<HD>(r, d)] = h;
+        ql[vt_swz<HD>(r, d)] = __float2half_rn(x - __half2float(h));
+    }
+
+    // the two rows of this thread and the positions they attend
+    const unsigned rA = warp * 16 + gid, rB = rA + 8;
+    auto row_end = [&](unsigned r) -> unsigned {
+        if (r >= M) return 0u;
+        const unsigned back = Q - 1 - r / G;
+        return min(c1, L > back ? L - back : 1u);
+    };
+    const unsigned eA = row_end(rA), eB = row_end(rB);
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+    float o[NB][4];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) o[b][0] = o[b][1] = o[b][2] = o[b][3] = 0.f;
+
+    for (unsigned it = 0; it < ntiles; ++it) {
+        if (it + 1 < ntiles) cp_async_wait<1>();
+        else cp_async_wait<0>();
+        __syncthreads();  // tile `it` visible to all warps; the stage of tile it - 1 is free
+        if (it + VT_STAGES - 1 < ntiles) issue(it + VT_STAGES - 1);
+        const __half *Ks = stage(it), *Vs = Ks + VT_TILE * HD;
+        const unsigned base = c0 + it * VT_TILE;
+
+        float s[4][4];
+#pragma unroll
+        for (int n = 0; n < 4; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+            unsigned ah[4], al[4];
+            const unsigned qr = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), qc = ks * 16 + 8 * (lane >> 4);
+            ldmatrix_x4(ah, qh + vt_swz<HD>(qr, qc));
+            ldmatrix_x4(al, ql + vt_swz<HD>(qr, qc));
+#pragma unroll
+            for (int n2 = 0; n2 < 2; ++n2) {
+                unsigned b[4];
+                const unsigned mi = lane >> 3;
+                ldmatrix_x4(b, Ks + vt_swz<HD>(16 * n2 + (lane & 7) + 8 * (mi >> 1), ks * 16 + 8 * (mi & 1)));
+                mma_f16_k16(s[2 * n2], ah, b[0], b[1]);
+                mma_f16_k16(s[2 * n2], al, b[0], b[1]);
+                mma_f16_k16(s[2 * n2 + 1], ah, b[2], b[3]);
+                mma_f16_k16(s[2 * n2 + 1], al, b[2], b[3]);
+            }
+        }
+        // mask, scale, online softmax (rows A = gid, B = gid + 8)
+        float tmA = -INFINITY, tmB = -INFINITY;
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const unsigned t = base + 8 * n + 2 * tig + e;
+                s[n][e] = t < eA ? s[n][e] * p.scale : -INFINITY;
+                s[n][2 + e] = t < eB ? s[n][2 + e] * p.scale : -INFINITY;
+                tmA = fmaxf(tmA, s[n][e]);
+                tmB = fmaxf(tmB, s[n][2 + e]);
+            }
+#pragma unroll
+        for (int x = 1; x <= 2; x <<= 1) {
+            tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, x));
+            tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, x));
+        }
+        const float nA = fmaxf(mA, tmA), nB = fmaxf(mB, tmB);
+        const float alA = nA == -INFINITY ? 1.f : expf(mA - nA), alB = nB == -INFINITY ? 1.f : expf(mB - nB);
+        float sumA = 0.f, sumB = 0.f;
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                s[n][e] = s[n][e] == -INFINITY ? 0.f : expf(s[n][e] - nA);
+                s[n][2 + e] = s[n][2 + e] == -INFINITY ? 0.f : expf(s[n][2 + e] - nB);
+                sumA += s[n][e];
+                sumB += s[n][2 + e];
+            }
+#pragma unroll
+        for (int x = 1; x <= 2; x <<= 1) {
+            sumA += __shfl_xor_sync(0xffffffffu, sumA, x);
+            sumB += __shfl_xor_sync(0xffffffffu, sumB, x);
+        }
+        lA = lA * alA + sumA;
+        lB = lB * alB + sumB;
+        mA = nA;
+        mB = nB;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            o[b][0] *= alA; o[b][1] *= alA;
+            o[b][2] *= alB; o[b][3] *= alB;
+        }
+        // O += P V, P as the A operand straight from the S fragments
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            unsigned ph[4], pl[4];
+            split_pack(s[2 * kk][0], s[2 * kk][1], ph[0], pl[0]);
+            split_pack(s[2 * kk][2], s[2 * kk][3], ph[1], pl[1]);
+            split_pack(s[2 * kk + 1][0], s[2 * kk + 1][1], ph[2], pl[2]);
+            split_pack(s[2 * kk + 1][2], s[2 * kk + 1][3], ph[3], pl[3]);
+#pragma unroll
+            for (int d2 = 0; d2 < NB / 2; ++d2) {
+                unsigned b[4];
+                const unsigned mi = lane >> 3;
+                ldmatrix_x4_trans(b, Vs + vt_swz<HD>(16 * kk + (lane & 7) + 8 * (mi & 1), 16 * d2 + 8 * (mi >> 1)));
+                mma_f16_k16(o[2 * d2], ph, b[0], b[1]);
+                mma_f16_k16(o[2 * d2], pl, b[0], b[1]);
+                mma_f16_k16(o[2 * d2 + 1], ph, b[2], b[3]);
+                mma_f16_k16(o[2 * d2 + 1], pl, b[2], b[3]);
+            }
+        }
+    }
+
+    // partial slots {o[hd], m, l} of each row, the per-row kernel's layout
+    auto slot_of = [&](unsigned r) {
+        const unsigned j = r / G, g = r - j * G;
+        const size_t pair = ((size_t)kvs * Q + j) * p.kv_heads + kh;
+        return p.partials + (pair * p.splits + sp) * (size_t)(G * (HD + 2)) + (size_t)g * (HD + 2);
+    };
+    if (rA < M) {
+        float *sl = slot_of(rA);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) { sl[8 * b + 2 * tig] = o[b][0]; sl[8 * b + 2 * tig + 1] = o[b][1]; }
+        if (tig == 0) { sl[HD] = mA; sl[HD + 1] = lA; }
+    }
+    if (rB < M) {
+        float *sl = slot_of(rB);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) { sl[8 * b + 2 * tig] = o[b][2]; sl[8 * b + 2 * tig + 1] = o[b][3]; }
+        if (tig == 0) { sl[HD] = mB; sl[HD + 1] = lB; }
+    }
+    __threadfence();
+    __syncthreads();
+    unsigned *counter = p.counters + (size_t)kvs * p.kv_heads + kh;
+    if (threadIdx.x == 0) last_flag = atomicAdd(counter, 1u) == p.splits - 1;
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    for (unsigned i = threadIdx.x; i < M * HD; i += NT) {
+        const unsigned r = i / HD, d = i % HD, j = r / G, g = r - j * G;
+        const size_t pair = ((size_t)kvs * Q + j) * p.kv_heads + kh;
+        const float *all = p.partials + pair * p.splits * (size_t)(G * (HD + 2)) + (size_t)g * (HD + 2);
+        float Mx = -INFINITY;
+        for (unsigned s2 = 0; s2 < p.splits; ++s2) Mx = fmaxf(Mx, __ldcg(all + (size_t)s2 * G * (HD + 2) + HD));
+        float acc = 0.f, den = 0.f;
+        for (unsigned s2 = 0; s2 < p.splits; ++s2) {
+            const float *sl = all + (size_t)s2 * G * (HD + 2);
+            const float ms = __ldcg(sl + HD);
+            const float f = ms == -INFINITY ? 0.f : expf(ms - Mx);
+            acc += __ldcg(sl + d) * f;
+            den += __ldcg(sl + HD + 1) * f;
+        }
+        p.out[(((size_t)kvs * Q + j) * p.heads + (size_t)kh * G + g) * HD + d] = acc / den;
+    }
+    if (threadIdx.x == 0) *counter = 0;
+}
+
+template <int HD, int RW>
+static cudaError_t launch_vt(const AtParams &p, dim3 grid, cudaStream_t s)
+{
+    const size_t smem = vt_smem_bytes<HD>(RW);
+    if (cudaFuncSetAttribute(verify_mma_kernel<HD, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+        return cudaErrorInvalidConfiguration;
+    verify_mma_kernel<HD, RW><<<grid, RW * 32, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
 size_t attention_workspace_bytes(const AttentionLaunch &L)
 {
     const unsigned G = L.heads / L.kv_heads;
@@ -313,8 +599,18 @@ int launch_attention(const AttentionLaunch &L, cudaStream_t s)
     size_t partial = (pairs * L.splits * G * (L.head_dim + 2) * sizeof(float) + 255) / 256 * 256;
     p.partials = (float *)L.workspace;
     p.counters = (unsigned *)((unsigned char *)L.workspace + partial);
-    dim3 grid(L.splits, L.kv_heads, rows);
     cudaError_t e = cudaErrorInvalidValue;
+    if (L.queries > 1 && G * L.queries <= VT_MAX_ROWS && (L.head_dim == 64 || L.head_dim == 128)) {
+        // all draft rows of a KV head in one CTA: K/V read once per draft
+        const dim3 vgrid(L.splits, L.kv_heads, L.nseq);
+        const int rw = (int)((G * L.queries + 15) / 16);
+#define FYB_VT(HDV, RWV) if (L.head_dim == HDV && rw == RWV) e = launch_vt<HDV, RWV>(p, vgrid, s);
+        FYB_VT(128, 1) FYB_VT(128, 2) FYB_VT(128, 3) FYB_VT(128, 4)
+        FYB_VT(64, 1) FYB_VT(64, 2) FYB_VT(64, 3) FYB_VT(64, 4)
+#undef FYB_VT
+        return e == cudaSuccess ? 0 : -2;
+    }
+    dim3 grid(L.splits, L.kv_heads, rows);
 #define FYB_AT(HDV, GV) if (L.head_dim == HDV && G == GV) e = launch_at<HDV, GV>(p, grid, s, L.pdl);
     FYB_AT(128, 1) FYB_AT(128, 2) FYB_AT(128, 4) FYB_AT(128, 8)
     FYB_AT(64, 1) FYB_AT(64, 2) FYB_AT(64, 4) FYB_AT(64, 8)

@@ -71,6 +71,137 @@ __global__ void gather_batch_kernel(const unsigned char *w, unsigned long long r
     }
 }
 
+// Q8_0 rows (34-byte blocks: fp16 d, 32 int8) staged in shared memory by one
+// bulk copy per CTA: a CTA takes 8 / P consecutive rows (contiguous bytes,
+// a multiple of 16 when cols % 256 == 0), warp w computes part w % P of row
+// w / P for NB vectors, lanes take whole blocks (y += d * sum q_i x_i, the
+// block sum in fp32), parts meet in shared memory and add in part order.
+// The weights cross HBM once however many vectors there are.
+constexpr unsigned Q8_WARPS = 8;
+
+template <int NB>
+__global__ void __launch_bounds__(Q8_WARPS * 32) q8_0_matmul_kernel(const unsigned char *w, unsigned rows,
+    unsigned cols, unsigned parts, const float *x, unsigned long long x_stride, float *y,
+    unsigned long long y_stride, int nb)
+{
+    extern __shared__ __align__(128) unsigned char q8s[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float red[Q8_WARPS][NB];
+    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned rpc = Q8_WARPS / parts, row0 = blockIdx.x * rpc;
+    const unsigned here = min(rpc, rows - row0);
+    const unsigned nblk = cols / 32, rb = nblk * 34;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        mbar_expect_tx(&bar, here * rb);
+        bulk_copy_g2s(q8s, w + (size_t)row0 * rb, here * rb, &bar);
+    }
+    const bool landed = mbar_wait_bounded(&bar, 0);  // a copy that never lands yields NaN rows
+    const unsigned r = warp / parts, part = warp % parts;
+    float acc[NB];
+#pragma unroll
+    for (int v = 0; v < NB; ++v) acc[v] = landed ? 0.f : __int_as_float(0x7fc00000);
+    if (landed && r < here) {
+        const unsigned char *row = q8s + (size_t)r * rb;
+        const unsigned b0 = nblk * part / parts, b1 = nblk * (part + 1) / parts;
+        for (unsigned b = b0 + lane; b < b1; b += 32) {
+            const unsigned char *blk = row + b * 34;
+            const float d = half_bits_to_float(*reinterpret_cast<const unsigned short *>(blk));
+            float q[32];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const unsigned short h = *reinterpret_cast<const unsigned short *>(blk + 2 + 2 * i);
+                q[2 * i] = (float)(signed char)(h & 0xff);
+                q[2 * i + 1] = (float)(signed char)(h >> 8);
+            }
+#pragma unroll
+            for (int v = 0; v < NB; ++v) {
+                if (v < nb) {
+                    const float4 *xv = reinterpret_cast<const float4 *>(x + v * x_stride + (size_t)b * 32);
+                    float s = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 t = __ldg(xv + j);
+                        s = fmaf(q[4 * j], t.x, s);
+                        s = fmaf(q[4 * j + 1], t.y, s);
+                        s = fmaf(q[4 * j + 2], t.z, s);
+                        s = fmaf(q[4 * j + 3], t.w, s);
+                    }
+                    acc[v] = fmaf(d, s, acc[v]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int v = 0; v < NB; ++v) acc[v] = warp_sum(acc[v]);
+    if (parts == 1) {
+        if (lane == 0 && r < here)
+#pragma unroll
+            for (int v = 0; v < NB; ++v)
+                if (v < nb) y[v * y_stride + row0 + r] = acc[v];
+        return;
+    }
+    if (lane == 0)
+#pragma unroll
+        for (int v = 0; v < NB; ++v) red[warp][v] = acc[v];
+    __syncthreads();
+    if (part == 0 && lane < (unsigned)nb && r < here) {
+        float s = 0.f;
+        for (unsigned j = 0; j < parts; ++j) s += red[warp + j][lane];
+        y[lane * y_stride + row0 + r] = s;
+    }
+}
+
+// Parts per row so that a CTA's rows fit Q8_SMEM_MAX bytes; 0 if one row
+// alone does not.
+constexpr unsigned Q8_SMEM_MAX = 100 * 1024;
+static unsigned q8_parts(size_t cols)
+{
+    const size_t rb = cols / 32 * 34;
+    for (unsigned p = 1; p <= Q8_WARPS; p *= 2)
+        if ((size_t)(Q8_WARPS / p) * rb <= Q8_SMEM_MAX) return p;
+    return 0;
+}
+
+static int launch_q8_0_matmul(const void *w, size_t rows, size_t cols, const float *x, size_t x_stride, float *y,
+    size_t y_stride, size_t batch, cudaStream_t s)
+{
+    const unsigned parts = q8_parts(cols);
+    const unsigned rpc = Q8_WARPS / parts;
+    const size_t smem = (size_t)rpc * (cols / 32 * 34);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(q8_0_matmul_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q8_SMEM_MAX) ||
+            cudaFuncSetAttribute(q8_0_matmul_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q8_SMEM_MAX) ||
+            cudaFuncSetAttribute(q8_0_matmul_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, Q8_SMEM_MAX))
+            return -2;
+        attr_set[dev] = true;
+    }
+    const unsigned blocks = (unsigned)((rows + rpc - 1) / rpc);
+    for (size_t b0 = 0; b0 < batch; b0 += 8) {
+        const int nb = (int)std::min<size_t>(8, batch - b0);
+        const float *xb = x + b0 * x_stride;
+        float *yb = y + b0 * y_stride;
+        if (nb == 1)
+            q8_0_matmul_kernel<1><<<blocks, Q8_WARPS * 32, smem, s>>>((const unsigned char *)w, (unsigned)rows,
+                (unsigned)cols, parts, xb, x_stride, yb, y_stride, nb);
+        else if (nb <= 4)
+            q8_0_matmul_kernel<4><<<blocks, Q8_WARPS * 32, smem, s>>>((const unsigned char *)w, (unsigned)rows,
+                (unsigned)cols, parts, xb, x_stride, yb, y_stride, nb);
+        else
+            q8_0_matmul_kernel<8><<<blocks, Q8_WARPS * 32, smem, s>>>((const unsigned char *)w, (unsigned)rows,
+                (unsigned)cols, parts, xb, x_stride, yb, y_stride, nb);
+        if (cudaGetLastError() != cudaSuccess) return -2;
+    }
+    return 0;
+}
+
 #define FYB_TYPE_SWITCH(type, ...)                                   \
     switch (type) {                                                  \
     case T_F32: { constexpr unsigned TT = T_F32; __VA_ARGS__; } break;  \
@@ -95,6 +226,9 @@ int launch_generic_matmul(const void *w, size_t row_bytes, size_t rows, size_t c
     const float *x, size_t x_stride, float *y, size_t y_stride, size_t batch, cudaStream_t s)
 {
     if (rows == 0 || batch == 0) return 0;
+    if (type == T_Q8_0 && cols % 256 == 0 && q8_parts(cols) && rows <= 0x7fffffffu && x_stride % 4 == 0 &&
+        (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
+        return launch_q8_0_matmul(w, rows, cols, x, x_stride, y, y_stride, batch, s);
     unsigned blocks = (unsigned)((rows + 7) / 8);
     for (size_t b0 = 0; b0 < batch; b0 += 8) {
         int nb = (int)std::min<size_t>(8, batch - b0);

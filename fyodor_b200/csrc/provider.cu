@@ -1342,6 +1342,45 @@ extern "C" int fyb_plan_tp_connect(void *opaque, const void *handles, size_t cou
     return 0;
 }
 
+extern "C" int fyb_plan_tp_connect_local(void *opaque, void *const *plans, size_t count)
+{
+    Plan *p = (Plan *)opaque;
+    if (!p || p->tp_size < 2 || p->connected || !plans || count != p->tp_size || plans[p->tp_rank] != opaque)
+        return -1;
+    for (unsigned j = 0; j < p->tp_size; ++j) {
+        const Plan *q = (const Plan *)plans[j];
+        if (!q || q->tp_size != p->tp_size || q->tp_rank != j || !q->xchg || q->xchg_bytes != p->xchg_bytes)
+            return -1;
+    }
+    DeviceScope scope(p->ctx->device);
+    for (unsigned j = 0; j < p->tp_size; ++j) {
+        const int dev = ((const Plan *)plans[j])->ctx->device;
+        if (dev == p->ctx->device) continue;
+        int can = 0;
+        if (cudaDeviceCanAccessPeer(&can, p->ctx->device, dev) != cudaSuccess || !can) { cudaGetLastError(); return -2; }
+        const cudaError_t e = cudaDeviceEnablePeerAccess(dev, 0);
+        if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) { cudaGetLastError(); return -2; }
+        cudaGetLastError();
+    }
+    std::vector<unsigned char *> peers(p->tp_size);
+    for (unsigned j = 0; j < p->tp_size; ++j) peers[j] = ((const Plan *)plans[j])->xchg;
+    if (!upload(p->peers_dev, peers.data(), p->tp_size * sizeof(void *), p->ctx->stream) ||
+        cudaStreamSynchronize(p->ctx->stream) != cudaSuccess)
+        return -2;
+    // the regions belong to the other plans: nothing to close on free
+    p->peers.assign(p->tp_size, nullptr);
+    p->peers[p->tp_rank] = p->xchg;
+    p->connected = true;
+    return 0;
+}
+
+extern "C" int fyb_plan_error(const void *opaque)
+{
+    const Plan *p = (const Plan *)opaque;
+    if (!p) return -1;
+    return p->err_host ? (int)*(volatile const unsigned *)p->err_host : 0;
+}
+
 extern "C" int fyb_plan_tp_disconnect(void *opaque)
 {
     Plan *p = (Plan *)opaque;

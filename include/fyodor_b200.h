@@ -204,6 +204,16 @@ int fyb_plan_tp_connect(void *plan, const void *handles, size_t count);
    the greedy loop return -1 without launching: what every rank does when
    another rank could not create its plan or open the regions. */
 int fyb_plan_tp_disconnect(void *plan);
+/* connects plans that live in this one process (one thread per GPU, or
+   several shards on one GPU): plans[j] is rank j's plan, count = size; the
+   regions are used through their device pointers (peer access is enabled
+   between different devices) instead of IPC handles. Connects `plan` only;
+   call it once per plan. 0, -1 invalid arguments, -2 peer access refused. */
+int fyb_plan_tp_connect_local(void *plan, void *const *plans, size_t count);
+/* the plan's device error word: 0 none, 1 a bounded wait ran out (a peer or
+   a producer never arrived), 2 non-finite logits, 4 an index out of range;
+   -1 for a NULL plan. A plan with a non-zero word has failed. */
+int fyb_plan_error(const void *plan);
 
 /* ---- synthetic GGUF-layout models (no reference counterpart) -------------
    Builds an in-memory model in the engine's own binding layout

@@ -281,3 +281,43 @@ class RefSession:
 
     def __del__(self):
         self.close()
+
+
+class RefCompute:
+    """The engine's "cpu" compute provider (backend/core/compute.c:85-99 over
+    cpu_backend.c's worker pool): matvec / matmul of GGUF weights from host
+    memory, for the CPU side of the matvec benchmark configurations."""
+
+    def __init__(self, provider="cpu"):
+        self.ptr = ref().nya_compute_create_for(provider.encode())
+        if not self.ptr:
+            raise RuntimeError("engine provider %s unavailable" % provider)
+
+    def matmul(self, data, rows, cols, type_id, xs, batch):
+        """y[batch][rows] = W x for each of the batch rows of xs; None on -1."""
+        xs = np.ascontiguousarray(xs, np.float32)
+        y = np.empty((batch, rows), np.float32)
+        if batch == 1:
+            r = ref().nya_compute_matvec_typed(self.ptr, _arr(data), rows, cols, type_id, _arr(xs), _arr(y))
+        else:
+            r = ref().nya_compute_matmul_typed(self.ptr, _arr(data), rows, cols, type_id, _arr(xs), _arr(y), batch)
+        return y if r == 0 else None
+
+    def time(self, data, rows, cols, type_id, xs, batch, seconds=0.5, max_calls=50):
+        """Microseconds per call: one warm-up call, then calls until `seconds`
+        have passed (at least two)."""
+        import time
+        assert self.matmul(data, rows, cols, type_id, xs, batch) is not None
+        n, t0 = 0, time.perf_counter()
+        while n < 2 or (n < max_calls and time.perf_counter() - t0 < seconds):
+            self.matmul(data, rows, cols, type_id, xs, batch)
+            n += 1
+        return (time.perf_counter() - t0) / n * 1e6
+
+    def close(self):
+        if self.ptr:
+            ref().nya_compute_free(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        self.close()

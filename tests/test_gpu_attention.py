@@ -102,6 +102,24 @@ def test_verify_draft_of_8(hd, heads, kv_heads):
     run_verify([8, 9, 40, 300, 1000], 8, heads, kv_heads, hd, 1024, 8, seed=hd)
 
 
+@pytest.mark.parametrize("queries,heads,kv_heads,hd", [(5, 32, 8, 128), (16, 32, 8, 128), (3, 8, 8, 64),
+                                                      (17, 32, 8, 128)])
+def test_verify_row_counts(queries, heads, kv_heads, hd):
+    """Query rows (queries x group) that are not a multiple of the 16-row
+    MMA tile (5 x 4 = 20, 3 x 1), the largest the shared-tile kernel takes
+    (16 x 4 = 64), and one above it (17 x 4) that runs a CTA per row."""
+    run_verify([queries, queries + 1, 100, 1023], queries, heads, kv_heads, hd, 1024, 5, seed=queries + hd)
+
+
+@pytest.mark.parametrize("splits", [1, 3, 16])
+def test_verify_c4_subset(splits):
+    """C4's speculative-verify variant (32/8 heads, hd 128, 8 draft rows)
+    with lengths up to 32768 and several partition counts."""
+    rng = np.random.default_rng(91)
+    lengths = [int(x) for x in rng.integers(128, 32769, size=3)] + [32768]
+    run_verify(lengths, 8, 32, 8, 128, 32768, splits, seed=splits)
+
+
 def test_verify_one_query_is_decode():
     """queries == 1 is plain decode attention."""
     run_verify([1, 77, 512], 1, 32, 8, 128, 512, 4, seed=3)

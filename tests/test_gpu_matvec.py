@@ -130,6 +130,32 @@ def test_projection_sweep(provider, type_id, rows, cols):
             assert np.all(err <= 1e-3 * (1 + np.abs(s[b]))), (batch, b)
 
 
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (1000, 14336), (37, 32768)])
+def test_q8_0_matvec(provider, rows, cols):
+    """C1 (Q8_0 4096x4096, BASELINE value distribution: int8 uniform in
+    [-127, 127], d = |N(0,1)| * 0.01) and row widths that split a row over 2
+    and 4 warps; batches 1, 5 and 8 through the engine's matvec / matmul.
+    Bounds as in test_projection_sweep, and the engine's own scalar Q8_0
+    matvec (oracle.matvec, llm_quant.c:145-312) within 1e-4 relative."""
+    nbytes = rows * F.row_bytes(F.Q8_0, cols)
+    data = np.empty(nbytes, np.uint8)
+    F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, F.Q8_0, 2024, rows * 7 + cols)
+    rng = np.random.default_rng(rows * 3 + cols)
+    xs = rng.standard_normal((8, cols)).astype(np.float32)
+    s, mag = double_reference(data, F.Q8_0, xs, cols, rows)
+    e0 = O.matvec(data, F.Q8_0, xs[0], cols, rows)
+    y = provider.matvec(data, rows, cols, F.Q8_0, xs[0])
+    assert y is not None
+    assert np.all(np.abs(y.astype(np.float64) - s[0]) <= 1e-6 * (1 + mag[0]))
+    assert np.all(np.abs(y - e0) <= 1e-4 * (1 + np.abs(e0)))
+    for batch in (5, 8):
+        y = provider.matmul(data, rows, cols, F.Q8_0, xs[:batch], batch)
+        assert y is not None
+        for b in range(batch):
+            err = np.abs(y[b].astype(np.float64) - s[b])
+            assert np.all(err <= 1e-6 * (1 + mag[b])), (batch, b)
+
+
 def test_dequantize_bit_exact_all_types():
     import torch
     for type_id in [F.F32, F.F16, F.BF16, F.Q4_0, F.Q8_0, F.Q4_K, F.Q6_K]:
