@@ -479,7 +479,7 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def attention_c4(reps=20, warmup=3, splits_decode=16, splits_verify=4):
+def attention_c4(reps=20, warmup=3, splits_decode=16, splits_verify=8, nseq=32):
     """The ragged-batch attention configuration: 32 sequences with context
     lengths uniform in [128, 32768] (seeded), 32 query / 8 KV heads, head_dim
     128, fp16 K/V; decode (one query per sequence) and speculative
@@ -489,7 +489,7 @@ def attention_c4(reps=20, warmup=3, splits_decode=16, splits_verify=4):
     import ctypes as C
     import torch
     import fyodor_b200 as F
-    nseq, heads, kvh, hd, cap = 32, 32, 8, 128, 32768
+    heads, kvh, hd, cap = 32, 8, 128, 32768
     rng = np.random.default_rng(1234)
     lengths = rng.integers(128, cap + 1, size=nseq).astype(np.int32)
     g = torch.Generator(device="cuda").manual_seed(1234)
@@ -537,17 +537,27 @@ def _cpu_compute():
 
 
 def _time_device(call, copies, reps, warmup):
-    """Milliseconds per call(copy) over CUDA events, rotating over `copies`."""
+    """Milliseconds per call(copy) of device time, rotating over `copies`:
+    the `reps` calls are captured once in a CUDA graph and the graph replay
+    is timed with CUDA events, so the host's per-call cost (ctypes, argument
+    checks, launch API) does not pace the GPU for kernels of a few us."""
     import torch
+    reps = max(reps, len(copies))  # every copy once per replay: the replays stream more than L2 holds
     for i in range(warmup):
         assert call(copies[i % len(copies)]) == 0
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(reps):
+            assert call(copies[i % len(copies)]) == 0
+    graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(reps):
-        assert call(copies[i % len(copies)]) == 0
+    graph.replay()
     e1.record()
     torch.cuda.synchronize()
+    del graph
     return e0.elapsed_time(e1) / reps
 
 
@@ -644,6 +654,33 @@ def matvec_c1(reps=200, warmup=5, cpu=False):
                       "sample": "nya_compute_matvec_typed on a \"cpu\" context, weights in host memory"}
         ref.close()
     return out
+
+
+def run_gemm_case(case, reps):
+    """One prepared Q4_K/Q6_K product (fyb_quant_matmul_prepared) of the C2
+    sweep, `reps` launches after 3 warm-up launches on one weight copy: the
+    small case an ncu capture of the small-batch GEMM or GEMV runs on."""
+    import ctypes as C
+    import torch
+    import fyodor_b200 as F
+    shape, tname, batch = case.split(":")
+    rows, cols = (int(v) for v in shape.split("x"))
+    t, batch = {"q4_k": F.Q4_K, "q6_k": F.Q6_K}[tname], int(batch)
+    P = lambda v: C.c_void_p(v.data_ptr())
+    stream = lambda: C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    nbytes = rows * F.row_bytes(t, cols)
+    data = np.empty(nbytes, np.uint8)
+    F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, t, 2024, rows * 7 + cols)
+    wsb = F.lib.fyb_quant_matmul_workspace(rows, cols, t, batch)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
+    dw = torch.from_numpy(data).cuda()
+    assert F.lib.fyb_quant_repack(P(dw), rows, cols, t, P(ws), wsb, stream()) == 0
+    x = torch.randn((batch, cols), device="cuda")
+    y = torch.empty((batch, rows), device="cuda")
+    ms = _time_device(lambda w: F.lib.fyb_quant_matmul_prepared(rows, cols, t, P(x), P(y), batch, P(w), wsb, stream()),
+                      [ws], reps, 3)
+    return {"gemm_case": case, "us_per_call": round(ms * 1e3, 2), "weight_bytes": nbytes,
+            "gb_s": round(nbytes / ms / 1e6, 1)}
 
 
 # ----------------------------------------------------------------------------- profiling modes
@@ -746,6 +783,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="with --eager-steps: layers of the model (small ncu cases)")
     ap.add_argument("--attention", action="store_true", help="time the ragged-batch attention configuration only")
     ap.add_argument("--matvec", action="store_true", help="time the matvec / small-batch GEMM sweep only")
+    ap.add_argument("--gemm-case", default="",
+                    help="ROWSxCOLS:TYPE:BATCH (TYPE q4_k or q6_k): time one prepared product (small ncu cases)")
+    ap.add_argument("--seqs", type=int, default=32, help="with --attention: sequences of the ragged batch")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--model", default="8b", choices=["8b", "70b"], help="70b: the tensor-parallel 70B configuration")
     ap.add_argument("--steps", type=int, default=5)
@@ -760,8 +800,10 @@ def main():
     elif args.matvec:
         print(json.dumps({"matvec_c1": matvec_c1(cpu=not args.no_cpu_baseline),
                           "matvec_c2": matvec_c2(cpu=not args.no_cpu_baseline)}))
+    elif args.gemm_case:
+        print(json.dumps(run_gemm_case(args.gemm_case, args.reps)))
     elif args.attention:
-        print(json.dumps({"attention_c4": attention_c4(reps=args.reps, warmup=3)}))
+        print(json.dumps({"attention_c4": attention_c4(reps=args.reps, warmup=3, nseq=args.seqs)}))
     elif args.eager_steps:
         run_steps_mode(args)
     elif args.trace_step:

@@ -14,8 +14,10 @@
 // slots in partition order and writes the normalized output, so the result
 // does not depend on scheduling. Nothing of size L is materialized.
 //
-// Inside a CTA (two warps: with 32 KB of stages per warp, three CTAs share an
-// SM, which measured faster than one CTA of four warps or six of one) each
+// The kernel below is the per-row form (G = 1 decode, drafts of more than
+// 64 query rows per KV head); the tensor-core kernel further down takes the
+// rest. Inside a CTA (two warps: with 32 KB of stages per warp, three CTAs
+// share an SM, which measured faster than one CTA of four warps or six of one) each
 // warp takes tiles of 32 positions (warp w: tiles w, w + 2, ...),
 // double-buffered in shared memory: while it computes one tile, the
 // K and V rows of its next tile stream in through cp.async (16-byte chunks,
@@ -264,13 +266,16 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
 }
 
 // ---------------------------------------------------------------------------
-// Speculative verification on tensor cores. One CTA per (partition, KV head,
-// KV sequence) takes all M = queries x G query rows of that KV head (row
-// r = j * G + g: draft query j, head g of the group), so each K/V tile
-// crosses HBM once for all draft rows (the per-row kernel above reads it
-// once per row). Warp w owns rows 16w..16w+15. Per 32-position tile, staged
-// in shared memory through a three-stage cp.async ring and shared by all
-// warps:
+// Decode and speculative verification on tensor cores (every shape with
+// 2 <= queries x G <= 64; the kernel above keeps G = 1 decode and larger
+// drafts). One CTA per (partition, KV head, KV sequence) takes all
+// M = queries x G query rows of that KV head (row r = j * G + g: draft query
+// j, head g of the group), so each K/V tile crosses HBM once for all of them
+// (the per-row kernel above reads it once per row). Warps (r, h): row group
+// r owns rows 16r..16r+15, half h the positions 16h..16h+15 of every
+// 32-position tile; the two halves of a row group merge their softmax
+// states at the end. Tiles are staged in shared memory through a three-stage
+// cp.async ring shared by all warps:
 //   S = Q K^T   (mma.sync m16n8k16, fp16 operands, fp32 accumulation; the
 //                fp32 query is split into q_hi = fp16(q) and
 //                q_lo = fp16(q - q_hi), two MMAs, so the products keep about
@@ -344,9 +349,9 @@ FYB_DEV void vt_stage_tile(__half *Ks, __half *Vs, const __half *K, const __half
 }
 
 template <int HD, int RW>
-__global__ void __launch_bounds__(RW * 32) verify_mma_kernel(const AtParams p)
+__global__ void __launch_bounds__(RW * 64) verify_mma_kernel(const AtParams p)
 {
-    constexpr int NT = RW * 32, NB = HD / 8;  // threads; 8-wide dimension blocks of the output
+    constexpr int NT = RW * 64, NB = HD / 8;  // threads; 8-wide dimension blocks of the output
     extern __shared__ __align__(128) unsigned char vt_smem[];
     __half *qh = reinterpret_cast<__half *>(vt_smem);
     __half *ql = qh + RW * 16 * HD;
@@ -355,6 +360,7 @@ __global__ void __launch_bounds__(RW * 32) verify_mma_kernel(const AtParams p)
 
     const unsigned sp = blockIdx.x, kh = blockIdx.y, kvs = blockIdx.z;
     const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
+    const unsigned rw = warp % RW, ph = warp / RW;  // row group; half of each tile's positions
     const unsigned G = p.heads / p.kv_heads, Q = p.queries, M = G * Q;
 
     pdl_launch_dependents();
@@ -390,7 +396,7 @@ __global__ void __launch_bounds__(RW * 32) verify_mma_kernel(const AtParams p)
     }
 
     // the two rows of this thread and the positions they attend
-    const unsigned rA = warp * 16 + gid, rB = rA + 8;
+    const unsigned rA = rw * 16 + gid, rB = rA + 8;
     auto row_end = [&](unsigned r) -> unsigned {
         if (r >= M) return 0u;
         const unsigned back = Q - 1 - r / G;
@@ -408,32 +414,28 @@ __global__ void __launch_bounds__(RW * 32) verify_mma_kernel(const AtParams p)
         __syncthreads();  // tile `it` visible to all warps; the stage of tile it - 1 is free
         if (it + VT_STAGES - 1 < ntiles) issue(it + VT_STAGES - 1);
         const __half *Ks = stage(it), *Vs = Ks + VT_TILE * HD;
-        const unsigned base = c0 + it * VT_TILE;
+        const unsigned base = c0 + it * VT_TILE + 16 * ph;  // this warp's 16 positions
 
-        float s[4][4];
+        float s[2][4];
 #pragma unroll
-        for (int n = 0; n < 4; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+        for (int n = 0; n < 2; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
-            unsigned ah[4], al[4];
-            const unsigned qr = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), qc = ks * 16 + 8 * (lane >> 4);
+            unsigned ah[4], al[4], b[4];
+            const unsigned qr = rw * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), qc = ks * 16 + 8 * (lane >> 4);
             ldmatrix_x4(ah, qh + vt_swz<HD>(qr, qc));
             ldmatrix_x4(al, ql + vt_swz<HD>(qr, qc));
-#pragma unroll
-            for (int n2 = 0; n2 < 2; ++n2) {
-                unsigned b[4];
-                const unsigned mi = lane >> 3;
-                ldmatrix_x4(b, Ks + vt_swz<HD>(16 * n2 + (lane & 7) + 8 * (mi >> 1), ks * 16 + 8 * (mi & 1)));
-                mma_f16_k16(s[2 * n2], ah, b[0], b[1]);
-                mma_f16_k16(s[2 * n2], al, b[0], b[1]);
-                mma_f16_k16(s[2 * n2 + 1], ah, b[2], b[3]);
-                mma_f16_k16(s[2 * n2 + 1], al, b[2], b[3]);
-            }
+            const unsigned mi = lane >> 3;
+            ldmatrix_x4(b, Ks + vt_swz<HD>(16 * ph + (lane & 7) + 8 * (mi >> 1), ks * 16 + 8 * (mi & 1)));
+            mma_f16_k16(s[0], ah, b[0], b[1]);
+            mma_f16_k16(s[1], ah, b[2], b[3]);
+            mma_f16_k16(s[0], al, b[0], b[1]);
+            mma_f16_k16(s[1], al, b[2], b[3]);
         }
         // mask, scale, online softmax (rows A = gid, B = gid + 8)
         float tmA = -INFINITY, tmB = -INFINITY;
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
+        for (int n = 0; n < 2; ++n)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const unsigned t = base + 8 * n + 2 * tig + e;
@@ -451,7 +453,7 @@ __global__ void __launch_bounds__(RW * 32) verify_mma_kernel(const AtParams p)
         const float alA = nA == -INFINITY ? 1.f : expf(mA - nA), alB = nB == -INFINITY ? 1.f : expf(mB - nB);
         float sumA = 0.f, sumB = 0.f;
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
+        for (int n = 0; n < 2; ++n)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 s[n][e] = s[n][e] == -INFINITY ? 0.f : expf(s[n][e] - nA);
@@ -473,44 +475,72 @@ __global__ void __launch_bounds__(RW * 32) verify_mma_kernel(const AtParams p)
             o[b][0] *= alA; o[b][1] *= alA;
             o[b][2] *= alB; o[b][3] *= alB;
         }
-        // O += P V, P as the A operand straight from the S fragments
+        // O += P V over this warp's 16 positions, P as the A operand straight
+        // from the S fragments
+        unsigned ph4[4], pl4[4];
+        split_pack(s[0][0], s[0][1], ph4[0], pl4[0]);
+        split_pack(s[0][2], s[0][3], ph4[1], pl4[1]);
+        split_pack(s[1][0], s[1][1], ph4[2], pl4[2]);
+        split_pack(s[1][2], s[1][3], ph4[3], pl4[3]);
 #pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-            unsigned ph[4], pl[4];
-            split_pack(s[2 * kk][0], s[2 * kk][1], ph[0], pl[0]);
-            split_pack(s[2 * kk][2], s[2 * kk][3], ph[1], pl[1]);
-            split_pack(s[2 * kk + 1][0], s[2 * kk + 1][1], ph[2], pl[2]);
-            split_pack(s[2 * kk + 1][2], s[2 * kk + 1][3], ph[3], pl[3]);
-#pragma unroll
-            for (int d2 = 0; d2 < NB / 2; ++d2) {
-                unsigned b[4];
-                const unsigned mi = lane >> 3;
-                ldmatrix_x4_trans(b, Vs + vt_swz<HD>(16 * kk + (lane & 7) + 8 * (mi & 1), 16 * d2 + 8 * (mi >> 1)));
-                mma_f16_k16(o[2 * d2], ph, b[0], b[1]);
-                mma_f16_k16(o[2 * d2], pl, b[0], b[1]);
-                mma_f16_k16(o[2 * d2 + 1], ph, b[2], b[3]);
-                mma_f16_k16(o[2 * d2 + 1], pl, b[2], b[3]);
-            }
+        for (int d2 = 0; d2 < NB / 2; ++d2) {
+            unsigned b[4];
+            const unsigned mi = lane >> 3;
+            ldmatrix_x4_trans(b, Vs + vt_swz<HD>(16 * ph + (lane & 7) + 8 * (mi & 1), 16 * d2 + 8 * (mi >> 1)));
+            mma_f16_k16(o[2 * d2], ph4, b[0], b[1]);
+            mma_f16_k16(o[2 * d2 + 1], ph4, b[2], b[3]);
+            mma_f16_k16(o[2 * d2], pl4, b[0], b[1]);
+            mma_f16_k16(o[2 * d2 + 1], pl4, b[2], b[3]);
         }
     }
 
-    // partial slots {o[hd], m, l} of each row, the per-row kernel's layout
-    auto slot_of = [&](unsigned r) {
-        const unsigned j = r / G, g = r - j * G;
-        const size_t pair = ((size_t)kvs * Q + j) * p.kv_heads + kh;
-        return p.partials + (pair * p.splits + sp) * (size_t)(G * (HD + 2)) + (size_t)g * (HD + 2);
-    };
-    if (rA < M) {
-        float *sl = slot_of(rA);
+    // the two position halves of each row group meet in shared memory (the
+    // stages are free): half 1 leaves (m, l, o) in fragment order, half 0
+    // rescales both to the common maximum and adds
+    __syncthreads();
+    float *xo = reinterpret_cast<float *>(stages) + ((size_t)rw * 32 + lane) * (NB * 4 + 4);
+    if (ph == 1) {
 #pragma unroll
-        for (int b = 0; b < NB; ++b) { sl[8 * b + 2 * tig] = o[b][0]; sl[8 * b + 2 * tig + 1] = o[b][1]; }
-        if (tig == 0) { sl[HD] = mA; sl[HD + 1] = lA; }
+        for (int b = 0; b < NB; ++b)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) xo[b * 4 + c] = o[b][c];
+        xo[NB * 4] = mA; xo[NB * 4 + 1] = mB; xo[NB * 4 + 2] = lA; xo[NB * 4 + 3] = lB;
     }
-    if (rB < M) {
-        float *sl = slot_of(rB);
+    __syncthreads();
+    if (ph == 0) {
+        const float m1A = xo[NB * 4], m1B = xo[NB * 4 + 1];
+        const float MA = fmaxf(mA, m1A), MB = fmaxf(mB, m1B);
+        const float f0A = mA == -INFINITY ? 0.f : expf(mA - MA), f1A = m1A == -INFINITY ? 0.f : expf(m1A - MA);
+        const float f0B = mB == -INFINITY ? 0.f : expf(mB - MB), f1B = m1B == -INFINITY ? 0.f : expf(m1B - MB);
 #pragma unroll
-        for (int b = 0; b < NB; ++b) { sl[8 * b + 2 * tig] = o[b][2]; sl[8 * b + 2 * tig + 1] = o[b][3]; }
-        if (tig == 0) { sl[HD] = mB; sl[HD + 1] = lB; }
+        for (int b = 0; b < NB; ++b) {
+            o[b][0] = o[b][0] * f0A + xo[b * 4] * f1A;
+            o[b][1] = o[b][1] * f0A + xo[b * 4 + 1] * f1A;
+            o[b][2] = o[b][2] * f0B + xo[b * 4 + 2] * f1B;
+            o[b][3] = o[b][3] * f0B + xo[b * 4 + 3] * f1B;
+        }
+        lA = lA * f0A + xo[NB * 4 + 2] * f1A;
+        lB = lB * f0B + xo[NB * 4 + 3] * f1B;
+        mA = MA;
+        mB = MB;
+        // partial slots {o[hd], m, l} of each row, the per-row kernel's layout
+        auto slot_of = [&](unsigned r) {
+            const unsigned j = r / G, g = r - j * G;
+            const size_t pair = ((size_t)kvs * Q + j) * p.kv_heads + kh;
+            return p.partials + (pair * p.splits + sp) * (size_t)(G * (HD + 2)) + (size_t)g * (HD + 2);
+        };
+        if (rA < M) {
+            float *sl = slot_of(rA);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) { sl[8 * b + 2 * tig] = o[b][0]; sl[8 * b + 2 * tig + 1] = o[b][1]; }
+            if (tig == 0) { sl[HD] = mA; sl[HD + 1] = lA; }
+        }
+        if (rB < M) {
+            float *sl = slot_of(rB);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) { sl[8 * b + 2 * tig] = o[b][2]; sl[8 * b + 2 * tig + 1] = o[b][3]; }
+            if (tig == 0) { sl[HD] = mB; sl[HD + 1] = lB; }
+        }
     }
     __threadfence();
     __syncthreads();
@@ -545,7 +575,7 @@ static cudaError_t launch_vt(const AtParams &p, dim3 grid, cudaStream_t s)
     if (cudaFuncSetAttribute(verify_mma_kernel<HD, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
         return cudaErrorInvalidConfiguration;
-    verify_mma_kernel<HD, RW><<<grid, RW * 32, smem, s>>>(p);
+    verify_mma_kernel<HD, RW><<<grid, RW * 64, smem, s>>>(p);
     return cudaGetLastError();
 }
 
@@ -600,8 +630,9 @@ int launch_attention(const AttentionLaunch &L, cudaStream_t s)
     p.partials = (float *)L.workspace;
     p.counters = (unsigned *)((unsigned char *)L.workspace + partial);
     cudaError_t e = cudaErrorInvalidValue;
-    if (L.queries > 1 && G * L.queries <= VT_MAX_ROWS && (L.head_dim == 64 || L.head_dim == 128)) {
-        // all draft rows of a KV head in one CTA: K/V read once per draft
+    if (G * L.queries >= 2 && G * L.queries <= VT_MAX_ROWS && (L.head_dim == 64 || L.head_dim == 128)) {
+        // all query rows of a KV head (its G heads, every draft token) in one
+        // CTA on tensor cores: K/V read once for all of them
         const dim3 vgrid(L.splits, L.kv_heads, L.nseq);
         const int rw = (int)((G * L.queries + 15) / 16);
 #define FYB_VT(HDV, RWV) if (L.head_dim == HDV && rw == RWV) e = launch_vt<HDV, RWV>(p, vgrid, s);

@@ -1006,58 +1006,51 @@ FYB_DEV bool attention_item(const DecodeParams &p, unsigned step, unsigned l, un
         return true;
     }
     if (dt) drecord(p, 26, globaltimer());
-    // merge: the partitions' maxima and sums polled into shared memory (one
-    // word per thread), then every output element polls its S - 1 values;
-    // the sums run in partition order
+    // merge: the other partitions' slots polled into shared memory, eight
+    // words in flight per thread (slot s2 at index (s2 - 1) * SLOT), this
+    // partition's own result stays in registers; then the sums run in
+    // partition order
     __syncthreads();  // every thread has read the warps' outputs
-    float *sM = sm.wo, *sD = sm.wo + ATT_MAX_PARTS * G;
+    float *const sp_all = sm.wo;
     bool mok = true;
+    const unsigned n = (S - 1) * SLOT;
+    for (unsigned q0 = threadIdx.x; q0 < n; q0 += 8 * QG_THREADS) {
+        u64 w[8];
 #pragma unroll
-    for (unsigned r = 0; r < EPT; ++r) {
-        const unsigned e = threadIdx.x + r * QG_THREADS, g = e / HD, dd = e % HD;
-        if (e < G * HD && dd == 0) { sM[g] = M0[r]; sD[g] = den0[r]; }
-    }
-    for (unsigned i = threadIdx.x; i < (S - 1) * G * 2; i += QG_THREADS) {
-        const unsigned s2 = 1 + i / (2 * G), gg = (i / 2) % G, w2 = i & 1;
-        float v = 0.f;
-        mok = mok && ll_wait1(p, parts_all + (size_t)s2 * SLOT + gg * (HD + 2) + HD + w2, tag, v);
-        (w2 ? sD : sM)[s2 * G + gg] = v;
+        for (unsigned j = 0; j < 8; ++j) {
+            const unsigned q = q0 + j * QG_THREADS;
+            w[j] = q < n ? ll_get(parts_all + SLOT + q) : 0ull;
+        }
+#pragma unroll
+        for (unsigned j = 0; j < 8; ++j) {
+            const unsigned q = q0 + j * QG_THREADS;
+            if (q >= n) break;
+            float v;
+            if (ll_ok(w[j], tag)) v = ll_val(w[j]);
+            else if (!ll_wait1(p, parts_all + SLOT + q, tag, v)) mok = false;
+            sp_all[q] = v;
+        }
     }
     if (__syncthreads_or(!mok)) return false;
 #pragma unroll
     for (unsigned r = 0; r < EPT; ++r) {
         const unsigned e = threadIdx.x + r * QG_THREADS, g = e / HD, dd = e % HD;
         if (e >= G * HD) continue;
-        float M = -INFINITY;
-        for (unsigned s2 = 0; s2 < S; ++s2) M = fmaxf(M, sM[s2 * G + g]);
+        const float *gs = sp_all + g * (HD + 2);  // gs[(s2 - 1) * SLOT + k]: partition s2 >= 1
+        float M = M0[r];
+        for (unsigned s2 = 1; s2 < S; ++s2) M = fmaxf(M, gs[(s2 - 1) * SLOT + HD]);
         float acc = 0.f, den = 0.f;
-        // partitions in order, four loads in flight at a time
-        for (unsigned s0 = 0; s0 < S; s0 += 4) {
-            u64 w[4];
-#pragma unroll
-            for (unsigned j = 0; j < 4; ++j) {
-                const unsigned s2 = s0 + j;
-                w[j] = s2 == 0 ? ll_pack(acc0[r], tag)
-                     : s2 < S ? ll_get(parts_all + (size_t)s2 * SLOT + g * (HD + 2) + dd) : ll_pack(0.f, tag);
-            }
-#pragma unroll
-            for (unsigned j = 0; j < 4; ++j) {
-                const unsigned s2 = s0 + j;
-                if (s2 >= S) break;
-                float v;
-                if (ll_ok(w[j], tag)) v = ll_val(w[j]);
-                else if (!ll_wait1(p, parts_all + (size_t)s2 * SLOT + g * (HD + 2) + dd, tag, v)) mok = false;
-                const float ms = sM[s2 * G + g];
-                const float f = ms == -INFINITY ? 0.f : expf(ms - M);
-                acc = fmaf(v, f, acc);
-                den = fmaf(sD[s2 * G + g], f, den);
-            }
+        for (unsigned s2 = 0; s2 < S; ++s2) {
+            const float ms = s2 ? gs[(s2 - 1) * SLOT + HD] : M0[r];
+            const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+            acc = fmaf(s2 ? gs[(s2 - 1) * SLOT + dd] : acc0[r], f, acc);
+            den = fmaf(s2 ? gs[(s2 - 1) * SLOT + HD + 1] : den0[r], f, den);
         }
         ll_put(p.ll.attn + ((size_t)kvh * G + g) * HD + dd, acc / den, tag);
     }
     if (dt) drecord(p, 27, globaltimer());
-    // a failed wait raised the abort word; the caller's barrier sees it
-    return __syncthreads_or(!mok) == 0;
+    __syncthreads();  // the shared scratch is free again
+    return true;
 }
 
 template <int HD, int G>

@@ -72,24 +72,27 @@ __global__ void gather_batch_kernel(const unsigned char *w, unsigned long long r
 }
 
 // Q8_0 rows (34-byte blocks: fp16 d, 32 int8) staged in shared memory by one
-// bulk copy per CTA: a CTA takes 8 / P consecutive rows (contiguous bytes,
-// a multiple of 16 when cols % 256 == 0), warp w computes part w % P of row
-// w / P for NB vectors, lanes take whole blocks (y += d * sum q_i x_i, the
-// block sum in fp32), parts meet in shared memory and add in part order.
-// The weights cross HBM once however many vectors there are.
+// bulk copy per CTA: a CTA takes R consecutive rows (contiguous bytes, a
+// multiple of 16 when cols % 256 == 0; R <= 8 so that they fit
+// Q8_SMEM_MAX). Warp w takes the blocks [nblk w / 8, nblk (w + 1) / 8) of all
+// R rows, each half-warp one block at a time: lane l holds values
+// 2 (l % 16), +1 of x for NB vectors (loaded once per warp, coalesced) and
+// accumulates (d q) x in fp32 for every row (d * q is exact). The warps'
+// sums meet in shared memory and add in warp order. The weights cross HBM
+// once however many vectors there are.
 constexpr unsigned Q8_WARPS = 8;
+constexpr unsigned Q8_SMEM_MAX = 100 * 1024;
 
 template <int NB>
 __global__ void __launch_bounds__(Q8_WARPS * 32) q8_0_matmul_kernel(const unsigned char *w, unsigned rows,
-    unsigned cols, unsigned parts, const float *x, unsigned long long x_stride, float *y,
+    unsigned cols, unsigned rpc, const float *x, unsigned long long x_stride, float *y,
     unsigned long long y_stride, int nb)
 {
     extern __shared__ __align__(128) unsigned char q8s[];
     __shared__ __align__(8) uint64_t bar;
-    __shared__ float red[Q8_WARPS][NB];
-    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const unsigned rpc = Q8_WARPS / parts, row0 = blockIdx.x * rpc;
-    const unsigned here = min(rpc, rows - row0);
+    __shared__ float red[Q8_WARPS][Q8_WARPS][NB];  // [warp][row][vector]
+    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5, hl = lane & 15;
+    const unsigned row0 = blockIdx.x * rpc, here = min(rpc, rows - row0);
     const unsigned nblk = cols / 32, rb = nblk * 34;
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
@@ -101,77 +104,65 @@ __global__ void __launch_bounds__(Q8_WARPS * 32) q8_0_matmul_kernel(const unsign
         bulk_copy_g2s(q8s, w + (size_t)row0 * rb, here * rb, &bar);
     }
     const bool landed = mbar_wait_bounded(&bar, 0);  // a copy that never lands yields NaN rows
-    const unsigned r = warp / parts, part = warp % parts;
-    float acc[NB];
+    float acc[Q8_WARPS][NB];
 #pragma unroll
-    for (int v = 0; v < NB; ++v) acc[v] = landed ? 0.f : __int_as_float(0x7fc00000);
-    if (landed && r < here) {
-        const unsigned char *row = q8s + (size_t)r * rb;
-        const unsigned b0 = nblk * part / parts, b1 = nblk * (part + 1) / parts;
-        for (unsigned b = b0 + lane; b < b1; b += 32) {
-            const unsigned char *blk = row + b * 34;
-            const float d = half_bits_to_float(*reinterpret_cast<const unsigned short *>(blk));
-            float q[32];
+    for (int r = 0; r < (int)Q8_WARPS; ++r)
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const unsigned short h = *reinterpret_cast<const unsigned short *>(blk + 2 + 2 * i);
-                q[2 * i] = (float)(signed char)(h & 0xff);
-                q[2 * i + 1] = (float)(signed char)(h >> 8);
-            }
+        for (int v = 0; v < NB; ++v) acc[r][v] = landed ? 0.f : __int_as_float(0x7fc00000);
+    if (landed) {
+        const unsigned b0 = nblk * warp / Q8_WARPS, b1 = nblk * (warp + 1) / Q8_WARPS;
+        for (unsigned b = b0 + (lane >> 4); b < b1; b += 2) {
+            float2 xv[NB];
 #pragma unroll
-            for (int v = 0; v < NB; ++v) {
-                if (v < nb) {
-                    const float4 *xv = reinterpret_cast<const float4 *>(x + v * x_stride + (size_t)b * 32);
-                    float s = 0.f;
+            for (int v = 0; v < NB; ++v)
+                xv[v] = v < nb ? __ldg(reinterpret_cast<const float2 *>(x + v * x_stride + (size_t)b * 32 + 2 * hl))
+                               : make_float2(0.f, 0.f);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float4 t = __ldg(xv + j);
-                        s = fmaf(q[4 * j], t.x, s);
-                        s = fmaf(q[4 * j + 1], t.y, s);
-                        s = fmaf(q[4 * j + 2], t.z, s);
-                        s = fmaf(q[4 * j + 3], t.w, s);
+            for (int r = 0; r < (int)Q8_WARPS; ++r) {
+                if ((unsigned)r < here) {
+                    const unsigned char *blk = q8s + (size_t)r * rb + b * 34;
+                    const float d = half_bits_to_float(*reinterpret_cast<const unsigned short *>(blk));
+                    const unsigned short h = *reinterpret_cast<const unsigned short *>(blk + 2 + 2 * hl);
+                    const float q0 = d * (float)(signed char)(h & 0xff), q1 = d * (float)(signed char)(h >> 8);
+#pragma unroll
+                    for (int v = 0; v < NB; ++v) {
+                        acc[r][v] = fmaf(q0, xv[v].x, acc[r][v]);
+                        acc[r][v] = fmaf(q1, xv[v].y, acc[r][v]);
                     }
-                    acc[v] = fmaf(d, s, acc[v]);
                 }
             }
         }
     }
 #pragma unroll
-    for (int v = 0; v < NB; ++v) acc[v] = warp_sum(acc[v]);
-    if (parts == 1) {
-        if (lane == 0 && r < here)
+    for (int r = 0; r < (int)Q8_WARPS; ++r)
 #pragma unroll
-            for (int v = 0; v < NB; ++v)
-                if (v < nb) y[v * y_stride + row0 + r] = acc[v];
-        return;
-    }
-    if (lane == 0)
-#pragma unroll
-        for (int v = 0; v < NB; ++v) red[warp][v] = acc[v];
+        for (int v = 0; v < NB; ++v) {
+            const float t = warp_sum(acc[r][v]);
+            if (lane == 0) red[warp][r][v] = t;
+        }
     __syncthreads();
-    if (part == 0 && lane < (unsigned)nb && r < here) {
-        float s = 0.f;
-        for (unsigned j = 0; j < parts; ++j) s += red[warp + j][lane];
-        y[lane * y_stride + row0 + r] = s;
+    for (unsigned t = threadIdx.x; t < here * (unsigned)nb; t += blockDim.x) {
+        const unsigned r = t / nb, v = t % nb;
+        float sum = 0.f;
+        for (unsigned w2 = 0; w2 < Q8_WARPS; ++w2) sum += red[w2][r][v];
+        y[v * y_stride + row0 + r] = sum;
     }
 }
 
-// Parts per row so that a CTA's rows fit Q8_SMEM_MAX bytes; 0 if one row
-// alone does not.
-constexpr unsigned Q8_SMEM_MAX = 100 * 1024;
-static unsigned q8_parts(size_t cols)
+// Rows per CTA (a power of two up to 8) so that they fit Q8_SMEM_MAX bytes;
+// 0 if one row alone does not.
+static unsigned q8_rows_per_cta(size_t cols)
 {
     const size_t rb = cols / 32 * 34;
-    for (unsigned p = 1; p <= Q8_WARPS; p *= 2)
-        if ((size_t)(Q8_WARPS / p) * rb <= Q8_SMEM_MAX) return p;
+    for (unsigned r = Q8_WARPS; r >= 1; r /= 2)
+        if ((size_t)r * rb <= Q8_SMEM_MAX) return r;
     return 0;
 }
 
 static int launch_q8_0_matmul(const void *w, size_t rows, size_t cols, const float *x, size_t x_stride, float *y,
     size_t y_stride, size_t batch, cudaStream_t s)
 {
-    const unsigned parts = q8_parts(cols);
-    const unsigned rpc = Q8_WARPS / parts;
+    const unsigned rpc = q8_rows_per_cta(cols);
     const size_t smem = (size_t)rpc * (cols / 32 * 34);
     static bool attr_set[64] = {};
     int dev = 0;
@@ -190,13 +181,13 @@ static int launch_q8_0_matmul(const void *w, size_t rows, size_t cols, const flo
         float *yb = y + b0 * y_stride;
         if (nb == 1)
             q8_0_matmul_kernel<1><<<blocks, Q8_WARPS * 32, smem, s>>>((const unsigned char *)w, (unsigned)rows,
-                (unsigned)cols, parts, xb, x_stride, yb, y_stride, nb);
+                (unsigned)cols, rpc, xb, x_stride, yb, y_stride, nb);
         else if (nb <= 4)
             q8_0_matmul_kernel<4><<<blocks, Q8_WARPS * 32, smem, s>>>((const unsigned char *)w, (unsigned)rows,
-                (unsigned)cols, parts, xb, x_stride, yb, y_stride, nb);
+                (unsigned)cols, rpc, xb, x_stride, yb, y_stride, nb);
         else
             q8_0_matmul_kernel<8><<<blocks, Q8_WARPS * 32, smem, s>>>((const unsigned char *)w, (unsigned)rows,
-                (unsigned)cols, parts, xb, x_stride, yb, y_stride, nb);
+                (unsigned)cols, rpc, xb, x_stride, yb, y_stride, nb);
         if (cudaGetLastError() != cudaSuccess) return -2;
     }
     return 0;
@@ -226,7 +217,7 @@ int launch_generic_matmul(const void *w, size_t row_bytes, size_t rows, size_t c
     const float *x, size_t x_stride, float *y, size_t y_stride, size_t batch, cudaStream_t s)
 {
     if (rows == 0 || batch == 0) return 0;
-    if (type == T_Q8_0 && cols % 256 == 0 && q8_parts(cols) && rows <= 0x7fffffffu && x_stride % 4 == 0 &&
+    if (type == T_Q8_0 && cols % 256 == 0 && q8_rows_per_cta(cols) && rows <= 0x7fffffffu && x_stride % 4 == 0 &&
         (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
         return launch_q8_0_matmul(w, rows, cols, x, x_stride, y, y_stride, batch, s);
     unsigned blocks = (unsigned)((rows + 7) / 8);

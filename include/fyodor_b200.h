@@ -46,12 +46,17 @@ size_t fyb_quant_matmul_workspace(size_t rows, size_t columns, unsigned type, si
 /* Y[b][r] = sum_k W[r][k] * X[b][k] on the device, the batched form of the
    engine's nya_compute_matmul_typed (backend/include/compute.h:80-83): W in
    GGUF row-major block storage, X batch-major [batch][columns], Y
-   [batch][rows]. Q4_K/Q6_K with batch <= 2 run the tensor-core GEMV; every
+   [batch][rows]. Q4_K/Q6_K run the tensor-core GEMV at batch 1-2 and the
+   small-batch GEMM above it (up to 16 vectors per launch, every weight unit
+   read once); Q8_0 with columns a multiple of 256 (and 16-byte aligned W and
+   X) runs the bulk-staged Q8_0 kernel (up to 8 vectors per launch); every
    other case runs the type-generic kernel. `workspace` must hold
-   fyb_quant_matmul_workspace() bytes, all zero before the first call; calls
-   leave it zeroed. Q6_K weights are repacked into the workspace's tail on
-   every call, so this entry point is for testing, not a hot loop (plans
-   repack once). */
+   fyb_quant_matmul_workspace() bytes: [counters][stream-K partials][repacked
+   units][small-batch GEMM scratch], the counters zero before the first call
+   (calls return them to zero). K-quant weights are repacked into the
+   workspace on every call, so this entry point is for testing, not a hot
+   loop (plans repack once). The layout depends on the device's SM count:
+   use a workspace on the device it was sized for. */
 int fyb_quant_matmul(const void *weights, size_t rows, size_t columns, unsigned type,
     const float *x, float *y, size_t batch, void *workspace, size_t workspace_bytes, void *stream);
 
@@ -71,7 +76,10 @@ int fyb_quant_matmul_prepared(size_t rows, size_t columns, unsigned type, const 
    k,v per sequence s at k + s*seq_stride: [kv_heads][capacity][head_dim] f16
    lengths[s] = attended positions of sequence s (device array, 1..capacity).
    splits = context partitions per (sequence, kv head); 0 picks a default.
-   workspace: fyb_attention_workspace() bytes, zero before the first call. */
+   workspace: fyb_attention_workspace() bytes, zero before the first call.
+   With 2..64 query heads per KV head one CTA computes all of them on tensor
+   cores (fp16 MMAs on hi/lo splits of q and of the probabilities, fp32
+   accumulation), reading each K/V tile once. */
 size_t fyb_attention_workspace(unsigned nseq, unsigned heads, unsigned kv_heads, unsigned head_dim, unsigned splits);
 int fyb_attention_decode(const float *q, const void *k_cache, const void *v_cache, size_t seq_stride,
     const unsigned *lengths, unsigned nseq, unsigned heads, unsigned kv_heads, unsigned head_dim,
@@ -85,7 +93,10 @@ int fyb_attention_decode(const float *q, const void *k_cache, const void *v_cach
    [nseq][queries][heads][head_dim]; lengths[s] counts sequence s's cached
    positions including its draft (>= queries), and query j attends positions
    0 .. lengths[s] - queries + j. workspace: fyb_attention_workspace(nseq *
-   queries, ...) bytes, zero before the first call. nseq * queries <= 65535. */
+   queries, ...) bytes, zero before the first call. nseq * queries <= 65535.
+   When queries x (heads / kv_heads) <= 64 one CTA takes all draft rows of a
+   KV head and reads each K/V tile once for them (the tensor-core kernel of
+   fyb_attention_decode); otherwise every row streams the cache on its own. */
 int fyb_attention_verify(const float *q, const void *k_cache, const void *v_cache, size_t seq_stride,
     const unsigned *lengths, unsigned nseq, unsigned queries, unsigned heads, unsigned kv_heads, unsigned head_dim,
     unsigned capacity, float scale, float *out, unsigned splits, void *workspace, size_t workspace_bytes,
