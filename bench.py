@@ -657,7 +657,8 @@ def matvec_c1(reps=200, warmup=5, cpu=False):
 
 
 def run_gemm_case(case, reps):
-    """One prepared Q4_K/Q6_K product (fyb_quant_matmul_prepared) of the C2
+    """One prepared Q4_K/Q6_K product (fyb_quant_matmul_prepared) or one Q8_0
+    product (fyb_quant_matmul) of the C1/C2
     sweep, `reps` launches after 3 warm-up launches on one weight copy: the
     small case an ncu capture of the small-batch GEMM or GEMV runs on."""
     import ctypes as C
@@ -665,22 +666,70 @@ def run_gemm_case(case, reps):
     import fyodor_b200 as F
     shape, tname, batch = case.split(":")
     rows, cols = (int(v) for v in shape.split("x"))
-    t, batch = {"q4_k": F.Q4_K, "q6_k": F.Q6_K}[tname], int(batch)
+    t, batch = {"q4_k": F.Q4_K, "q6_k": F.Q6_K, "q8_0": F.Q8_0}[tname], int(batch)
     P = lambda v: C.c_void_p(v.data_ptr())
     stream = lambda: C.c_void_p(torch.cuda.current_stream().cuda_stream)
     nbytes = rows * F.row_bytes(t, cols)
     data = np.empty(nbytes, np.uint8)
     F.lib.fyb_synth_fill(C.c_void_p(data.ctypes.data), rows, cols, t, 2024, rows * 7 + cols)
+    x = torch.randn((batch, cols), device="cuda")
+    y = torch.empty((batch, rows), device="cuda")
+    if t == F.Q8_0:  # no repack: the Q8_0 kernel reads the GGUF rows
+        dw = torch.from_numpy(data).cuda()
+        ms = _time_device(lambda w: F.lib.fyb_quant_matmul(P(w), rows, cols, t, P(x), P(y), batch, None, 0, stream()),
+                          [dw], reps, 3)
+        return {"gemm_case": case, "us_per_call": round(ms * 1e3, 2), "weight_bytes": nbytes,
+                "gb_s": round(nbytes / ms / 1e6, 1)}
     wsb = F.lib.fyb_quant_matmul_workspace(rows, cols, t, batch)
     ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
     dw = torch.from_numpy(data).cuda()
     assert F.lib.fyb_quant_repack(P(dw), rows, cols, t, P(ws), wsb, stream()) == 0
-    x = torch.randn((batch, cols), device="cuda")
-    y = torch.empty((batch, rows), device="cuda")
     ms = _time_device(lambda w: F.lib.fyb_quant_matmul_prepared(rows, cols, t, P(x), P(y), batch, P(w), wsb, stream()),
                       [ws], reps, 3)
     return {"gemm_case": case, "us_per_call": round(ms * 1e3, 2), "weight_bytes": nbytes,
             "gb_s": round(nbytes / ms / 1e6, 1)}
+
+
+def run_allreduce_probe(args):
+    """The exchange of the reference design for tensor parallelism (one NCCL
+    all-reduce of the d-wide residual per attention block and per MLP block,
+    64 per 8B token): under torchrun, every rank times `--reps` all-reduces
+    of 4096 fp32 values captured in a CUDA graph, max over ranks. Prints us
+    per all-reduce and the exchange time alone per 8B token."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    x = torch.ones(CFG8B["embedding"], device="cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(5):
+            dist.all_reduce(x)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(args.reps):
+            dist.all_reduce(x)
+    graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record()
+        graph.replay()
+        e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.reps
+    t = torch.tensor([us], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del graph
+    if rank == 0:
+        print(json.dumps({"allreduce_probe": {"ranks": world, "bytes": 4 * CFG8B["embedding"], "us": round(float(t.item()), 2),
+                                              "per_8b_token_us": round(float(t.item()) * 2 * CFG8B["layers"], 1)}}))
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 # ----------------------------------------------------------------------------- profiling modes
@@ -784,8 +833,10 @@ def main():
     ap.add_argument("--attention", action="store_true", help="time the ragged-batch attention configuration only")
     ap.add_argument("--matvec", action="store_true", help="time the matvec / small-batch GEMM sweep only")
     ap.add_argument("--gemm-case", default="",
-                    help="ROWSxCOLS:TYPE:BATCH (TYPE q4_k or q6_k): time one prepared product (small ncu cases)")
+                    help="ROWSxCOLS:TYPE:BATCH (TYPE q4_k, q6_k or q8_0): time one product (small ncu cases)")
     ap.add_argument("--seqs", type=int, default=32, help="with --attention: sequences of the ragged batch")
+    ap.add_argument("--allreduce-probe", action="store_true",
+                    help="under torchrun: time the reference design's NCCL all-reduce of the residual")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--model", default="8b", choices=["8b", "70b"], help="70b: the tensor-parallel 70B configuration")
     ap.add_argument("--steps", type=int, default=5)
@@ -800,6 +851,8 @@ def main():
     elif args.matvec:
         print(json.dumps({"matvec_c1": matvec_c1(cpu=not args.no_cpu_baseline),
                           "matvec_c2": matvec_c2(cpu=not args.no_cpu_baseline)}))
+    elif args.allreduce_probe:
+        run_allreduce_probe(args)
     elif args.gemm_case:
         print(json.dumps(run_gemm_case(args.gemm_case, args.reps)))
     elif args.attention:

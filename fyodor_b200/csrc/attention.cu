@@ -289,13 +289,23 @@ __global__ void __launch_bounds__(AT_THREADS) attention_kernel(const AtParams p)
 // The partials go to the same slots as the per-row kernel's and the last CTA
 // of a (KV sequence, KV head) merges them in partition order.
 constexpr int VT_TILE = 32;    // positions per tile
-constexpr int VT_STAGES = 3;
+constexpr int VT_STAGES = 2;  // measured: 494 us for C4 decode against 605 with three (more CTAs per SM)
 constexpr unsigned VT_MAX_ROWS = 64;  // queries x G handled by this kernel
 
+// Dynamic shared memory: the query rows (hi, lo) and, in the same region
+// after the last tile, the stages or the half-merge area (per thread of a
+// row group: HD / 2 output values, two maxima, two sums), whichever is larger.
+template <int HD>
+constexpr size_t vt_stage_area(int rw)
+{
+    return (size_t)VT_STAGES * 2 * VT_TILE * HD * sizeof(__half) > (size_t)rw * 32 * (HD / 2 + 4) * sizeof(float)
+               ? (size_t)VT_STAGES * 2 * VT_TILE * HD * sizeof(__half)
+               : (size_t)rw * 32 * (HD / 2 + 4) * sizeof(float);
+}
 template <int HD>
 constexpr size_t vt_smem_bytes(int rw)
 {
-    return (size_t)rw * 16 * HD * 2 * sizeof(__half) + (size_t)VT_STAGES * 2 * VT_TILE * HD * sizeof(__half);
+    return (size_t)rw * 16 * HD * 2 * sizeof(__half) + vt_stage_area<HD>(rw);
 }
 
 template <int HD>
@@ -408,17 +418,23 @@ __global__ void __launch_bounds__(RW * 64) verify_mma_kernel(const AtParams p)
 #pragma unroll
     for (int b = 0; b < NB; ++b) o[b][0] = o[b][1] = o[b][2] = o[b][3] = 0.f;
 
+    static_assert(VT_STAGES == 2 || VT_STAGES == 3, "the waits below cover two or three stages");
     for (unsigned it = 0; it < ntiles; ++it) {
-        if (it + 1 < ntiles) cp_async_wait<1>();
+        // tiles it + 1 .. it + VT_STAGES - 2 (those issued) may stay in flight
+        if (VT_STAGES == 3 && it + 1 < ntiles) cp_async_wait<1>();
         else cp_async_wait<0>();
         __syncthreads();  // tile `it` visible to all warps; the stage of tile it - 1 is free
         if (it + VT_STAGES - 1 < ntiles) issue(it + VT_STAGES - 1);
         const __half *Ks = stage(it), *Vs = Ks + VT_TILE * HD;
         const unsigned base = c0 + it * VT_TILE + 16 * ph;  // this warp's 16 positions
 
-        float s[2][4];
+        // the q_hi and q_lo products accumulate separately (four independent
+        // MMA chains instead of two), then add
+        float s[2][4], sl[2][4];
 #pragma unroll
-        for (int n = 0; n < 2; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) s[n][i] = sl[n][i] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
             unsigned ah[4], al[4], b[4];
@@ -429,9 +445,13 @@ __global__ void __launch_bounds__(RW * 64) verify_mma_kernel(const AtParams p)
             ldmatrix_x4(b, Ks + vt_swz<HD>(16 * ph + (lane & 7) + 8 * (mi >> 1), ks * 16 + 8 * (mi & 1)));
             mma_f16_k16(s[0], ah, b[0], b[1]);
             mma_f16_k16(s[1], ah, b[2], b[3]);
-            mma_f16_k16(s[0], al, b[0], b[1]);
-            mma_f16_k16(s[1], al, b[2], b[3]);
+            mma_f16_k16(sl[0], al, b[0], b[1]);
+            mma_f16_k16(sl[1], al, b[2], b[3]);
         }
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) s[n][i] += sl[n][i];
         // mask, scale, online softmax (rows A = gid, B = gid + 8)
         float tmA = -INFINITY, tmB = -INFINITY;
 #pragma unroll

@@ -110,24 +110,37 @@ __global__ void __launch_bounds__(Q8_WARPS * 32) q8_0_matmul_kernel(const unsign
 #pragma unroll
         for (int v = 0; v < NB; ++v) acc[r][v] = landed ? 0.f : __int_as_float(0x7fc00000);
     if (landed) {
+        // U block pairs per step: their x loads are all issued before any is
+        // used, so a warp waits on one round trip per step
+        constexpr int U = NB == 1 ? 8 : NB <= 4 ? 2 : 1;
         const unsigned b0 = nblk * warp / Q8_WARPS, b1 = nblk * (warp + 1) / Q8_WARPS;
-        for (unsigned b = b0 + (lane >> 4); b < b1; b += 2) {
-            float2 xv[NB];
+        for (unsigned bs = b0 + (lane >> 4); bs < b1; bs += 2 * U) {
+            float2 xv[U][NB];
 #pragma unroll
-            for (int v = 0; v < NB; ++v)
-                xv[v] = v < nb ? __ldg(reinterpret_cast<const float2 *>(x + v * x_stride + (size_t)b * 32 + 2 * hl))
-                               : make_float2(0.f, 0.f);
+            for (int u = 0; u < U; ++u)
 #pragma unroll
-            for (int r = 0; r < (int)Q8_WARPS; ++r) {
-                if ((unsigned)r < here) {
-                    const unsigned char *blk = q8s + (size_t)r * rb + b * 34;
-                    const float d = half_bits_to_float(*reinterpret_cast<const unsigned short *>(blk));
-                    const unsigned short h = *reinterpret_cast<const unsigned short *>(blk + 2 + 2 * hl);
-                    const float q0 = d * (float)(signed char)(h & 0xff), q1 = d * (float)(signed char)(h >> 8);
+                for (int v = 0; v < NB; ++v) {
+                    const unsigned b = bs + 2 * u;
+                    xv[u][v] = v < nb && b < b1
+                                   ? __ldg(reinterpret_cast<const float2 *>(x + v * x_stride + (size_t)b * 32 + 2 * hl))
+                                   : make_float2(0.f, 0.f);
+                }
 #pragma unroll
-                    for (int v = 0; v < NB; ++v) {
-                        acc[r][v] = fmaf(q0, xv[v].x, acc[r][v]);
-                        acc[r][v] = fmaf(q1, xv[v].y, acc[r][v]);
+            for (int u = 0; u < U; ++u) {
+                const unsigned b = bs + 2 * u;
+                if (b >= b1) break;
+#pragma unroll
+                for (int r = 0; r < (int)Q8_WARPS; ++r) {
+                    if ((unsigned)r < here) {
+                        const unsigned char *blk = q8s + (size_t)r * rb + b * 34;
+                        const float d = half_bits_to_float(*reinterpret_cast<const unsigned short *>(blk));
+                        const unsigned short h = *reinterpret_cast<const unsigned short *>(blk + 2 + 2 * hl);
+                        const float q0 = d * (float)(signed char)(h & 0xff), q1 = d * (float)(signed char)(h >> 8);
+#pragma unroll
+                        for (int v = 0; v < NB; ++v) {
+                            acc[r][v] = fmaf(q0, xv[u][v].x, acc[r][v]);
+                            acc[r][v] = fmaf(q1, xv[u][v].y, acc[r][v]);
+                        }
                     }
                 }
             }

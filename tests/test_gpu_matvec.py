@@ -215,9 +215,10 @@ def test_prepared_matches_one_call(type_id):
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (1024, 14336), (3000, 4096)])
 def test_prepared_small_batch_gemm(type_id, rows, cols):
     """Batches of 3..17 through fyb_quant_matmul_prepared (the weight-reusing
-    small-batch GEMM for groups of 3..16 vectors, the GEMV for a remainder of
-    one or two) against the double reference, with the forward-error bound of
-    the GEMV tests. K = 14336 needs several K-slices at 16 vectors (their
+    small-batch GEMM for groups of 3..16 vectors: the integer mma.sync kernel
+    for 3, the tcgen05 kernel with 16, 32 and 64 B columns for 4, 5..8 and
+    9..16; the GEMV for a remainder of one or two) against the double
+    reference, with the forward-error bound of the GEMV tests. K = 14336 needs several K-slices at 16 vectors (their
     partial rows are added in slice order); 3000 rows end in a partial tile."""
     import torch
     P = lambda t: C.c_void_p(t.data_ptr())
@@ -232,7 +233,7 @@ def test_prepared_small_batch_gemm(type_id, rows, cols):
     dw = torch.from_numpy(data).cuda()
     assert F.lib.fyb_quant_repack(P(dw), rows, cols, type_id, P(ws), wsb, None) == 0
     x = torch.from_numpy(xs).cuda()
-    for batch in (3, 8, 16, 17):
+    for batch in (3, 4, 5, 8, 12, 16, 17):
         y = torch.full((batch, rows), float("nan"), device="cuda")
         for rep in range(2):  # twice: the scratch counters must be back at zero
             assert F.lib.fyb_quant_matmul_prepared(rows, cols, type_id, P(x), P(y), batch, P(ws), wsb, None) == 0
