@@ -20,6 +20,8 @@
 // partial rows to a scratch area and the last CTA of a tile group (atomic
 // count) adds the slices in slice order, so results do not depend on timing.
 #include "qgemv_core.cuh"
+#include <cstdio>
+#include <cstdlib>
 
 namespace fyb {
 
@@ -71,7 +73,7 @@ static unsigned qm_blocks_per_slice(unsigned np, unsigned nblk)
 template <unsigned TYPE>
 __global__ void __launch_bounds__(QG_THREADS, 1) qgemm_kernel(const QmParams p)
 {
-    extern __shared__ __align__(128) unsigned char smem[];
+    extern __shared__ __align__(1024) unsigned char smem[];
     const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, tig = lane & 3;
     const unsigned s = blockIdx.x % p.KS, j = blockIdx.x / p.KS;
     if (j >= p.G) return;
@@ -281,68 +283,179 @@ static QmParams qm_plan(unsigned type, unsigned rows, unsigned cols, unsigned nv
 constexpr size_t QM_COUNTER_BYTES = 4096;  // up to 1024 tile groups
 
 // ===========================================================================
-// The same product on the 5th-generation tensor cores (tcgen05, for
-// TC_MIN_NV..16 vectors). A CTA of 256 threads takes M-tiles of 128 weight
-// rows (8 unit tiles) over a K slice. Per 256-column block:
-//  - the 8 units arrive by bulk copy (two-stage ring of whole blocks);
-//  - every thread owns one row and half of its groups: it scales the row's
-//    4- or 6-bit values by their group scale in integer and writes the
-//    product A' as two byte planes (A' = lo + 256 hi; Q6_K adds 8192 so
-//    both planes are unsigned) into shared memory in the canonical K-major
-//    layout (8-row x 16-byte core matrices, no swizzle);
-//  - one thread issues tcgen05.mma kind::i8 (u8 A x s8 B, M 128, N = 4 limbs
-//    x vectors, K 32) for each group and plane; the products of all 8 groups
-//    accumulate in TMEM (one fp32-exact int32 column set per plane), so the
-//    group scales cost no epilogue work;
-//  - tcgen05.commit signals an mbarrier; the threads read their row from
-//    TMEM (tcgen05.ld 32x32b), form T = lo + 256 hi per limb (minus the
-//    Q6_K bias times the block's limb sums) and apply d 2^(E - 6 - 7 limb)
-//    and the Q4_K minimum term in fp32.
-// The x limbs of the slice are split once per CTA into the B operand (same
-// split as the mma.sync path); K slices meet as in qgemm_kernel.
-constexpr unsigned TC_THREADS = 256;
-constexpr unsigned TC_MIN_NV = 4;
-constexpr unsigned TC_RING = 2;  // stages of 8 units
+// The same product on the 5th-generation tensor cores (tcgen05), for
+// TC_MIN_NV..16 vectors. A first small kernel (tc_limbs_kernel) splits the
+// vectors once into the B operand of every 256-column block: four signed
+// 7-bit limbs per value (the split of the mma.sync path), stored as
+// canonical K-major core matrices, followed by the block's x constants
+// (exponents, 32-value group sums, limb sums). The GEMM kernel then runs one
+// CTA per SM as a warp-specialized pipeline over items; an item is one
+// M-tile of 128 weight rows (8 unit tiles) times one block of the CTA's K
+// slice:
+//  - producer (warp 0, one thread): bulk-copies the item's 8 units into a
+//    unit ring stage, freed as soon as staging has read it, and the block's
+//    B operand with its x constants into a B ring stage, freed once the MMAs
+//    that read it and the epilogue are done (full / empty mbarriers per
+//    stage; the two rings advance independently). With programmatic
+//    dependent launch it starts streaming weights while the limb kernel
+//    still runs and waits for that kernel only before the first B copy;
+//  - staging (warps 2-9, two threads per row, each four of the eight
+//    groups): form the scaled weights A' = s q of the row as two byte planes
+//    in one of up to four operand buffers (two halves of 128 columns per
+//    item). Q4_K: s = 8 s_hi + s_lo with 3-bit parts, plane p = s_p q <= 105,
+//    one integer multiply per four packed nibbles (no carries between
+//    bytes); Q6_K: s (q - 32) + 8192 in 16-bit lanes split into its two
+//    bytes. They also copy the row's block constants (d, dmin, minimums) to a
+//    small buffer for the epilogue, so the unit stage is free as soon as the
+//    item is staged;
+//  - MMA (warp 1, one thread): tcgen05.mma kind::i8 (u8 A x s8 B, M 128,
+//    N = 4 limbs x padded vectors, K 32) per 32-value group and plane into
+//    one of four TMEM accumulators (the eight groups of a block accumulate in
+//    TMEM, so the group scales cost no epilogue work); tcgen05.commit frees
+//    the operand buffer and hands the accumulator to the epilogue;
+//  - epilogue (warps 10-17: a row and half of the vectors per thread; warp
+//    w reads TMEM lanes 32 (w % 4)..+31): tcgen05.ld of its row, planes and
+//    limbs combined in integer (Q4_K: T = lo + 8 hi, then 128 T0 + T1 and
+//    128 T2 + T3, which stay below 2^31), d 2^(E - 6 - 7 limb) and the Q4_K
+//    minimum term applied in fp32, the row accumulated over the blocks of
+//    the slice in registers.
+// Every wait is bounded and polls a shared abort word, so a timeout in one
+// role ends the others; the CTA lets its copies and MMAs in flight finish
+// before it frees TMEM and leaves. K slices (used when the rows give fewer
+// M-tiles than SMs) meet as in qgemm_kernel: partial rows in a scratch area,
+// the last CTA of a group adds them in slice order.
+constexpr unsigned TC_THREADS = 576;              // 18 warps
+constexpr unsigned TC_STAGE0 = 2, TC_NSTAGE = 8;  // staging warps 2..9
+constexpr unsigned TC_EPI0 = 10, TC_NEPI = 8;     // epilogue warps 10..17
+constexpr unsigned TC_MIN_NV = 9;  // below it the mma.sync kernel is faster (measured)
+constexpr unsigned TC_CST = 2048;                 // per item: 128 rows x 16 B
 
 FYB_HOST_DEV unsigned tc_n(unsigned nv) { return nv <= 4 ? 16u : nv <= 8 ? 32u : 64u; }  // 4 limbs x padded vectors
+// B block: the MMA's operand [8 groups][N/8 core rows][2 K halves][8][16] s8
+// limbs | exps [N/4] | group sums [N/4][8] | limb sums [N]
+FYB_HOST_DEV constexpr unsigned tc_bop(unsigned N) { return 8 * N * 32; }
+FYB_HOST_DEV constexpr unsigned tc_bblk(unsigned N) { return tc_bop(N) + (N / 4) * 4 + (N / 4) * 32 + N * 4; }
 
 struct TcSmem {
-    size_t b, exps, gsums, lsum, a, ring, bars, misc, total;
+    size_t a, ring, bring, cst, bars, misc, total;
 };
 
-FYB_HOST_DEV TcSmem tc_smem(unsigned type, unsigned N, unsigned nbs)
+// da operand half-buffers (2 planes x 4 groups x 128 x 32 B), rs unit ring
+// stages (8 units each), rb B stages, dc accumulator / constant buffers.
+FYB_HOST_DEV TcSmem tc_smem(unsigned type, unsigned N, unsigned rs, unsigned rb, unsigned da, unsigned dc)
 {
     TcSmem s;
-    s.b = 0;                                                   // [nbs][8 groups][N/8][2][8][16] s8 limbs
-    s.exps = s.b + (size_t)nbs * 8 * N * 32;                   // [nbs][N/4] int
-    s.gsums = s.exps + (size_t)nbs * (N / 4) * 4;              // [nbs][N/4][8] float
-    s.lsum = s.gsums + (size_t)nbs * (N / 4) * 8 * 4;          // [nbs][N] int
-    s.a = (s.lsum + (size_t)nbs * N * 4 + 1023) / 1024 * 1024; // [2 halves][2 planes][4 groups][16][2][8][16]
-    s.ring = s.a + 2 * 2 * 4 * 4096;                           // [TC_RING][8 units]
-    s.bars = s.ring + (size_t)TC_RING * 8 * unit_bytes(type);
-    s.misc = s.bars + (TC_RING + 1) * 8;
+    s.a = 0;                                                  // [da][2 planes][4 groups][128 x 32 B]
+    s.ring = s.a + (size_t)da * 32768;                        // [rs][8 units]
+    s.bring = s.ring + (size_t)rs * 8 * unit_bytes(type);     // [rb][B block]
+    s.cst = s.bring + (size_t)rb * tc_bblk(N);                // [dc][TC_CST]
+    s.bars = s.cst + (size_t)dc * TC_CST;
+    s.misc = s.bars + (2 * rs + 2 * rb + 2 * da + 4 * dc + 1) * 8;
     s.total = s.misc + 16;
     return s;
 }
 
-static unsigned tc_blocks_per_slice(unsigned type, unsigned N, unsigned nblk)
+// Pipeline depths: four accumulators (4 x 2N TMEM columns, 512 at most)
+// and the first of these (operand buffers, unit stages, B stages) that fits.
+struct TcDepth {
+    unsigned rs, rb, da, dc;
+};
+static TcDepth tc_depth(unsigned type, unsigned N)
 {
-    unsigned nbs = nblk;
-    while (nbs > 1 && tc_smem(type, N, nbs).total > 227 * 1024) --nbs;
-    return tc_smem(type, N, nbs).total <= 227 * 1024 ? nbs : 0;
+    constexpr size_t cap = 227 * 1024;
+    const unsigned pref[][3] = {{4, 4, 3}, {4, 3, 3}, {3, 4, 3}, {3, 4, 2}, {3, 3, 3}, {3, 3, 2}, {2, 3, 2}, {2, 2, 2}};
+    for (const auto &q : pref)
+        if (tc_smem(type, N, q[1], q[2], q[0], 4).total <= cap) return {q[1], q[2], q[0], 4};
+    return {0, 0, 0, 0};
 }
 
 struct TcParams {
     const unsigned char *units;
     unsigned rows, K, nblk, tiles, mtiles, nv, N;
-    unsigned nbs, KS, G;
+    unsigned nbs, KS, G, rs, rb, da, dc;
     const float *x;
     float *y;
     unsigned long long out_stride;
-    float *scratch;      // [KS][mtiles * 128][N / 4] when KS > 1
-    unsigned *counters;  // [G]
+    const unsigned char *bops;  // [nblk][tc_bblk(N)] (tc_limbs_kernel)
+    float *scratch;             // [KS][mtiles * 128][N / 4] when KS > 1
+    unsigned *counters;         // [G]
     unsigned *error;
 };
+
+// Offset of row R, K half kc within one group's 128 x 32 (or N x 32) operand.
+FYB_HOST_DEV unsigned tc_core(unsigned R, unsigned kc) { return (R >> 3) * 256 + kc * 128 + (R & 7) * 16; }
+
+// The B block of block blockIdx.x: thread i takes the 16-value slot i % 16
+// of vector i / 16 (zero past nv).
+template <unsigned N>
+__global__ void __launch_bounds__(N * 4) tc_limbs_kernel(const float *x, unsigned K, unsigned nv, unsigned char *bops,
+    unsigned *error)
+{
+    const unsigned bl = blockIdx.x, v = threadIdx.x >> 4, k16 = threadIdx.x & 15;
+    unsigned char *out = bops + (size_t)bl * tc_bblk(N);
+    int *exps = reinterpret_cast<int *>(out + tc_bop(N));
+    float *gsums = reinterpret_cast<float *>(out + tc_bop(N) + (N / 4) * 4);
+    int *lsum = reinterpret_cast<int *>(out + tc_bop(N) + (N / 4) * 36);
+    float xv[16];
+    if (v < nv) load16(x + (size_t)v * K + (size_t)bl * 256 + 16 * k16, xv);
+    else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) xv[q] = 0.f;
+    }
+    pdl_launch_dependents();
+    float gs = 0.f, mx = 0.f;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) { gs = __fadd_rn(gs, xv[q]); mx = fmaxf(mx, fabsf(xv[q])); }
+    const float other = __shfl_xor_sync(0xffffffffu, gs, 1);
+    if ((k16 & 1) == 0) gsums[v * 8 + k16 / 2] = __fadd_rn(gs, other);
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    int E = 0;
+    const bool bad = !(mx <= 3.0e38f);  // inf or NaN in the block
+    if (!bad && mx > 0.f) {
+        frexpf(mx, &E);
+        if (E < -120) E = -120;  // below 2^-121 the limbs round to zero anyway
+    }
+    if (k16 == 0) exps[v] = E;
+    if (bad && error) *(volatile unsigned *)error = ERR_NONFINITE;
+    const float sc = pow2f(6 - E);
+    unsigned words[4][4];
+    int ls[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        unsigned t[4][4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float r = bad ? 0.f : __fmul_rn(xv[4 * q + e], sc);
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const float m = __fadd_rn(r, 12582912.0f);  // rint via the 1.5*2^23 magic
+                const float X = __fsub_rn(m, 12582912.0f);
+                t[l][e] = __float_as_uint(m);
+                ls[l] += (int)X;
+                r = __fmul_rn(__fsub_rn(r, X), 128.0f);
+            }
+        }
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const unsigned lo = __byte_perm(t[l][0], t[l][1], 0x0040);
+            const unsigned hi = __byte_perm(t[l][2], t[l][3], 0x0040);
+            words[l][q] = __byte_perm(lo, hi, 0x5410);
+        }
+    }
+#pragma unroll
+    for (int l = 0; l < 4; ++l)
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) ls[l] += __shfl_xor_sync(0xffffffffu, ls[l], o);
+    const unsigned g = k16 / 2, kc = k16 & 1;
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const unsigned n = 4 * v + l;
+        *reinterpret_cast<uint4 *>(out + (size_t)g * N * 32 + tc_core(n, kc)) =
+            make_uint4(words[l][0], words[l][1], words[l][2], words[l][3]);
+        if (k16 == 0) lsum[n] = ls[l];
+    }
+}
 
 // K-major canonical operand descriptor: core matrices of 8 rows x 16 bytes,
 // the two 16-byte K halves 128 bytes apart (leading offset), 8-row groups
@@ -378,9 +491,26 @@ FYB_DEV void tc_ld8(uint32_t taddr, int *r)
                  : "r"(taddr) : "memory");
 }
 FYB_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Offset of row R, K half kc within one group's 128 x 32 operand.
-FYB_DEV unsigned tc_core(unsigned R, unsigned kc) { return (R >> 3) * 256 + kc * 128 + (R & 7) * 16; }
+FYB_DEV void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+FYB_DEV bool mbar_test_wait(uint64_t *bar, unsigned parity)  // non-blocking
+{
+    unsigned ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait that also gives up when another role raised the abort word.
+FYB_DEV bool tc_wait(uint64_t *bar, unsigned parity, const volatile unsigned *abort)
+{
+    for (unsigned i = 0; i < (1u << 22); ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 63u && *abort) return false;
+    }
+    return false;
+}
 
 // A' = (s - m) q + bias of four packed byte values q < 64 in 16-bit lanes
 // (s <= 255; every lane stays in [0, 2^16) before and after the
@@ -394,21 +524,30 @@ FYB_DEV void tc_scale4(unsigned q, unsigned s, unsigned bias2, unsigned m, unsig
     hi = __byte_perm(pa, pb, 0x7531);
 }
 
-template <unsigned TYPE, unsigned NH>
+template <unsigned TYPE, unsigned N>
 __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams p)
 {
-    constexpr unsigned N = 2 * NH, NVH = NH / 4;  // columns per plane; vectors per thread
+    constexpr unsigned NV4 = N / 4;        // vector slots
+    constexpr unsigned EV = N / 8;         // vectors per epilogue thread
+    constexpr unsigned BBLK = tc_bblk(N);
+    constexpr unsigned BOP = tc_bop(N);
+    constexpr unsigned UB = unit_bytes(TYPE);
+    constexpr unsigned NCOLS = 8 * N;       // four accumulators x two planes: 128, 256 or 512 TMEM columns
     extern __shared__ __align__(1024) unsigned char smem[];
-    const TcSmem L = tc_smem(TYPE, N, p.nbs);
-    signed char *bsm = reinterpret_cast<signed char *>(smem + L.b);
-    int *exps = reinterpret_cast<int *>(smem + L.exps);
-    float *gsums = reinterpret_cast<float *>(smem + L.gsums);
-    int *lsum = reinterpret_cast<int *>(smem + L.lsum);
-    unsigned char *asm_ = smem + L.a;
+    const unsigned rs = p.rs, rb = p.rb, da = p.da, dc = p.dc;
+    const TcSmem L = tc_smem(TYPE, N, rs, rb, da, dc);
+    unsigned char *abuf = smem + L.a;
     unsigned char *ring = smem + L.ring;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);  // [TC_RING] units, [TC_RING] MMAs done
+    unsigned char *bring = smem + L.bring;
+    unsigned char *cst = smem + L.cst;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *u_full = bars, *u_empty = u_full + rs, *b_full = u_empty + rs, *b_empty = b_full + rb;
+    uint64_t *a_full = b_empty + rb, *a_empty = a_full + da;
+    uint64_t *acc_full = a_empty + da, *acc_empty = acc_full + dc, *cst_full = acc_empty + dc, *cst_empty = cst_full + dc;
+    uint64_t *drain = cst_empty + dc;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.misc);
     unsigned *flag = reinterpret_cast<unsigned *>(smem + L.misc + 4);
+    volatile unsigned *abort = reinterpret_cast<volatile unsigned *>(smem + L.misc + 8);
 
     const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const unsigned s = blockIdx.x % p.KS, j = blockIdx.x / p.KS;
@@ -417,270 +556,287 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
     const unsigned mb = (unsigned)((unsigned long long)p.mtiles * j / p.G);
     const unsigned me = (unsigned)((unsigned long long)p.mtiles * (j + 1) / p.G);
     const unsigned items = (me - mb) * nb;
-    const unsigned ub = unit_bytes(TYPE);
-    const unsigned ncols = N * 2 <= 32 ? 32u : N * 2;  // TMEM columns: the two planes
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     :: "r"(smem_u32(tmem_slot)), "r"(ncols) : "memory");
+                     :: "r"(smem_u32(tmem_slot)), "r"(NCOLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (threadIdx.x == 0) {
-        for (unsigned k = 0; k < TC_RING + 1; ++k) mbar_init(bars + k, 1);
+    if (threadIdx.x == 32) {
+        for (unsigned k = 0; k < rs; ++k) { mbar_init(u_full + k, 1); mbar_init(u_empty + k, TC_NSTAGE); }
+        for (unsigned k = 0; k < rb; ++k) { mbar_init(b_full + k, 1); mbar_init(b_empty + k, 1 + TC_NEPI); }
+        for (unsigned k = 0; k < da; ++k) {
+            mbar_init(a_full + k, TC_NSTAGE);
+            mbar_init(a_empty + k, 1);
+        }
+        for (unsigned k = 0; k < dc; ++k) {
+            mbar_init(acc_full + k, 1);
+            mbar_init(acc_empty + k, TC_NEPI);
+            mbar_init(cst_full + k, TC_NSTAGE);
+            mbar_init(cst_empty + k, TC_NEPI);
+        }
+        mbar_init(drain, 1);
+        *abort = 0u;
         fence_barrier_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
-    auto issue = [&](unsigned it) {  // the 8 units of item `it` into ring stage it % TC_RING
-        const unsigned mt = mb + it / nb, bl = it % nb, st = it % TC_RING;
-        const unsigned t0 = mt * 8, nt = min(8u, p.tiles - t0);
-        mbar_expect_tx(bars + st, nt * ub);
-        for (unsigned i = 0; i < nt; ++i)
-            bulk_copy_g2s(ring + ((size_t)st * 8 + i) * ub,
-                          p.units + ((unsigned long long)(t0 + i) * p.nblk + b0 + bl) * ub, ub, bars + st);
+    auto fail = [&]() {
+        *abort = 1u;
+        if (p.error) atomicCAS(p.error, 0u, (unsigned)ERR_TIMEOUT);
     };
-    if (threadIdx.x == 0)
-        for (unsigned it = 0; it < items && it < TC_RING; ++it) issue(it);
 
-    // B: the slice's x limbs, vector v (zero past nv) in rows 4v..4v+3
-    {
-        const unsigned nslot = nb * 16, vtot = N / 4;
-        for (unsigned s0 = 0; s0 < vtot * nslot; s0 += TC_THREADS) {
-            const unsigned i = s0 + threadIdx.x;
-            const bool ok = i < vtot * nslot;
-            const unsigned v = ok ? i / nslot : 0, sl = ok ? i % nslot : 0, bl = sl / 16, k16 = sl % 16;
-            float x[16];
-            if (ok && v < p.nv) load16(p.x + (size_t)v * p.K + (size_t)b0 * 256 + 16 * sl, x);
-            else {
-#pragma unroll
-                for (int q = 0; q < 16; ++q) x[q] = 0.f;
-            }
-            float gs = 0.f, mx = 0.f;
-#pragma unroll
-            for (int q = 0; q < 16; ++q) { gs = __fadd_rn(gs, x[q]); mx = fmaxf(mx, fabsf(x[q])); }
-            const float other = __shfl_xor_sync(0xffffffffu, gs, 1);
-            if (ok && (k16 & 1) == 0) gsums[(bl * vtot + v) * 8 + k16 / 2] = __fadd_rn(gs, other);
-#pragma unroll
-            for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            int E = 0;
-            const bool bad = !(mx <= 3.0e38f);
-            if (!bad && mx > 0.f) {
-                frexpf(mx, &E);
-                if (E < -120) E = -120;
-            }
-            if (ok && k16 == 0) exps[bl * vtot + v] = E;
-            if (ok && bad && p.error) *(volatile unsigned *)p.error = ERR_NONFINITE;
-            const float sc = pow2f(6 - E);
-            unsigned words[4][4];
-            int ls[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                unsigned t[4][4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    float r = bad ? 0.f : __fmul_rn(x[4 * q + e], sc);
-#pragma unroll
-                    for (int l = 0; l < 4; ++l) {
-                        const float m = __fadd_rn(r, 12582912.0f);
-                        const float X = __fsub_rn(m, 12582912.0f);
-                        t[l][e] = __float_as_uint(m);
-                        ls[l] += (int)X;
-                        r = __fmul_rn(__fsub_rn(r, X), 128.0f);
-                    }
+    if (warp == 0) {
+        // ---------------------------------------------------------- producer
+        // two rings served independently: units (freed by staging) and B
+        // blocks (freed by the MMAs that read them and the epilogue)
+        if (lane == 0) {
+            unsigned iu = 0, ib = 0, idle = 0;
+            while ((iu < items || ib < items) && !*abort) {
+                bool moved = false;
+                if (iu < items && (iu < rs || mbar_test_wait(u_empty + iu % rs, (iu / rs - 1) & 1u))) {
+                    const unsigned st = iu % rs, mt = mb + iu / nb, bl = iu % nb;
+                    const unsigned t0 = mt * 8, nt = min(8u, p.tiles - t0);
+                    unsigned char *dst = ring + (size_t)st * 8 * UB;
+                    mbar_expect_tx(u_full + st, nt * UB);
+                    for (unsigned i = 0; i < nt; ++i)
+                        bulk_copy_g2s(dst + i * UB, p.units + ((unsigned long long)(t0 + i) * p.nblk + b0 + bl) * UB, UB,
+                                      u_full + st);
+                    ++iu;
+                    moved = true;
                 }
-#pragma unroll
-                for (int l = 0; l < 4; ++l) {
-                    const unsigned lo = __byte_perm(t[l][0], t[l][1], 0x0040);
-                    const unsigned hi = __byte_perm(t[l][2], t[l][3], 0x0040);
-                    words[l][q] = __byte_perm(lo, hi, 0x5410);
+                if (ib < items && (ib < rb || mbar_test_wait(b_empty + ib % rb, (ib / rb - 1) & 1u))) {
+                    const unsigned st = ib % rb, bl = ib % nb;
+                    if (ib == 0) pdl_wait();  // the limb kernel's output is complete and visible
+                    mbar_expect_tx(b_full + st, BBLK);
+                    bulk_copy_g2s(bring + (size_t)st * BBLK, p.bops + (size_t)(b0 + bl) * BBLK, BBLK, b_full + st);
+                    ++ib;
+                    moved = true;
                 }
+                if (moved) idle = 0;
+                else if (++idle > (1u << 24)) { fail(); break; }
+                else __nanosleep(32);
             }
-#pragma unroll
-            for (int l = 0; l < 4; ++l)
-#pragma unroll
-                for (int o = 1; o < 16; o <<= 1) ls[l] += __shfl_xor_sync(0xffffffffu, ls[l], o);
-            if (ok) {
-                const unsigned g = k16 / 2, kc = k16 & 1;
-#pragma unroll
-                for (int l = 0; l < 4; ++l) {
-                    const unsigned n = 4 * v + l;
-                    *reinterpret_cast<uint4 *>(bsm + ((size_t)(bl * 8 + g) * (N / 8)) * 256 + tc_core(n, kc)) =
-                        make_uint4(words[l][0], words[l][1], words[l][2], words[l][3]);
-                    if (k16 == 0) lsum[bl * N + n] = ls[l];
-                }
-            }
+            // every issued copy lands before the CTA leaves (bounded)
+            for (unsigned st = 0; st < rs && st < iu; ++st) mbar_wait_bounded(u_full + st, ((iu - st - 1) / rs) & 1u);
+            for (unsigned st = 0; st < rb && st < ib; ++st) mbar_wait_bounded(b_full + st, ((ib - st - 1) / rb) & 1u);
         }
-    }
-    fence_proxy_async();
-    __syncthreads();
-
-    // rows: thread t owns row R = t % 128 of the M-tile; its half vh = t / 128
-    // of the groups (staging) and of the vectors (epilogue); warp w reads TMEM
-    // lanes 32 (w % 4) .. + 31, which are exactly rows R
-    const unsigned R = threadIdx.x & 127, vh = threadIdx.x >> 7;
-    const uint32_t idesc = tc_idesc(N);
-    const uint32_t trow = tmem + ((32u * (warp & 3)) << 16);
-    float acc[NVH];
-#pragma unroll
-    for (unsigned q = 0; q < NVH; ++q) acc[q] = 0.f;
-    unsigned rpar = 0;
-    bool ok = true;
-    for (unsigned it = 0; it < items && ok; ++it) {
-        const unsigned mt = mb + it / nb, bl = it % nb, st = it % TC_RING;
-        const bool landed = mbar_wait_bounded(bars + st, (rpar >> st) & 1u);
-        if (__syncthreads_or(!landed)) {
-            if (threadIdx.x == 0 && p.error) atomicCAS(p.error, 0u, (unsigned)ERR_TIMEOUT);
-            ok = false;
-            break;
-        }
-        rpar ^= 1u << st;
-        const unsigned tile = R >> 4, r = R & 15;
-        const bool have = mt * 8 + tile < p.tiles;
-        const unsigned char *u = ring + ((size_t)st * 8 + tile) * ub;
-        // this row's block constants, read before the ring stage is refilled
-        float d = 0.f, dmin = 0.f, mins[8];
-        unsigned scq[8];
-        if constexpr (TYPE == T_Q4_K) {
-            const uint4 hd = have ? *reinterpret_cast<const uint4 *>(u + 2048 + r * 16) : make_uint4(0, 0, 0, 0);
-            d = half_bits_to_float((unsigned short)(hd.x & 0xffffu));
-            dmin = half_bits_to_float((unsigned short)(hd.x >> 16));
-            const unsigned sc0 = hd.y & 0x3F3F3F3Fu, sc1 = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
-            const unsigned m0 = hd.z & 0x3F3F3F3Fu, m1 = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-                scq[g] = __byte_perm(g < 4 ? sc0 : sc1, 0u, 0x4440 + (g & 3));
-                mins[g] = (float)__byte_perm(g < 4 ? m0 : m1, 0u, 0x4440 + (g & 3));
-            }
-        } else {
-            d = have ? half_bits_to_float(*reinterpret_cast<const unsigned short *>(u + 3328 + r * 2)) : 0.f;
-#pragma unroll
-            for (int g = 0; g < 8; ++g) { scq[g] = 0; mins[g] = 0.f; }
-        }
-        for (unsigned h = 0; h < 2; ++h) {
-            // groups 4h + 2vh, +1 of row R into the half-h operand buffer
-            unsigned char *ah = asm_ + (size_t)h * 2 * 4 * 4096;
-#pragma unroll
-            for (unsigned gi = 0; gi < 2; ++gi) {
-                const unsigned g = 4 * h + 2 * vh + gi, gl = g & 3;
-#pragma unroll
-                for (unsigned kc = 0; kc < 2; ++kc) {
-                    uint4 lo4 = make_uint4(0, 0, 0, 0), hi4 = make_uint4(0, 0, 0, 0);
-                    if (have) {
-                        unsigned w[4], lo[4], hi[4];
-                        if constexpr (TYPE == T_Q4_K) {
-                            const uint4 q = *reinterpret_cast<const uint4 *>(u + ((g >> 1) * 32 + kc * 16 + r) * 16);
-                            const unsigned sh = (g & 1) * 4;
-                            w[0] = (q.x >> sh) & 0x0F0F0F0Fu; w[1] = (q.y >> sh) & 0x0F0F0F0Fu;
-                            w[2] = (q.z >> sh) & 0x0F0F0F0Fu; w[3] = (q.w >> sh) & 0x0F0F0F0Fu;
-                            const unsigned sg = vh ? scq[4 * h + 2 + gi] : scq[4 * h + gi];  // g, without a runtime index
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) tc_scale4(w[e], sg, 0u, 0u, lo[e], hi[e]);  // A' = s q
-                        } else {
-                            // value l = 16 kc + e of group g = 4 n2 + qq: ql chunk (2 n2 + (qq & 1), kc),
-                            // qh chunk (n2, kc), scale byte 8 n2 + 2 qq + kc
-                            const unsigned n2 = g >> 2, qq = g & 3;
-                            const uint4 ql = *reinterpret_cast<const uint4 *>(u + ((2 * n2 + (qq & 1)) * 32 + kc * 16 + r) * 16);
-                            const uint4 qh = *reinterpret_cast<const uint4 *>(u + 2048 + (n2 * 32 + kc * 16 + r) * 16);
-                            const int sgn = (int)(signed char)u[3072 + r * 16 + 8 * n2 + 2 * qq + kc];
-                            const unsigned sp = (unsigned)(sgn + 128);                 // 0..255
-                            const unsigned bias = (unsigned)(8192 - 32 * sgn);          // s (q - 32) + 8192 > 0
-                            const unsigned bias2 = bias | (bias << 16);
-                            const unsigned qsh = (qq >= 2) ? 4u : 0u, hsh = 2 * qq;
-                            const unsigned lq[4] = {ql.x, ql.y, ql.z, ql.w}, hq[4] = {qh.x, qh.y, qh.z, qh.w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                w[e] = ((lq[e] >> qsh) & 0x0F0F0F0Fu) | (((hq[e] >> hsh) & 0x03030303u) << 4);
-                                // (s + 128) q - 128 q + 8192 - 32 s = s (q - 32) + 8192
-                                tc_scale4(w[e], sp, bias2, 128u, lo[e], hi[e]);
-                            }
-                        }
-                        lo4 = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                        hi4 = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                    }
-                    *reinterpret_cast<uint4 *>(ah + (0 * 4 + gl) * 4096 + tc_core(R, kc)) = lo4;
-                    *reinterpret_cast<uint4 *>(ah + (1 * 4 + gl) * 4096 + tc_core(R, kc)) = hi4;
-                }
-            }
-            fence_proxy_async();
-            __syncthreads();
-            if (threadIdx.x == 0) {
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issue
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc_idesc(N);
+            for (unsigned it = 0; it < items; ++it) {
+                const unsigned t = it % dc, sb = it % rb;
+                if (it >= dc && !tc_wait(acc_empty + t, (it / dc - 1) & 1u, abort)) { fail(); break; }
+                if (!tc_wait(b_full + sb, (it / rb) & 1u, abort)) { fail(); break; }
                 tc_fence_after();
-                const signed char *bb = bsm + (size_t)bl * 8 * (N / 8) * 256;
+                const uint32_t dacc = tmem + t * 2 * N;
+                const unsigned char *bb = bring + (size_t)sb * BBLK;
+                bool ok = true;
+                for (unsigned h = 0; h < 2; ++h) {
+                    const unsigned hh = 2 * it + h, ab = hh % da;
+                    if (!tc_wait(a_full + ab, (hh / da) & 1u, abort)) { fail(); ok = false; break; }
+                    tc_fence_after();
+                    const unsigned char *ah = abuf + ab * 32768;
 #pragma unroll
-                for (unsigned gl = 0; gl < 4; ++gl) {
-                    const uint64_t bd = tc_desc(bb + (size_t)(4 * h + gl) * (N / 8) * 256);
-                    const uint32_t acc_in = (h | gl) ? 1u : 0u;
-                    tc_mma(tmem, tc_desc(ah + (0 * 4 + gl) * 4096), bd, idesc, acc_in);
-                    tc_mma(tmem + N, tc_desc(ah + (1 * 4 + gl) * 4096), bd, idesc, acc_in);
+                    for (unsigned gl = 0; gl < 4; ++gl) {
+                        const uint64_t bd = tc_desc(bb + (size_t)(4 * h + gl) * N * 32);
+                        const uint32_t acc_in = (h | gl) ? 1u : 0u;
+                        tc_mma(dacc, tc_desc(ah + gl * 4096), bd, idesc, acc_in);
+                        tc_mma(dacc + N, tc_desc(ah + (4 + gl) * 4096), bd, idesc, acc_in);
+                    }
+                    tc_commit(a_empty + ab);
                 }
-                if (h == 1) {
-                    tc_commit(bars + TC_RING);  // every MMA of the item: the planes are complete
-                    if (it + TC_RING < items) issue(it + TC_RING);  // the stage has been read by all threads
-                }
+                if (!ok) break;
+                tc_commit(b_empty + sb);
+                tc_commit(acc_full + t);
             }
+            // every MMA issued has completed before TMEM is freed (bounded)
+            tc_commit(drain);
+            mbar_wait_bounded(drain, 0);
         }
-        // epilogue: this row's planes for the vector half vh
-        if (!mbar_wait_bounded(bars + TC_RING, it & 1u)) {
-            if (p.error) atomicCAS(p.error, 0u, (unsigned)ERR_TIMEOUT);
-            ok = false;
-        }
-        if (__syncthreads_or(!ok)) { ok = false; break; }
-        tc_fence_after();
-        int lo[NH], hi[NH];
-#pragma unroll
-        for (unsigned c = 0; c < NH; c += 8) {
-            tc_ld8(trow + vh * NH + c, lo + c);
-            tc_ld8(trow + N + vh * NH + c, hi + c);
-        }
-        tc_wait_ld();
-        tc_fence_before();
-#pragma unroll
-        for (unsigned q = 0; q < NVH; ++q) {
-            const unsigned v = vh * NVH + q;
-            const int E = exps[bl * (N / 4) + v];
-            float sum = 0.f;
-#pragma unroll
-            for (unsigned l = 0; l < 4; ++l) {
-                int T = lo[4 * q + l] + (hi[4 * q + l] << 8);
-                if constexpr (TYPE == T_Q6_K) T -= 8192 * lsum[bl * N + 4 * v + l];
-                sum = fmaf((float)T, pow2f(E - 6 - 7 * (int)l), sum);
-            }
-            acc[q] = fmaf(d, sum, acc[q]);
+    } else if (warp < TC_EPI0) {
+        // ---------------------------------------------------------- staging
+        const unsigned sid = threadIdx.x - TC_STAGE0 * 32;  // 0..255
+        const unsigned R = sid & 127, vh = sid >> 7, tile = R >> 4, r = R & 15;
+        for (unsigned it = 0; it < items; ++it) {
+            const unsigned st = it % rs, mt = mb + it / nb, cb = it % dc;
+            if (!tc_wait(u_full + st, (it / rs) & 1u, abort)) { fail(); break; }
+            const bool have = mt * 8 + tile < p.tiles;
+            const unsigned char *u = ring + (size_t)st * 8 * UB + tile * UB;
+            // the row's block constants for the epilogue
+            if (it >= dc && !tc_wait(cst_empty + cb, (it / dc - 1) & 1u, abort)) { fail(); break; }
+            unsigned char *cb_base = cst + cb * TC_CST;
+            uint4 hd = make_uint4(0u, 0u, 0u, 0u);
             if constexpr (TYPE == T_Q4_K) {
-                const float *gsv = gsums + (bl * (N / 4) + v) * 8;
-                float mt_ = 0.f;
-#pragma unroll
-                for (int g = 0; g < 8; ++g) mt_ = fmaf(mins[g], gsv[g], mt_);
-                acc[q] = fmaf(-dmin, mt_, acc[q]);
-            }
-        }
-        if (bl + 1 == nb) {  // the M-tile's last block of this slice: write the rows
-            const unsigned row = mt * 128 + R;
-#pragma unroll
-            for (unsigned q = 0; q < NVH; ++q) {
-                const unsigned v = vh * NVH + q;
-                if (p.KS == 1) {
-                    if (v < p.nv && row < p.rows) p.y[v * p.out_stride + row] = acc[q];
-                } else {
-                    p.scratch[((size_t)s * p.mtiles * 128 + row) * (N / 4) + v] = acc[q];
+                if (have) hd = *reinterpret_cast<const uint4 *>(u + 2048 + r * 16);
+                if (vh == 0) {
+                    const float d = half_bits_to_float((unsigned short)(hd.x & 0xffffu));
+                    const float dmin = half_bits_to_float((unsigned short)(hd.x >> 16));
+                    const unsigned m0 = hd.z & 0x3F3F3F3Fu, m1 = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+                    *reinterpret_cast<uint4 *>(cb_base + R * 16) =
+                        make_uint4(__float_as_uint(d), __float_as_uint(dmin), m0, m1);
                 }
-                acc[q] = 0.f;
+            } else {
+                if (vh == 0) {
+                    const float d = have ? half_bits_to_float(*reinterpret_cast<const unsigned short *>(u + 3328 + r * 2))
+                                         : 0.f;
+                    *reinterpret_cast<uint4 *>(cb_base + R * 16) = make_uint4(__float_as_uint(d), 0u, 0u, 0u);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(cst_full + cb);
+            bool ok = true;
+            for (unsigned h = 0; h < 2; ++h) {
+                const unsigned hh = 2 * it + h, ab = hh % da;
+                if (hh >= da && !tc_wait(a_empty + ab, (hh / da - 1) & 1u, abort)) { fail(); ok = false; break; }
+                unsigned char *ah = abuf + ab * 32768;
+#pragma unroll
+                for (unsigned gi = 0; gi < 2; ++gi) {
+                    const unsigned g = 4 * h + 2 * vh + gi, gl = 2 * vh + gi;
+#pragma unroll
+                    for (unsigned kc = 0; kc < 2; ++kc) {
+                        uint4 lo4 = make_uint4(0u, 0u, 0u, 0u), hi4 = make_uint4(0u, 0u, 0u, 0u);
+                        if (have) {
+                            unsigned lo[4], hi[4];
+                            if constexpr (TYPE == T_Q4_K) {
+                                const unsigned sw = h ? ((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u))
+                                                      : (hd.y & 0x3F3F3F3Fu);
+                                const unsigned sg = __byte_perm(sw, 0u, 0x4440 + gl);
+                                const unsigned slo = sg & 7u, shi = sg >> 3;
+                                const uint4 q = *reinterpret_cast<const uint4 *>(u + ((g >> 1) * 32 + kc * 16 + r) * 16);
+                                const unsigned qa[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const unsigned w = (gi ? (qa[e] >> 4) : qa[e]) & 0x0F0F0F0Fu;
+                                    lo[e] = w * slo;  // every byte <= 105: no carry into the next
+                                    hi[e] = w * shi;
+                                }
+                            } else {
+                                // value l = 16 kc + e of group g = 4 n2 + qq: ql chunk (2 n2 + (qq & 1), kc),
+                                // qh chunk (n2, kc), scale byte 8 n2 + 2 qq + kc
+                                const unsigned n2 = h, qq = gl;
+                                const uint4 ql = *reinterpret_cast<const uint4 *>(u + ((2 * n2 + (qq & 1)) * 32 + kc * 16 + r) * 16);
+                                const uint4 qh = *reinterpret_cast<const uint4 *>(u + 2048 + (n2 * 32 + kc * 16 + r) * 16);
+                                const int sgn = (int)(signed char)u[3072 + r * 16 + 8 * n2 + 2 * qq + kc];
+                                const unsigned sp = (unsigned)(sgn + 128);         // 0..255
+                                const unsigned bias = (unsigned)(8192 - 32 * sgn);  // s (q - 32) + 8192 > 0
+                                const unsigned bias2 = bias | (bias << 16);
+                                const unsigned qsh = (qq >= 2) ? 4u : 0u, hsh = 2 * qq;
+                                const unsigned lq[4] = {ql.x, ql.y, ql.z, ql.w}, hq[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const unsigned w = ((lq[e] >> qsh) & 0x0F0F0F0Fu) | (((hq[e] >> hsh) & 0x03030303u) << 4);
+                                    // (s + 128) q - 128 q + 8192 - 32 s = s (q - 32) + 8192
+                                    tc_scale4(w, sp, bias2, 128u, lo[e], hi[e]);
+                                }
+                            }
+                            lo4 = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                            hi4 = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        }
+                        *reinterpret_cast<uint4 *>(ah + gl * 4096 + tc_core(R, kc)) = lo4;
+                        *reinterpret_cast<uint4 *>(ah + (4 + gl) * 4096 + tc_core(R, kc)) = hi4;
+                    }
+                }
+                fence_proxy_async();  // the operand is read by the tensor cores (async proxy)
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_full + ab);
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(u_empty + st);  // the unit stage is read
+        }
+    } else {
+        // ---------------------------------------------------------- epilogue
+        const unsigned q4 = warp & 3u, vh = (warp - TC_EPI0) >> 2;
+        const unsigned R = 32 * q4 + lane;
+        const uint32_t trow = tmem + ((32u * q4) << 16);
+        float acc[EV];
+#pragma unroll
+        for (unsigned q = 0; q < EV; ++q) acc[q] = 0.f;
+        for (unsigned it = 0; it < items; ++it) {
+            const unsigned t = it % dc, mt = mb + it / nb, bl = it % nb, sb = it % rb;
+            // b_full is complete already; waiting on it orders the B block's bytes for these threads
+            if (!tc_wait(acc_full + t, (it / dc) & 1u, abort) || !tc_wait(cst_full + t, (it / dc) & 1u, abort) ||
+                !tc_wait(b_full + sb, (it / rb) & 1u, abort)) {
+                fail();
+                break;
+            }
+            tc_fence_after();
+            const unsigned char *cb_base = cst + t * TC_CST;
+            const uint4 c = *reinterpret_cast<const uint4 *>(cb_base + R * 16);
+            const unsigned char *xcon = bring + (size_t)sb * BBLK + BOP;  // the block's x constants
+            const int *exps = reinterpret_cast<const int *>(xcon);
+            const float *gsums = reinterpret_cast<const float *>(xcon + NV4 * 4);
+            const int *lsum = reinterpret_cast<const int *>(xcon + NV4 * 36);
+            const float d = __uint_as_float(c.x), dmin = __uint_as_float(c.y);
+            float mins[8];
+#pragma unroll
+            for (int g = 0; g < 8; ++g) mins[g] = (float)__byte_perm(g < 4 ? c.z : c.w, 0u, 0x4440 + (g & 3));
+            const uint32_t tacc = trow + t * 2 * N + vh * 4 * EV;
+#pragma unroll
+            for (unsigned c8 = 0; c8 < 4 * EV; c8 += 8) {
+                int lo[8], hi[8];
+                tc_ld8(tacc + c8, lo);
+                tc_ld8(tacc + N + c8, hi);
+                tc_wait_ld();
+#pragma unroll
+                for (unsigned k = 0; k < 2; ++k) {
+                    const unsigned qv = c8 / 4 + k, v = vh * EV + qv;
+                    const int E = exps[v];
+                    if constexpr (TYPE == T_Q4_K) {
+                        const int T0 = lo[4 * k] + 8 * hi[4 * k], T1 = lo[4 * k + 1] + 8 * hi[4 * k + 1];
+                        const int T2 = lo[4 * k + 2] + 8 * hi[4 * k + 2], T3 = lo[4 * k + 3] + 8 * hi[4 * k + 3];
+                        const int P01 = T0 * 128 + T1, P23 = T2 * 128 + T3;  // |T| <= 945 * 64 * 256: below 2^31
+                        const float sum = fmaf((float)P01, pow2f(E - 13), (float)P23 * pow2f(E - 27));
+                        acc[qv] = fmaf(d, sum, acc[qv]);
+                        const float *gsv = gsums + v * 8;
+                        float mt_ = 0.f;
+#pragma unroll
+                        for (int g = 0; g < 8; ++g) mt_ = fmaf(mins[g], gsv[g], mt_);
+                        acc[qv] = fmaf(-dmin, mt_, acc[qv]);
+                    } else {
+                        float sum = 0.f;
+#pragma unroll
+                        for (unsigned l = 0; l < 4; ++l) {
+                            const int T = lo[4 * k + l] + (hi[4 * k + l] << 8) - 8192 * lsum[4 * v + l];
+                            sum = fmaf((float)T, pow2f(E - 6 - 7 * (int)l), sum);
+                        }
+                        acc[qv] = fmaf(d, sum, acc[qv]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(acc_empty + t);
+                mbar_arrive(cst_empty + t);
+                mbar_arrive(b_empty + sb);
+            }
+            if (bl + 1 == nb) {  // the M-tile's last block of this slice: write the rows
+                const unsigned row = mt * 128 + R;
+#pragma unroll
+                for (unsigned q = 0; q < EV; ++q) {
+                    const unsigned v = vh * EV + q;
+                    if (p.KS == 1) {
+                        if (v < p.nv && row < p.rows) p.y[v * p.out_stride + row] = acc[q];
+                    } else {
+                        p.scratch[((size_t)s * p.mtiles * 128 + row) * NV4 + v] = acc[q];
+                    }
+                    acc[q] = 0.f;
+                }
             }
         }
     }
-    // copies still in flight land before the CTA leaves (bounded)
-    if (threadIdx.x == 0 && !ok)
-        for (unsigned it2 = 0; it2 < TC_RING; ++it2) mbar_wait_bounded(bars + it2, (rpar >> it2) & 1u);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(ncols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(NCOLS) : "memory");
     }
-    if (p.KS == 1 || !ok) return;
+    if (p.KS == 1 || *abort) return;
     // slices: the last CTA of the M-tile group adds them in slice order
     __threadfence();
     __syncthreads();
@@ -688,53 +844,98 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
     __syncthreads();
     if (!*flag) return;
     __threadfence();
-    const unsigned r0 = mb * 128, r1 = min(me * 128, p.rows), vt = N / 4;
+    const unsigned r0 = mb * 128, r1 = min(me * 128, p.rows);
     for (unsigned i = threadIdx.x; i < (r1 - r0) * p.nv; i += TC_THREADS) {
         const unsigned row = r0 + i / p.nv, v = i % p.nv;
         float y = 0.f;
-        for (unsigned q = 0; q < p.KS; ++q) y += __ldcg(p.scratch + ((size_t)q * p.mtiles * 128 + row) * vt + v);
+        for (unsigned q = 0; q < p.KS; ++q) y += __ldcg(p.scratch + ((size_t)q * p.mtiles * 128 + row) * NV4 + v);
         p.y[v * p.out_stride + row] = y;
     }
     if (threadIdx.x == 0) p.counters[j] = 0;
 }
 
+// Layout of a launch: K slices and M-tile groups chosen for the least time
+// of the busiest CTA (its items at about one SM's share of HBM time each,
+// plus the slice sum by the last CTA of a group); G = 0 if the shape does
+// not fit.
 static TcParams tc_plan(unsigned type, unsigned rows, unsigned cols, unsigned nv, int sms, size_t *scratch_bytes)
 {
     TcParams p = {};
     p.rows = rows; p.K = cols; p.nblk = cols / 256; p.tiles = (rows + 15) / 16; p.mtiles = (p.tiles + 7) / 8;
     p.nv = nv; p.N = tc_n(nv);
-    p.nbs = tc_blocks_per_slice(type, p.N, p.nblk);
-    p.KS = p.nbs ? (p.nblk + p.nbs - 1) / p.nbs : 0;
-    p.G = p.KS && p.KS <= (unsigned)sms ? std::max(1u, std::min((unsigned)sms / p.KS, p.mtiles)) : 0;
+    const TcDepth dp = tc_depth(type, p.N);
+    p.rs = dp.rs; p.rb = dp.rb; p.da = dp.da; p.dc = dp.dc;
+    // tuning override "operand buffers,unit stages,B stages" (FYB_TC_DEPTH), taken when it fits
+    if (const char *env = std::getenv("FYB_TC_DEPTH")) {
+        unsigned a = 0, r = 0, b = 0;
+        if (std::sscanf(env, "%u,%u,%u", &a, &r, &b) == 3 && a >= 2 && a <= 8 && r >= 2 && r <= 16 && b >= 2 &&
+            b <= 16 && tc_smem(type, p.N, r, b, a, 4).total <= 227 * 1024) {
+            p.da = a; p.rs = r; p.rb = b;
+        }
+    }
+    *scratch_bytes = 0;
+    if (!p.rs || sms < 1 || p.nblk == 0) return p;
+    const double item_us = unit_bytes(type) * 8 / 43.0e3;
+    double best = 1e30;
+    for (unsigned nbs = p.nblk; nbs >= 1; --nbs) {
+        const unsigned ks = (p.nblk + nbs - 1) / nbs;
+        if ((p.nblk + ks - 1) / ks != nbs || ks > (unsigned)sms) continue;  // the same slices with fewer blocks
+        const unsigned g = std::max(1u, std::min((unsigned)sms / ks, p.mtiles));
+        const unsigned mt = (p.mtiles + g - 1) / g;
+        double cost = (double)mt * nbs * item_us;
+        if (ks > 1) cost += 1.0 + (double)ks * mt * 128 * nv * 4 / 150.0e3;  // slice sum (us)
+        if (cost < best) { best = cost; p.nbs = nbs; p.KS = ks; p.G = g; }
+    }
     *scratch_bytes = p.KS > 1 ? (size_t)p.KS * p.mtiles * 128 * (p.N / 4) * sizeof(float) : 0;
     return p;
 }
 
-// Workspace of either kernel: the larger of the two needs.
+// Workspace: [counters][B blocks (tcgen05 path)][slice scratch of either kernel].
+static size_t tc_bops_bytes(unsigned N, unsigned nblk) { return ((size_t)nblk * tc_bblk(N) + 255) / 256 * 256; }
+
 size_t qgemm_workspace_bytes(unsigned type, size_t rows, size_t cols, size_t nv, int sms)
 {
     if (nv < 3 || nv > 2 * QM_MAX_PAIRS || cols % 256 || sms > 1024) return 0;
-    size_t sb, cn, tb = 0;
+    size_t sb, cn, tb = 0, bb = 0;
     qm_plan(type, (unsigned)rows, (unsigned)cols, (unsigned)nv, sms, &sb, &cn);
-    if (nv >= TC_MIN_NV) tc_plan(type, (unsigned)rows, (unsigned)cols, (unsigned)nv, sms, &tb);
-    return QM_COUNTER_BYTES + (std::max(sb, tb) + 255) / 256 * 256;
+    if (nv >= TC_MIN_NV) {
+        tc_plan(type, (unsigned)rows, (unsigned)cols, (unsigned)nv, sms, &tb);
+        bb = tc_bops_bytes(tc_n((unsigned)nv), (unsigned)(cols / 256));
+    }
+    return QM_COUNTER_BYTES + bb + (std::max(sb, tb) + 255) / 256 * 256;
+}
+
+template <unsigned TYPE, unsigned N>
+static cudaError_t launch_tc_n(const TcParams &p, cudaStream_t st)
+{
+    cudaError_t e = cudaSuccess;
+    tc_limbs_kernel<N><<<p.nblk, N * 4, 0, st>>>(p.x, p.K, p.nv, const_cast<unsigned char *>(p.bops), p.error);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // at least half of the SM's shared memory, so one CTA holds an SM and
+    // its TMEM allocation never waits for another CTA's
+    const size_t smem = std::max(tc_smem(TYPE, N, p.rs, p.rb, p.da, p.dc).total, (size_t)116 * 1024);
+    if ((e = cudaFuncSetAttribute(qgemm_tc_kernel<TYPE, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+        cudaSuccess)
+        return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.G * p.KS);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, qgemm_tc_kernel<TYPE, N>, p);
 }
 
 template <unsigned TYPE>
 static cudaError_t launch_tc(const TcParams &p, cudaStream_t st)
 {
-    // at least half of the SM's shared memory, so one CTA holds an SM and
-    // its TMEM allocation never waits for another CTA's
-    const size_t smem = std::max(tc_smem(TYPE, p.N, p.nbs).total, (size_t)116 * 1024);
-    cudaError_t e = cudaSuccess;
-#define FYB_TC(NHV)                                                                                               \
-    if (p.N == 2 * NHV) {                                                                                         \
-        e = cudaFuncSetAttribute(qgemm_tc_kernel<TYPE, NHV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-        if (e == cudaSuccess) qgemm_tc_kernel<TYPE, NHV><<<p.G * p.KS, TC_THREADS, smem, st>>>(p);               \
-    }
-    FYB_TC(8) FYB_TC(16) FYB_TC(32)
-#undef FYB_TC
-    return e != cudaSuccess ? e : cudaGetLastError();
+    if (p.N == 16) return launch_tc_n<TYPE, 16>(p, st);
+    if (p.N == 32) return launch_tc_n<TYPE, 32>(p, st);
+    return launch_tc_n<TYPE, 64>(p, st);
 }
 
 int launch_qgemm(const QWeights &w, unsigned rows, const float *x, float *y, size_t out_stride, unsigned nv,
@@ -744,15 +945,16 @@ int launch_qgemm(const QWeights &w, unsigned rows, const float *x, float *y, siz
         !x || !y || rows == 0 || (rows + 15) / 16 != w.tiles || !workspace || sms > 1024)
         return -1;
     if (workspace_bytes < qgemm_workspace_bytes(w.type, rows, w.cols, nv, sms)) return -1;
+    unsigned char *ws = reinterpret_cast<unsigned char *>(workspace);
     if (nv >= TC_MIN_NV) {
         size_t tb;
         TcParams p = tc_plan(w.type, rows, w.cols, nv, sms, &tb);
         if (p.G) {
             p.units = w.units;
             p.x = x; p.y = y; p.out_stride = out_stride;
-            p.counters = reinterpret_cast<unsigned *>(workspace);
-            p.scratch = tb ? reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(workspace) + QM_COUNTER_BYTES)
-                           : nullptr;
+            p.counters = reinterpret_cast<unsigned *>(ws);
+            p.bops = ws + QM_COUNTER_BYTES;
+            p.scratch = tb ? reinterpret_cast<float *>(ws + QM_COUNTER_BYTES + tc_bops_bytes(p.N, p.nblk)) : nullptr;
             p.error = error;
             const cudaError_t e = w.type == T_Q4_K ? launch_tc<T_Q4_K>(p, st) : launch_tc<T_Q6_K>(p, st);
             return e == cudaSuccess ? 0 : -2;
@@ -763,8 +965,8 @@ int launch_qgemm(const QWeights &w, unsigned rows, const float *x, float *y, siz
     if (p.G == 0) return -1;
     p.units = w.units;
     p.x = x; p.y = y; p.out_stride = out_stride;
-    p.counters = reinterpret_cast<unsigned *>(workspace);
-    p.scratch = sb ? reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(workspace) + QM_COUNTER_BYTES) : nullptr;
+    p.counters = reinterpret_cast<unsigned *>(ws);
+    p.scratch = sb ? reinterpret_cast<float *>(ws + QM_COUNTER_BYTES) : nullptr;
     p.error = error;
     const size_t smem = qm_smem(p.np, p.nbs).total;
     auto kern = w.type == T_Q4_K ? qgemm_kernel<T_Q4_K> : qgemm_kernel<T_Q6_K>;
