@@ -288,7 +288,7 @@ constexpr size_t QM_COUNTER_BYTES = 4096;  // up to 1024 tile groups
 // vectors once into the B operand of every 256-column block: four signed
 // 7-bit limbs per value (the split of the mma.sync path), stored as
 // canonical K-major core matrices, followed by the block's x constants
-// (exponents, 32-value group sums, limb sums). The GEMM kernel then runs one
+// (limb scales, 32-value group sums, limb sums). The GEMM kernel then runs one
 // CTA per SM as a warp-specialized pipeline over items; an item is one
 // M-tile of 128 weight rows (8 unit tiles) times one block of the CTA's K
 // slice:
@@ -301,14 +301,16 @@ constexpr size_t QM_COUNTER_BYTES = 4096;  // up to 1024 tile groups
 //    still runs and waits for that kernel only before the first B copy;
 //  - staging (warps 2-9, two threads per row, each four of the eight
 //    groups): form the scaled weights A' = s q of the row as two byte planes
-//    in one of up to four operand buffers (two halves of 128 columns per
-//    item). Q4_K: s = 8 s_hi + s_lo with 3-bit parts, plane p = s_p q <= 105,
+//    in one of four operand half-buffers in tensor memory (tcgen05.st;
+//    two halves of 128 columns per item), so neither the staging nor the MMA
+//    moves the 2-byte-per-weight operand through shared memory. Q4_K: s = 8 s_hi + s_lo with 3-bit parts, plane p = s_p q <= 105,
 //    one integer multiply per four packed nibbles (no carries between
 //    bytes); Q6_K: s (q - 32) + 8192 in 16-bit lanes split into its two
 //    bytes. They also copy the row's block constants (d, dmin, minimums) to a
 //    small buffer for the epilogue, so the unit stage is free as soon as the
 //    item is staged;
-//  - MMA (warp 1, one thread): tcgen05.mma kind::i8 (u8 A x s8 B, M 128,
+//  - MMA (warp 1, one thread): tcgen05.mma kind::i8 (u8 A from TMEM x s8 B
+//    from shared memory, M 128,
 //    N = 4 limbs x padded vectors, K 32) per 32-value group and plane into
 //    one of four TMEM accumulators (the eight groups of a block accumulate in
 //    TMEM, so the group scales cost no epilogue work); tcgen05.commit frees
@@ -328,25 +330,29 @@ constexpr unsigned TC_THREADS = 576;              // 18 warps
 constexpr unsigned TC_STAGE0 = 2, TC_NSTAGE = 8;  // staging warps 2..9
 constexpr unsigned TC_EPI0 = 10, TC_NEPI = 8;     // epilogue warps 10..17
 constexpr unsigned TC_MIN_NV = 9;  // below it the mma.sync kernel is faster (measured)
+#ifndef FYB_TC_SLEEP_NS
+#define FYB_TC_SLEEP_NS 64
+#endif
 constexpr unsigned TC_CST = 2048;                 // per item: 128 rows x 16 B
 
 FYB_HOST_DEV unsigned tc_n(unsigned nv) { return nv <= 4 ? 16u : nv <= 8 ? 32u : 64u; }  // 4 limbs x padded vectors
 // B block: the MMA's operand [8 groups][N/8 core rows][2 K halves][8][16] s8
-// limbs | exps [N/4] | group sums [N/4][8] | limb sums [N]
+// limbs | limb scales [N/4][4] (2^(E - 6 - 7 l) of the block exponent E) |
+// group sums [N/4][8] | limb sums [N]
 FYB_HOST_DEV constexpr unsigned tc_bop(unsigned N) { return 8 * N * 32; }
-FYB_HOST_DEV constexpr unsigned tc_bblk(unsigned N) { return tc_bop(N) + (N / 4) * 4 + (N / 4) * 32 + N * 4; }
+FYB_HOST_DEV constexpr unsigned tc_bblk(unsigned N) { return tc_bop(N) + (N / 4) * 16 + (N / 4) * 32 + N * 4; }
 
 struct TcSmem {
     size_t a, ring, bring, cst, bars, misc, total;
 };
 
-// da operand half-buffers (2 planes x 4 groups x 128 x 32 B), rs unit ring
-// stages (8 units each), rb B stages, dc accumulator / constant buffers.
+// rs unit ring stages (8 units each), rb B stages, dc constant buffers,
+// barriers for da operand half-buffers and dc accumulators (both in TMEM).
 FYB_HOST_DEV TcSmem tc_smem(unsigned type, unsigned N, unsigned rs, unsigned rb, unsigned da, unsigned dc)
 {
     TcSmem s;
-    s.a = 0;                                                  // [da][2 planes][4 groups][128 x 32 B]
-    s.ring = s.a + (size_t)da * 32768;                        // [rs][8 units]
+    s.a = 0;
+    s.ring = 0;                                               // [rs][8 units]
     s.bring = s.ring + (size_t)rs * 8 * unit_bytes(type);     // [rb][B block]
     s.cst = s.bring + (size_t)rb * tc_bblk(N);                // [dc][TC_CST]
     s.bars = s.cst + (size_t)dc * TC_CST;
@@ -355,17 +361,20 @@ FYB_HOST_DEV TcSmem tc_smem(unsigned type, unsigned N, unsigned rs, unsigned rb,
     return s;
 }
 
-// Pipeline depths: four accumulators (4 x 2N TMEM columns, 512 at most)
-// and the first of these (operand buffers, unit stages, B stages) that fits.
+// TMEM columns (512, one CTA per SM): dc accumulators of 2N columns (two
+// planes), then da operand half-buffers of 64 columns (2 planes x 4 groups x
+// 32 bytes per row). Four half-buffers; four accumulators, two at N = 64.
+// Shared memory: the most unit stages (up to 8), then B stages (up to 4).
 struct TcDepth {
     unsigned rs, rb, da, dc;
 };
 static TcDepth tc_depth(unsigned type, unsigned N)
 {
     constexpr size_t cap = 227 * 1024;
-    const unsigned pref[][3] = {{4, 4, 3}, {4, 3, 3}, {3, 4, 3}, {3, 4, 2}, {3, 3, 3}, {3, 3, 2}, {2, 3, 2}, {2, 2, 2}};
-    for (const auto &q : pref)
-        if (tc_smem(type, N, q[1], q[2], q[0], 4).total <= cap) return {q[1], q[2], q[0], 4};
+    const unsigned da = 4, dc = N == 64 ? 2 : 4;
+    for (unsigned rb = 4; rb >= 2; --rb)
+        for (unsigned rs = 8; rs >= 3; --rs)
+            if (tc_smem(type, N, rs, rb, da, dc).total <= cap && (rs >= 6 || rb == 2)) return {rs, rb, da, dc};
     return {0, 0, 0, 0};
 }
 
@@ -393,9 +402,9 @@ __global__ void __launch_bounds__(N * 4) tc_limbs_kernel(const float *x, unsigne
 {
     const unsigned bl = blockIdx.x, v = threadIdx.x >> 4, k16 = threadIdx.x & 15;
     unsigned char *out = bops + (size_t)bl * tc_bblk(N);
-    int *exps = reinterpret_cast<int *>(out + tc_bop(N));
-    float *gsums = reinterpret_cast<float *>(out + tc_bop(N) + (N / 4) * 4);
-    int *lsum = reinterpret_cast<int *>(out + tc_bop(N) + (N / 4) * 36);
+    float *scl = reinterpret_cast<float *>(out + tc_bop(N));
+    float *gsums = reinterpret_cast<float *>(out + tc_bop(N) + (N / 4) * 16);
+    int *lsum = reinterpret_cast<int *>(out + tc_bop(N) + (N / 4) * 48);
     float xv[16];
     if (v < nv) load16(x + (size_t)v * K + (size_t)bl * 256 + 16 * k16, xv);
     else {
@@ -416,7 +425,7 @@ __global__ void __launch_bounds__(N * 4) tc_limbs_kernel(const float *x, unsigne
         frexpf(mx, &E);
         if (E < -120) E = -120;  // below 2^-121 the limbs round to zero anyway
     }
-    if (k16 == 0) exps[v] = E;
+    if (k16 < 4) scl[v * 4 + k16] = pow2f(E - 6 - 7 * (int)k16);
     if (bad && error) *(volatile unsigned *)error = ERR_NONFINITE;
     const float sc = pow2f(6 - E);
     unsigned words[4][4];
@@ -491,6 +500,23 @@ FYB_DEV void tc_ld8(uint32_t taddr, int *r)
                  : "r"(taddr) : "memory");
 }
 FYB_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// sixteen consecutive 32-bit columns of this thread's TMEM lane
+FYB_DEV void tc_st16(uint32_t taddr, const unsigned (&v)[16])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+                 "%14, %15, %16};"
+                 :: "r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+                    "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+                 : "memory");
+}
+FYB_DEV void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// D (TMEM) (+)= A (TMEM: row m in lane m, 32 int8 K values in 8 consecutive columns) x B (shared memory)
+FYB_DEV void tc_mma_ta(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n"
+                 :: "r"(d), "r"(a), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
+}
 FYB_DEV void mbar_arrive(uint64_t *bar)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
@@ -503,13 +529,23 @@ FYB_DEV bool mbar_test_wait(uint64_t *bar, unsigned parity)  // non-blocking
     return ok != 0;
 }
 // Bounded wait that also gives up when another role raised the abort word.
+// After a few polls it sleeps between polls, so waiting warps leave the
+// issue slots to the warps that stage operands.
 FYB_DEV bool tc_wait(uint64_t *bar, unsigned parity, const volatile unsigned *abort)
 {
     for (unsigned i = 0; i < (1u << 22); ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 63u && *abort) return false;
+        if (i >= 4) __nanosleep(FYB_TC_SLEEP_NS);
     }
     return false;
+}
+
+// The same for every lane of a warp (the warp then runs .sync.aligned
+// tcgen05 instructions together).
+FYB_DEV bool tc_wait_warp(uint64_t *bar, unsigned parity, const volatile unsigned *abort)
+{
+    return __all_sync(0xffffffffu, tc_wait(bar, parity, abort));
 }
 
 // A' = (s - m) q + bias of four packed byte values q < 64 in 16-bit lanes
@@ -532,11 +568,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
     constexpr unsigned BBLK = tc_bblk(N);
     constexpr unsigned BOP = tc_bop(N);
     constexpr unsigned UB = unit_bytes(TYPE);
-    constexpr unsigned NCOLS = 8 * N;       // four accumulators x two planes: 128, 256 or 512 TMEM columns
+    constexpr unsigned NCOLS = 512;         // accumulators and operand buffers
     extern __shared__ __align__(1024) unsigned char smem[];
     const unsigned rs = p.rs, rb = p.rb, da = p.da, dc = p.dc;
     const TcSmem L = tc_smem(TYPE, N, rs, rb, da, dc);
-    unsigned char *abuf = smem + L.a;
     unsigned char *ring = smem + L.ring;
     unsigned char *bring = smem + L.bring;
     unsigned char *cst = smem + L.cst;
@@ -583,6 +618,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const uint32_t acols = dc * 2 * N;  // first TMEM column of the operand half-buffers
     auto fail = [&]() {
         *abort = 1u;
         if (p.error) atomicCAS(p.error, 0u, (unsigned)ERR_TIMEOUT);
@@ -639,13 +675,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
                     const unsigned hh = 2 * it + h, ab = hh % da;
                     if (!tc_wait(a_full + ab, (hh / da) & 1u, abort)) { fail(); ok = false; break; }
                     tc_fence_after();
-                    const unsigned char *ah = abuf + ab * 32768;
+                    const uint32_t ah = tmem + acols + ab * 64;  // plane p, group gl at column 32 p + 8 gl
 #pragma unroll
                     for (unsigned gl = 0; gl < 4; ++gl) {
                         const uint64_t bd = tc_desc(bb + (size_t)(4 * h + gl) * N * 32);
                         const uint32_t acc_in = (h | gl) ? 1u : 0u;
-                        tc_mma(dacc, tc_desc(ah + gl * 4096), bd, idesc, acc_in);
-                        tc_mma(dacc + N, tc_desc(ah + (4 + gl) * 4096), bd, idesc, acc_in);
+                        tc_mma_ta(dacc, ah + gl * 8, bd, idesc, acc_in);
+                        tc_mma_ta(dacc + N, ah + 32 + gl * 8, bd, idesc, acc_in);
                     }
                     tc_commit(a_empty + ab);
                 }
@@ -659,15 +695,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
         }
     } else if (warp < TC_EPI0) {
         // ---------------------------------------------------------- staging
-        const unsigned sid = threadIdx.x - TC_STAGE0 * 32;  // 0..255
-        const unsigned R = sid & 127, vh = sid >> 7, tile = R >> 4, r = R & 15;
+        // warp w writes TMEM lanes 32 (w % 4)..+31: row R, half vh of the groups
+        const unsigned q4 = warp & 3u, vh = (warp - TC_STAGE0) >> 2;
+        const unsigned R = 32 * q4 + lane, tile = R >> 4, r = R & 15;
+        const uint32_t tA = tmem + ((32u * q4) << 16) + acols;
         for (unsigned it = 0; it < items; ++it) {
             const unsigned st = it % rs, mt = mb + it / nb, cb = it % dc;
-            if (!tc_wait(u_full + st, (it / rs) & 1u, abort)) { fail(); break; }
+            if (!tc_wait_warp(u_full + st, (it / rs) & 1u, abort)) { fail(); break; }
             const bool have = mt * 8 + tile < p.tiles;
             const unsigned char *u = ring + (size_t)st * 8 * UB + tile * UB;
             // the row's block constants for the epilogue
-            if (it >= dc && !tc_wait(cst_empty + cb, (it / dc - 1) & 1u, abort)) { fail(); break; }
+            if (it >= dc && !tc_wait_warp(cst_empty + cb, (it / dc - 1) & 1u, abort)) { fail(); break; }
             unsigned char *cb_base = cst + cb * TC_CST;
             uint4 hd = make_uint4(0u, 0u, 0u, 0u);
             if constexpr (TYPE == T_Q4_K) {
@@ -691,8 +729,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
             bool ok = true;
             for (unsigned h = 0; h < 2; ++h) {
                 const unsigned hh = 2 * it + h, ab = hh % da;
-                if (hh >= da && !tc_wait(a_empty + ab, (hh / da - 1) & 1u, abort)) { fail(); ok = false; break; }
-                unsigned char *ah = abuf + ab * 32768;
+                if (hh >= da && !tc_wait_warp(a_empty + ab, (hh / da - 1) & 1u, abort)) { fail(); ok = false; break; }
+                unsigned v0[16], v1[16];  // planes 0 and 1: groups 2 vh, 2 vh + 1 of the half (K order)
 #pragma unroll
                 for (unsigned gi = 0; gi < 2; ++gi) {
                     const unsigned g = 4 * h + 2 * vh + gi, gl = 2 * vh + gi;
@@ -736,11 +774,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
                             lo4 = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                             hi4 = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                         }
-                        *reinterpret_cast<uint4 *>(ah + gl * 4096 + tc_core(R, kc)) = lo4;
-                        *reinterpret_cast<uint4 *>(ah + (4 + gl) * 4096 + tc_core(R, kc)) = hi4;
+                        const unsigned o = gi * 8 + kc * 4;
+                        v0[o] = lo4.x; v0[o + 1] = lo4.y; v0[o + 2] = lo4.z; v0[o + 3] = lo4.w;
+                        v1[o] = hi4.x; v1[o + 1] = hi4.y; v1[o + 2] = hi4.z; v1[o + 3] = hi4.w;
                     }
                 }
-                fence_proxy_async();  // the operand is read by the tensor cores (async proxy)
+                tc_st16(tA + ab * 64 + 16 * vh, v0);
+                tc_st16(tA + ab * 64 + 32 + 16 * vh, v1);
+                tc_wait_st();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(a_full + ab);
             }
@@ -759,8 +801,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
         for (unsigned it = 0; it < items; ++it) {
             const unsigned t = it % dc, mt = mb + it / nb, bl = it % nb, sb = it % rb;
             // b_full is complete already; waiting on it orders the B block's bytes for these threads
-            if (!tc_wait(acc_full + t, (it / dc) & 1u, abort) || !tc_wait(cst_full + t, (it / dc) & 1u, abort) ||
-                !tc_wait(b_full + sb, (it / rb) & 1u, abort)) {
+            if (!tc_wait_warp(acc_full + t, (it / dc) & 1u, abort) || !tc_wait_warp(cst_full + t, (it / dc) & 1u, abort) ||
+                !tc_wait_warp(b_full + sb, (it / rb) & 1u, abort)) {
                 fail();
                 break;
             }
@@ -768,9 +810,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
             const unsigned char *cb_base = cst + t * TC_CST;
             const uint4 c = *reinterpret_cast<const uint4 *>(cb_base + R * 16);
             const unsigned char *xcon = bring + (size_t)sb * BBLK + BOP;  // the block's x constants
-            const int *exps = reinterpret_cast<const int *>(xcon);
-            const float *gsums = reinterpret_cast<const float *>(xcon + NV4 * 4);
-            const int *lsum = reinterpret_cast<const int *>(xcon + NV4 * 36);
+            const float4 *scl = reinterpret_cast<const float4 *>(xcon);
+            const float *gsums = reinterpret_cast<const float *>(xcon + NV4 * 16);
+            const int *lsum = reinterpret_cast<const int *>(xcon + NV4 * 48);
             const float d = __uint_as_float(c.x), dmin = __uint_as_float(c.y);
             float mins[8];
 #pragma unroll
@@ -785,12 +827,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
 #pragma unroll
                 for (unsigned k = 0; k < 2; ++k) {
                     const unsigned qv = c8 / 4 + k, v = vh * EV + qv;
-                    const int E = exps[v];
+                    const float4 fs = scl[v];  // 2^(E - 6), 2^(E - 13), 2^(E - 20), 2^(E - 27)
                     if constexpr (TYPE == T_Q4_K) {
                         const int T0 = lo[4 * k] + 8 * hi[4 * k], T1 = lo[4 * k + 1] + 8 * hi[4 * k + 1];
                         const int T2 = lo[4 * k + 2] + 8 * hi[4 * k + 2], T3 = lo[4 * k + 3] + 8 * hi[4 * k + 3];
                         const int P01 = T0 * 128 + T1, P23 = T2 * 128 + T3;  // |T| <= 945 * 64 * 256: below 2^31
-                        const float sum = fmaf((float)P01, pow2f(E - 13), (float)P23 * pow2f(E - 27));
+                        const float sum = fmaf((float)P01, fs.y, (float)P23 * fs.w);
                         acc[qv] = fmaf(d, sum, acc[qv]);
                         const float *gsv = gsums + v * 8;
                         float mt_ = 0.f;
@@ -798,11 +840,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) qgemm_tc_kernel(const TcParams 
                         for (int g = 0; g < 8; ++g) mt_ = fmaf(mins[g], gsv[g], mt_);
                         acc[qv] = fmaf(-dmin, mt_, acc[qv]);
                     } else {
+                        const float f[4] = {fs.x, fs.y, fs.z, fs.w};
                         float sum = 0.f;
 #pragma unroll
                         for (unsigned l = 0; l < 4; ++l) {
                             const int T = lo[4 * k + l] + (hi[4 * k + l] << 8) - 8192 * lsum[4 * v + l];
-                            sum = fmaf((float)T, pow2f(E - 6 - 7 * (int)l), sum);
+                            sum = fmaf((float)T, f[l], sum);
                         }
                         acc[qv] = fmaf(d, sum, acc[qv]);
                     }
