@@ -180,6 +180,44 @@ def cpu_reference_rate(model_ptr, vocabulary, sample_seconds, max_tokens=64):
 
 
 # ----------------------------------------------------------------------------- provider arm
+def batch_decode(nseq, steps=3, warmup=1, model_name="8b"):
+    """Batched decode (fyb_batch_*): nseq sequences of the 8B model, each
+    with its own random 512-token prompt (prefilled by batched steps, one
+    token of every sequence per step), then greedy decode of DECODE tokens per
+    sequence at positions 512.., timed with CUDA events over graph replays.
+    Returns tok/s over all sequences, ms per step, the weight bytes per step
+    and the GB/s those bytes make at that step time."""
+    import fyodor_b200 as F
+    from tests.patterns import bench_tokens
+    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **CFG8B)
+    provider = F.Provider()
+    plan = provider.plan(model, PROMPT + DECODE + 2)
+    if plan is None:
+        raise SystemExit("the provider declined the 8B plan")
+    batch = F.Batch(plan, nseq)
+    prompts = np.stack([bench_tokens(PROMPT, model.vocabulary, start=997 * b) for b in range(nseq)])
+    for i in range(PROMPT):
+        _, am = batch.step(prompts[:, i], np.full(nseq, i, np.uint32), logits=False)
+    first, start = am.astype(np.uint32), np.full(nseq, PROMPT, np.uint32)
+    for _ in range(warmup):
+        batch.time_greedy(first, start, DECODE)
+    ms = [batch.time_greedy(first, start, DECODE) for _ in range(steps)]
+    if min(ms) < 0:
+        raise SystemExit("batched decode failed")
+    step_ms = sum(ms) / len(ms)
+    out = {"sequences": nseq, "tok_s": round(nseq * 1000.0 / step_ms, 1), "ms_per_step": round(step_ms, 4),
+           "weight_bytes_per_step": WEIGHT_BYTES_8B,
+           "weights_gb_s": round(WEIGHT_BYTES_8B / step_ms / 1e6, 1),
+           "launches_per_step": int(batch.launches_per_step()),
+           "workload": "8B, %d sequences x (512-token prompt + %d greedy tokens), positions 512..%d"
+                       % (nseq, DECODE, PROMPT + DECODE - 1)}
+    batch.close()
+    plan.close()
+    model.close()
+    provider.close()
+    return out
+
+
 def run_provider(args):
     import torch
     import fyodor_b200 as F
@@ -837,6 +875,7 @@ def main():
     ap.add_argument("--seqs", type=int, default=32, help="with --attention: sequences of the ragged batch")
     ap.add_argument("--allreduce-probe", action="store_true",
                     help="under torchrun: time the reference design's NCCL all-reduce of the residual")
+    ap.add_argument("--batch", type=int, default=0, help="time batched decode of this many sequences (1..16)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--model", default="8b", choices=["8b", "70b"], help="70b: the tensor-parallel 70B configuration")
     ap.add_argument("--steps", type=int, default=5)
@@ -851,6 +890,8 @@ def main():
     elif args.matvec:
         print(json.dumps({"matvec_c1": matvec_c1(cpu=not args.no_cpu_baseline),
                           "matvec_c2": matvec_c2(cpu=not args.no_cpu_baseline)}))
+    elif args.batch:
+        print(json.dumps({"batch_decode": batch_decode(args.batch)}))
     elif args.allreduce_probe:
         run_allreduce_probe(args)
     elif args.gemm_case:

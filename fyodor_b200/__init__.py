@@ -123,6 +123,15 @@ def _load():
     lib.fyb_plan_profile.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t, _P]
     lib.fyb_plan_time_projection.restype = C.c_double
     lib.fyb_plan_time_projection.argtypes = [_P, C.c_uint, C.c_uint, C.c_uint, C.POINTER(C.c_size_t)]
+    lib.fyb_batch_create.restype = _P
+    lib.fyb_batch_create.argtypes = [_P, C.c_uint]
+    lib.fyb_batch_free.argtypes = [_P]
+    lib.fyb_batch_step.argtypes = [_P, _P, _P, _P, _P]
+    lib.fyb_batch_decode_greedy.argtypes = [_P, _P, _P, C.c_size_t, _P]
+    lib.fyb_batch_time_greedy.restype = C.c_double
+    lib.fyb_batch_time_greedy.argtypes = [_P, _P, _P, C.c_size_t]
+    lib.fyb_batch_launches_per_step.restype = C.c_ulonglong
+    lib.fyb_batch_launches_per_step.argtypes = [_P]
     lib.fyb_synth_create.restype = _P
     lib.fyb_synth_create.argtypes = [C.POINTER(SynthConfig)]
     lib.fyb_synth_free.argtypes = [_P]
@@ -140,6 +149,8 @@ EXPORTS = ["nya_cuda_backend", "fyb_version", "fyb_device_count", "fyb_dequantiz
            "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_decode_form", "fyb_plan_profile", "fyb_plan_trace",
            "fyb_plan_tp_info", "fyb_plan_tp_handle", "fyb_plan_tp_connect", "fyb_plan_tp_disconnect",
            "fyb_plan_tp_connect_local", "fyb_plan_error", "fyb_plan_time_projection",
+           "fyb_batch_create", "fyb_batch_free", "fyb_batch_step", "fyb_batch_decode_greedy", "fyb_batch_time_greedy",
+           "fyb_batch_launches_per_step",
            "fyb_synth_create",
            "fyb_synth_free", "fyb_synth_fill"]
 
@@ -275,6 +286,60 @@ class Provider:
                 plan.close()
             self.api.destroy(self.state)
             self.state = None
+
+    def __del__(self):
+        self.close()
+
+
+class Batch:
+    """B sequences (1..16) of one plan's model decoded together (fyb_batch_*):
+    each sequence has its own KV cache and position; every projection reads
+    each weight once per step for all of them. The plan must outlive it."""
+
+    def __init__(self, plan, batch):
+        self.plan, self.B = plan, batch
+        self.V = plan.model.vocabulary
+        self.ptr = lib.fyb_batch_create(C.c_void_p(plan.ptr), batch)
+        if not self.ptr:
+            raise ValueError("batch of %d declined" % batch)
+
+    def _req(self, tokens, positions):
+        t = np.ascontiguousarray(tokens, np.uint32)
+        p = np.ascontiguousarray(positions, np.uint32)
+        assert t.shape == (self.B,) and p.shape == (self.B,)
+        return t, p
+
+    def step(self, tokens, positions, logits=True):
+        """One step: (logits [B][V] or None, argmax [B])."""
+        t, p = self._req(tokens, positions)
+        lg = np.empty((self.B, self.V), np.float32) if logits else None
+        am = np.empty(self.B, np.uint32)
+        r = lib.fyb_batch_step(C.c_void_p(self.ptr), _ptr(t), _ptr(p), _ptr(lg), _ptr(am))
+        if r:
+            raise RuntimeError("fyb_batch_step failed (%d)" % r)
+        return lg, am
+
+    def decode_greedy(self, tokens, positions, steps):
+        """Greedy tokens [steps][B] decoded on the device."""
+        t, p = self._req(tokens, positions)
+        out = np.empty((steps, self.B), np.uint32)
+        r = lib.fyb_batch_decode_greedy(C.c_void_p(self.ptr), _ptr(t), _ptr(p), steps, _ptr(out))
+        if r:
+            raise RuntimeError("fyb_batch_decode_greedy failed (%d)" % r)
+        return out
+
+    def time_greedy(self, tokens, positions, steps):
+        """Milliseconds per greedy step (device events)."""
+        t, p = self._req(tokens, positions)
+        return lib.fyb_batch_time_greedy(C.c_void_p(self.ptr), _ptr(t), _ptr(p), steps)
+
+    def launches_per_step(self):
+        return lib.fyb_batch_launches_per_step(C.c_void_p(self.ptr))
+
+    def close(self):
+        if self.ptr:
+            lib.fyb_batch_free(C.c_void_p(self.ptr))
+            self.ptr = None
 
     def __del__(self):
         self.close()

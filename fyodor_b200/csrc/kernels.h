@@ -206,4 +206,21 @@ int decode_supported(const DecodeGeometry &g, unsigned type_out);
 int decode_grid(int sms, const DecodeGeometry &g);
 int launch_decode(const DecodeLaunch &L, cudaStream_t s);
 
+// ---------------------------------------------------------------- batch.cu
+// Elementwise kernels of the batched decode step (B <= BATCH_MAX sequences).
+// req on the device: [B] tokens | [B] positions | [B] attended lengths | step.
+constexpr unsigned BATCH_MAX = 16;
+struct BatchRequest {
+    unsigned token[BATCH_MAX], position[BATCH_MAX];
+};
+int launch_bt_add_norm(float *x, const float *delta, const float *w, float *xn, unsigned d, float eps, unsigned nseq,
+    cudaStream_t s);
+int launch_bt_rope_kv(const float *y, unsigned qkv_rows, unsigned H, unsigned Hkv, unsigned hd,
+    const unsigned *positions, const float *rope_cos, const float *rope_sin, float *q, __half *kc, __half *vc,
+    unsigned capacity, unsigned nseq, cudaStream_t s);
+int launch_bt_swiglu(const float *y, unsigned ffn, float *h, unsigned nseq, cudaStream_t s);
+int launch_bt_argmax(const float *logits, unsigned V, unsigned *req, unsigned nseq, unsigned *tokens_out, unsigned *log,
+    bool advance, unsigned *error, cudaStream_t s);
+int launch_bt_set(const BatchRequest &r, unsigned *req, unsigned nseq, cudaStream_t s);
+
 }  // namespace fyb

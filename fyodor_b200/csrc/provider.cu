@@ -1091,6 +1091,265 @@ extern "C" const nya_backend_interface *nya_cuda_backend(void)
     return &api;
 }
 
+// ======================================================================
+// Batched decode: B sequences (1..16) of one resident plan's model, each at
+// its own position with its own KV cache, decoded together. Every
+// projection is one small-batch GEMM over the plan's repacked weights
+// (GEMV for one or two sequences, the mma.sync GEMM for 3..8, tcgen05 for
+// 9..16: each weight unit read once per step for all sequences); attention
+// is the ragged-batch kernel over the sequences' caches; norms, RoPE + KV
+// append, SwiGLU and the greedy argmax are the kernels of batch.cu. A step is
+// captured in a CUDA graph after its first (eager) run has sized the GEMM
+// scratch; tokens, positions and attended lengths live on the device, so the
+// graph serves every step.
+// ======================================================================
+struct Batch {
+    Plan *p = nullptr;
+    unsigned B = 0;
+    size_t capacity = 0;
+    std::vector<void *> allocations;
+    __half *kc = nullptr, *vc = nullptr;  // [layer][seq][kv head][capacity][hd]
+    float *x = nullptr, *xn = nullptr, *delta = nullptr, *y = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
+    float *logits = nullptr;             // [B][V]
+    unsigned *req = nullptr;             // [B] tokens | [B] positions | [B] lengths | step
+    unsigned *tokens = nullptr;          // [B] argmax of the last step
+    unsigned *log = nullptr;             // [steps][B] greedy tokens
+    size_t log_bytes = 0;
+    void *attn_ws = nullptr;
+    size_t attn_ws_bytes = 0;
+    unsigned splits = 1;
+    unsigned *counters = nullptr;
+    size_t counters_bytes = 0;
+    float *partials = nullptr;
+    size_t partials_bytes = 0;
+    void *gemm = nullptr;
+    size_t gemm_bytes = 0;
+    cudaGraphExec_t graphs[2] = {nullptr, nullptr};  // logits step, greedy step
+    bool sized[2] = {false, false};
+    unsigned long long launches = 0;
+};
+
+static void batch_free(Batch *bt)
+{
+    if (!bt) return;
+    DeviceScope scope(bt->p->ctx->device);
+    cudaStreamSynchronize(bt->p->ctx->stream);
+    for (auto &g : bt->graphs) if (g) cudaGraphExecDestroy(g);
+    for (void *a : bt->allocations) cudaFree(a);  // the attention workspace among them
+    for (void *a : {(void *)bt->log, (void *)bt->counters, (void *)bt->partials, bt->gemm})  // grown buffers
+        if (a) cudaFree(a);
+    cudaGetLastError();
+    delete bt;
+}
+
+static AttentionLaunch batch_attention(const Batch *bt, unsigned l)
+{
+    const Plan *p = bt->p;
+    const size_t per_seq = (size_t)p->Hkv * bt->capacity * p->hd;
+    AttentionLaunch A;
+    A.q = bt->q;
+    A.k = bt->kc + (size_t)l * bt->B * per_seq;
+    A.v = bt->vc + (size_t)l * bt->B * per_seq;
+    A.seq_stride = per_seq;
+    A.lengths = bt->req + 2 * bt->B;
+    A.nseq = bt->B; A.heads = p->H; A.kv_heads = p->Hkv; A.head_dim = p->hd;
+    A.capacity = (unsigned)bt->capacity;
+    A.scale = 1.0f / std::sqrt((float)p->hd);
+    A.out = bt->attn;
+    A.splits = bt->splits;
+    A.workspace = bt->attn_ws; A.workspace_bytes = bt->attn_ws_bytes;
+    return A;
+}
+
+// One batched step reading tokens and positions from bt->req; greedy steps
+// advance every sequence to its argmax token at the next position.
+static int batch_enqueue(Batch *bt, bool greedy)
+{
+    Plan *p = bt->p;
+    cudaStream_t s = p->ctx->stream;
+    const int sms = p->ctx->sms;
+    const unsigned B = bt->B;
+    const Scratch sc{&bt->counters, &bt->counters_bytes, &bt->partials, &bt->partials_bytes, &bt->gemm,
+                     &bt->gemm_bytes};
+    const size_t per_seq = (size_t)p->Hkv * bt->capacity * p->hd;
+    bt->launches = 0;
+#define BRUN(expr) do { const int r_ = (expr); ++bt->launches; if (r_) return r_; } while (0)
+    BRUN(launch_gather_batch(p->embd, p->embd_row_bytes, p->embd_type, p->d, bt->req, B, bt->x, s));
+    for (unsigned l = 0; l < p->nl; ++l) {
+        const LayerW &L = p->layers[l];
+        const size_t qkv_rows = (size_t)L.qkv.tiles * 16, gu_rows = (size_t)L.gateup.tiles * 16;
+        BRUN(launch_bt_add_norm(bt->x, l ? bt->delta : nullptr, L.attn_norm, bt->xn, p->d, p->eps, B, s));
+        BRUN(device_matmul(&L.qkv, nullptr, 0, qkv_rows, p->d, L.qkv.type, bt->xn, bt->y, B, sc, s, sms));
+        BRUN(launch_bt_rope_kv(bt->y, (unsigned)qkv_rows, p->H, p->Hkv, p->hd, bt->req + B, p->rope_cos, p->rope_sin,
+                               bt->q, bt->kc + (size_t)l * B * per_seq, bt->vc + (size_t)l * B * per_seq,
+                               (unsigned)bt->capacity, B, s));
+        BRUN(launch_attention(batch_attention(bt, l), s));
+        BRUN(device_matmul(&L.o, nullptr, 0, p->d, (size_t)p->H * p->hd, L.o.type, bt->attn, bt->delta, B, sc, s, sms));
+        BRUN(launch_bt_add_norm(bt->x, bt->delta, L.ffn_norm, bt->xn, p->d, p->eps, B, s));
+        BRUN(device_matmul(&L.gateup, nullptr, 0, gu_rows, p->d, L.gateup.type, bt->xn, bt->y, B, sc, s, sms));
+        BRUN(launch_bt_swiglu(bt->y, p->ffn, bt->h, B, s));
+        BRUN(device_matmul(&L.down, nullptr, 0, p->d, p->ffn, L.down.type, bt->h, bt->delta, B, sc, s, sms));
+    }
+    BRUN(launch_bt_add_norm(bt->x, bt->delta, p->out_norm, bt->xn, p->d, p->eps, B, s));
+    BRUN(device_matmul(&p->out_head, nullptr, 0, p->V, p->d, p->out_head.type, bt->xn, bt->logits, B, sc, s, sms));
+    BRUN(launch_bt_argmax(bt->logits, p->V, bt->req, B, bt->tokens, bt->log, greedy, p->err_dev, s));
+#undef BRUN
+    return 0;
+}
+
+// The first step of a mode runs eagerly (the GEMM scratch grows to its
+// size); later steps replay one captured graph.
+static int batch_run(Batch *bt, bool greedy)
+{
+    cudaStream_t s = bt->p->ctx->stream;
+    const int m = greedy ? 1 : 0;
+    if (!bt->sized[m]) {
+        const int r = batch_enqueue(bt, greedy);
+        if (r) return r;
+        if (cudaStreamSynchronize(s) != cudaSuccess) return -2;
+        bt->sized[m] = true;
+        return 0;
+    }
+    if (!bt->graphs[m]) {
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return -2;
+        const int r = batch_enqueue(bt, greedy);
+        cudaError_t e = cudaStreamEndCapture(s, &g);
+        if (r || e != cudaSuccess) { if (g) cudaGraphDestroy(g); cudaGetLastError(); return -2; }
+        e = cudaGraphInstantiateWithFlags(&bt->graphs[m], g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) { bt->graphs[m] = nullptr; cudaGetLastError(); return -2; }
+    }
+    return cudaGraphLaunch(bt->graphs[m], s) == cudaSuccess ? 0 : -2;
+}
+
+static int batch_set(Batch *bt, const uint32_t *tokens, const uint32_t *positions, size_t steps)
+{
+    BatchRequest r = {};
+    for (unsigned b = 0; b < bt->B; ++b) {
+        if (tokens[b] >= bt->p->V || (size_t)positions[b] + steps > bt->capacity) return -1;
+        r.token[b] = tokens[b];
+        r.position[b] = positions[b];
+    }
+    return launch_bt_set(r, bt->req, bt->B, bt->p->ctx->stream);
+}
+
+extern "C" void *fyb_batch_create(void *plan, unsigned batch)
+{
+    Plan *p = (Plan *)plan;
+    if (!p || p->failed || batch < 1 || batch > BATCH_MAX || p->tp_size != 1 || p->hd % 16 || p->ffn % 8) return nullptr;
+    DeviceScope scope(p->ctx->device);
+    if (!scope.ok) return nullptr;
+    Batch *bt = new Batch;
+    bt->p = p;
+    bt->B = batch;
+    bt->capacity = p->capacity;
+    const size_t kv = (size_t)p->nl * batch * p->Hkv * bt->capacity * p->hd;
+    const size_t qkv_rows = (size_t)p->layers[0].qkv.tiles * 16;
+    const size_t ywidth = std::max<size_t>(qkv_rows, (size_t)p->layers[0].gateup.tiles * 16);
+    bool ok = true;
+    auto A = [&](size_t bytes) -> void * {
+        void *d = nullptr;
+        if (!ok || cudaMalloc(&d, bytes ? bytes : 256) != cudaSuccess) { cudaGetLastError(); ok = false; return nullptr; }
+        bt->allocations.push_back(d);
+        return d;
+    };
+    bt->kc = (__half *)A(kv * 2); bt->vc = (__half *)A(kv * 2);
+    bt->x = (float *)A((size_t)batch * p->d * 4); bt->xn = (float *)A((size_t)batch * p->d * 4);
+    bt->delta = (float *)A((size_t)batch * p->d * 4);
+    bt->y = (float *)A((size_t)batch * ywidth * 4);
+    bt->q = (float *)A((size_t)batch * p->H * p->hd * 4); bt->attn = (float *)A((size_t)batch * p->H * p->hd * 4);
+    bt->h = (float *)A((size_t)batch * p->ffn * 4);
+    bt->logits = (float *)A((size_t)batch * p->V * 4);
+    bt->req = (unsigned *)A((3 * BATCH_MAX + 1) * 4); bt->tokens = (unsigned *)A(BATCH_MAX * 4);
+    // partitions of each (sequence, KV head): about two waves of the SMs at the longest context
+    bt->splits = (unsigned)std::max<size_t>(1, std::min<size_t>(16, (size_t)2 * p->ctx->sms / (batch * p->Hkv)));
+    if (ok) {
+        AttentionLaunch L = batch_attention(bt, 0);
+        bt->attn_ws_bytes = attention_workspace_bytes(L);
+        bt->attn_ws = A(bt->attn_ws_bytes);
+    }
+    if (ok) ok = cudaMemset(bt->kc, 0, kv * 2) == cudaSuccess && cudaMemset(bt->vc, 0, kv * 2) == cudaSuccess &&
+                 cudaMemset(bt->attn_ws, 0, bt->attn_ws_bytes) == cudaSuccess &&
+                 cudaMemset(bt->req, 0, (3 * BATCH_MAX + 1) * 4) == cudaSuccess &&
+                 grow((void **)&bt->log, &bt->log_bytes, (size_t)BATCH_MAX * 4, true) == 0 &&
+                 cudaDeviceSynchronize() == cudaSuccess;
+    if (!ok) {
+        batch_free(bt);
+        return nullptr;
+    }
+    return bt;
+}
+
+extern "C" void fyb_batch_free(void *batch) { batch_free((Batch *)batch); }
+
+extern "C" int fyb_batch_step(void *batch, const uint32_t *tokens, const uint32_t *positions, float *logits,
+    uint32_t *argmax)
+{
+    Batch *bt = (Batch *)batch;
+    if (!bt || !tokens || !positions || bt->p->failed) return -1;
+    DeviceScope scope(bt->p->ctx->device);
+    if (!scope.ok) return -1;
+    cudaStream_t s = bt->p->ctx->stream;
+    int r = batch_set(bt, tokens, positions, 1);
+    if (r) return r;
+    if ((r = batch_run(bt, false)) != 0) return r;
+    if (logits && cudaMemcpyAsync(logits, bt->logits, (size_t)bt->B * bt->p->V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+        return -2;
+    if (argmax && cudaMemcpyAsync(argmax, bt->tokens, (size_t)bt->B * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+        return -2;
+    if (cudaStreamSynchronize(s) != cudaSuccess || *(volatile unsigned *)bt->p->err_host) return -2;
+    return 0;
+}
+
+// `steps` greedy steps from tokens / positions on the device; out[step][b].
+extern "C" int fyb_batch_decode_greedy(void *batch, const uint32_t *tokens, const uint32_t *positions, size_t steps,
+    uint32_t *out)
+{
+    Batch *bt = (Batch *)batch;
+    if (!bt || !tokens || !positions || !out || steps == 0 || bt->p->failed) return -1;
+    DeviceScope scope(bt->p->ctx->device);
+    if (!scope.ok) return -1;
+    cudaStream_t s = bt->p->ctx->stream;
+    if (grow((void **)&bt->log, &bt->log_bytes, steps * bt->B * 4, true)) return -2;
+    int r = batch_set(bt, tokens, positions, steps);
+    for (size_t i = 0; i < steps && !r; ++i) r = batch_run(bt, true);
+    if (r) return r;
+    if (cudaMemcpyAsync(out, bt->log, steps * bt->B * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess || *(volatile unsigned *)bt->p->err_host)
+        return -2;
+    return 0;
+}
+
+// Milliseconds per greedy step of `steps` graph replays (CUDA events on the
+// plan's stream, after one untimed step that captures the graph); < 0 on error.
+extern "C" double fyb_batch_time_greedy(void *batch, const uint32_t *tokens, const uint32_t *positions, size_t steps)
+{
+    Batch *bt = (Batch *)batch;
+    if (!bt || !tokens || !positions || steps == 0) return -1.0;
+    DeviceScope scope(bt->p->ctx->device);
+    cudaStream_t s = bt->p->ctx->stream;
+    if (grow((void **)&bt->log, &bt->log_bytes, (steps + 2) * bt->B * 4, true)) return -1.0;
+    if (batch_set(bt, tokens, positions, steps + 2)) return -1.0;
+    for (int w = 0; w < 2; ++w) if (batch_run(bt, true)) return -1.0;  // sizes, then captures
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0); cudaEventCreate(&e1);
+    cudaEventRecord(e0, s);
+    int r = 0;
+    for (size_t i = 0; i < steps && !r; ++i) r = batch_run(bt, true);
+    cudaEventRecord(e1, s);
+    float ms = -1.f;
+    if (!r && cudaEventSynchronize(e1) == cudaSuccess) cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0); cudaEventDestroy(e1);
+    if (r || *(volatile unsigned *)bt->p->err_host) return -1.0;
+    return ms / (double)steps;
+}
+
+extern "C" unsigned long long fyb_batch_launches_per_step(const void *batch)
+{
+    return batch ? ((const Batch *)batch)->launches : 0;
+}
+
 extern "C" const char *fyb_version(void) { return "fyodor_b200 0.1 (sm_100a)"; }
 
 extern "C" int fyb_device_count(void)

@@ -189,6 +189,31 @@ long fyb_plan_trace(void *plan, uint32_t token, size_t position, unsigned long l
    launches read different weights (more bytes than L2 holds). */
 double fyb_plan_time_projection(void *plan, unsigned layer, unsigned which, unsigned reps, size_t *bytes);
 
+/* ---- batched decode (the engine's per-token step, reference
+   CUDA/resident.inc:434-595 and backend/core/llm_cpu.c:424-578, applied to
+   B sequences at once; the reference plan decodes one sequence) ----------
+   fyb_batch_create: B (1..16) sequences of a resident plan's model, each with
+   its own fp16 KV cache of the plan's capacity and its own position; they
+   share the plan's weights (the plan must outlive the batch; single-GPU
+   plans only). NULL if declined. Every step multiplies each weight once for
+   all B sequences (batches of 9..16 on the tcgen05 small-batch GEMM).
+   fyb_batch_step: one step of every sequence b at positions[b] with
+   tokens[b] (position + 1 <= capacity); logits [B][V] (raw, no suppressed
+   ids) and argmax [B] (first index of the maximum) copied out when
+   non-null. 0 / -1 invalid / -2 device failure.
+   fyb_batch_decode_greedy: `steps` greedy steps on the device from
+   tokens / positions (each position + steps <= capacity); out [steps][B].
+   fyb_batch_time_greedy: milliseconds per greedy step over `steps` graph
+   replays (CUDA events), after two untimed steps; < 0 on error.
+   fyb_batch_launches_per_step: kernels in the last step enqueued. */
+void *fyb_batch_create(void *plan, unsigned batch);
+void fyb_batch_free(void *batch);
+int fyb_batch_step(void *batch, const uint32_t *tokens, const uint32_t *positions, float *logits, uint32_t *argmax);
+int fyb_batch_decode_greedy(void *batch, const uint32_t *tokens, const uint32_t *positions, size_t steps,
+    uint32_t *out);
+double fyb_batch_time_greedy(void *batch, const uint32_t *tokens, const uint32_t *positions, size_t steps);
+unsigned long long fyb_batch_launches_per_step(const void *batch);
+
 /* ---- tensor parallelism across processes (no reference counterpart) -----
    A process whose environment holds NYA_CUDA_TP_SIZE=N (2..8) and
    NYA_CUDA_TP_RANK=r (and NYA_CUDA_DEVICE for its GPU) creates plans that hold
