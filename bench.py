@@ -180,8 +180,9 @@ def cpu_reference_rate(model_ptr, vocabulary, sample_seconds, max_tokens=64):
 
 
 # ----------------------------------------------------------------------------- provider arm
-def batch_decode(nseq, steps=3, warmup=1, model_name="8b"):
-    """Batched decode (fyb_batch_*): nseq sequences of the 8B model, each
+def batch_decode(nseq, steps=3, warmup=1, plan=None, model=None, model_name="8b", prompt=PROMPT, decode=DECODE):
+    """Batched decode (fyb_batch_*): nseq sequences of the 8B (or, with
+    model_name "70b", the 70B) model, each
     with its own random 512-token prompt (prefilled by batched steps, one
     token of every sequence per step), then greedy decode of DECODE tokens per
     sequence at positions 512.., timed with CUDA events over graph replays.
@@ -189,32 +190,44 @@ def batch_decode(nseq, steps=3, warmup=1, model_name="8b"):
     and the GB/s those bytes make at that step time."""
     import fyodor_b200 as F
     from tests.patterns import bench_tokens
-    model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **CFG8B)
-    provider = F.Provider()
-    plan = provider.plan(model, PROMPT + DECODE + 2)
+    own = plan is None  # else: the bench's 8B plan (capacity PROMPT + DECODE), its weights shared
+    wbytes, name = WEIGHT_BYTES_8B, "8B"
+    if own and model_name == "70b":  # C5 geometry on one GPU, fp16 KV for 8192 positions per sequence
+        path = "/dev/shm/fyb_bench_70b_%d.bin" % CFG70B["seed"]
+        model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q4_K, path=path, **CFG70B)
+        if os.path.exists(path):
+            os.unlink(path)
+        provider = F.Provider()
+        plan = provider.plan(model, CAPACITY_70B)
+        wbytes, name = int(bytes_per_token_70b(1, [-1])), "70B"  # position -1: no KV term
+    elif own:
+        model = F.SynthModel(matrix_type=F.Q4_K, embed_type=F.Q6_K, output_type=F.Q6_K, **CFG8B)
+        provider = F.Provider()
+        plan = provider.plan(model, PROMPT + DECODE)
     if plan is None:
-        raise SystemExit("the provider declined the 8B plan")
+        raise SystemExit("the provider declined the %s plan" % name)
     batch = F.Batch(plan, nseq)
-    prompts = np.stack([bench_tokens(PROMPT, model.vocabulary, start=997 * b) for b in range(nseq)])
-    for i in range(PROMPT):
+    prompts = np.stack([bench_tokens(prompt, model.vocabulary, start=997 * b) for b in range(nseq)])
+    for i in range(prompt):
         _, am = batch.step(prompts[:, i], np.full(nseq, i, np.uint32), logits=False)
-    first, start = am.astype(np.uint32), np.full(nseq, PROMPT, np.uint32)
+    first, start = am.astype(np.uint32), np.full(nseq, prompt, np.uint32)
     for _ in range(warmup):
-        batch.time_greedy(first, start, DECODE)
-    ms = [batch.time_greedy(first, start, DECODE) for _ in range(steps)]
+        batch.time_greedy(first, start, decode)
+    ms = [batch.time_greedy(first, start, decode) for _ in range(steps)]
     if min(ms) < 0:
         raise SystemExit("batched decode failed")
     step_ms = sum(ms) / len(ms)
     out = {"sequences": nseq, "tok_s": round(nseq * 1000.0 / step_ms, 1), "ms_per_step": round(step_ms, 4),
-           "weight_bytes_per_step": WEIGHT_BYTES_8B,
-           "weights_gb_s": round(WEIGHT_BYTES_8B / step_ms / 1e6, 1),
+           "weight_bytes_per_step": wbytes,
+           "weights_gb_s": round(wbytes / step_ms / 1e6, 1),
            "launches_per_step": int(batch.launches_per_step()),
-           "workload": "8B, %d sequences x (512-token prompt + %d greedy tokens), positions 512..%d"
-                       % (nseq, DECODE, PROMPT + DECODE - 1)}
+           "workload": "%s, %d sequences x (%d-token prompt + %d greedy tokens), positions %d..%d"
+                       % (name, nseq, prompt, decode, prompt, prompt + decode - 1)}
     batch.close()
-    plan.close()
-    model.close()
-    provider.close()
+    if own:
+        plan.close()
+        model.close()
+        provider.close()
     return out
 
 
@@ -320,6 +333,7 @@ def run_provider(args):
     with_cpu = not args.no_cpu_baseline
     mv_c2 = matvec_c2(cpu=with_cpu) if rank == 0 and world == 1 else None
     mv_c1 = matvec_c1(cpu=with_cpu) if rank == 0 and world == 1 else None
+    batch16 = batch_decode(16, steps=2, plan=plan, model=model) if rank == 0 and world == 1 else None
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -353,6 +367,7 @@ def run_provider(args):
         "attention_c4": attn_c4,
         "matvec_c2": mv_c2,
         "matvec_c1": mv_c1,
+        "batch_decode": batch16,
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
@@ -393,7 +408,7 @@ def run_provider_70b(args):
     launch's ranks (one process per GPU; 1 = a single GPU). All ranks map one
     copy of the model in /dev/shm (the first creates it), as processes on a
     host map one GGUF file. Prompt 512 then 256 greedy tokens per step, batch
-    1 (batched decode is not built)."""
+    1 (batches of up to 16 sequences on one GPU: --batch 16 --model 70b)."""
     import torch
     import fyodor_b200 as F
     from tests.patterns import bench_tokens
@@ -876,6 +891,8 @@ def main():
     ap.add_argument("--allreduce-probe", action="store_true",
                     help="under torchrun: time the reference design's NCCL all-reduce of the residual")
     ap.add_argument("--batch", type=int, default=0, help="time batched decode of this many sequences (1..16)")
+    ap.add_argument("--batch-prompt", type=int, default=PROMPT, help="with --batch: prompt tokens per sequence")
+    ap.add_argument("--batch-decode", type=int, default=DECODE, help="with --batch: greedy tokens per timed step")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--model", default="8b", choices=["8b", "70b"], help="70b: the tensor-parallel 70B configuration")
     ap.add_argument("--steps", type=int, default=5)
@@ -891,7 +908,9 @@ def main():
         print(json.dumps({"matvec_c1": matvec_c1(cpu=not args.no_cpu_baseline),
                           "matvec_c2": matvec_c2(cpu=not args.no_cpu_baseline)}))
     elif args.batch:
-        print(json.dumps({"batch_decode": batch_decode(args.batch)}))
+        print(json.dumps({"batch_decode": batch_decode(args.batch, steps=args.steps, warmup=min(args.warmup, 1),
+                                                       model_name=args.model, prompt=args.batch_prompt,
+                                                       decode=args.batch_decode)}))
     elif args.allreduce_probe:
         run_allreduce_probe(args)
     elif args.gemm_case:
