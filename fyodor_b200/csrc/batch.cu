@@ -20,37 +20,46 @@ namespace fyb {
 
 // x[b] += delta[b] (when delta is given, written back), then
 // xn[b] = x[b] * (1 / sqrt(mean(x^2) + eps)) * w with the sum of squares in
-// double (llm_cpu.c:83-103). One CTA per sequence.
-__global__ void __launch_bounds__(256) bt_add_norm_kernel(float *x, const float *delta, const float *w, float *xn,
-    unsigned d, float eps)
+// double (llm_cpu.c:83-103). One CTA of 1024 threads per sequence, four
+// consecutive values per thread and pass (d a multiple of 4).
+constexpr unsigned BT_NORM_THREADS = 1024;
+__global__ void __launch_bounds__(BT_NORM_THREADS) bt_add_norm_kernel(float *x, const float *delta, const float *w,
+    float *xn, unsigned d, float eps)
 {
     const unsigned b = blockIdx.x;
-    float *xr = x + (size_t)b * d;
-    const float *dr = delta ? delta + (size_t)b * d : nullptr;
-    __shared__ double part[8];
+    float4 *xr = reinterpret_cast<float4 *>(x + (size_t)b * d);
+    const float4 *dr = delta ? reinterpret_cast<const float4 *>(delta + (size_t)b * d) : nullptr;
+    __shared__ double part[BT_NORM_THREADS / 32];
     __shared__ float scale_s;
     double ss = 0.0;
-    for (unsigned i = threadIdx.x; i < d; i += blockDim.x) {
-        float v = xr[i];
+    for (unsigned i = threadIdx.x; i < d / 4; i += BT_NORM_THREADS) {
+        float4 v = xr[i];
         if (dr) {
-            v = __fadd_rn(v, dr[i]);
+            const float4 e = dr[i];
+            v.x = __fadd_rn(v.x, e.x); v.y = __fadd_rn(v.y, e.y); v.z = __fadd_rn(v.z, e.z); v.w = __fadd_rn(v.w, e.w);
             xr[i] = v;
         }
-        ss += (double)v * (double)v;
+        ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        double t = 0.0;
-        for (unsigned k = 0; k < blockDim.x / 32; ++k) t += part[k];
-        scale_s = (float)(1.0 / sqrt(t / (double)d + (double)eps));
+    if (threadIdx.x < 32) {
+        double t = part[threadIdx.x];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (threadIdx.x == 0) scale_s = (float)(1.0 / sqrt(t / (double)d + (double)eps));
     }
     __syncthreads();
     const float scale = scale_s;
-    for (unsigned i = threadIdx.x; i < d; i += blockDim.x)
-        xn[(size_t)b * d + i] = __fmul_rn(__fmul_rn(xr[i], scale), w ? w[i] : 1.0f);
+    float4 *out = reinterpret_cast<float4 *>(xn + (size_t)b * d);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    for (unsigned i = threadIdx.x; i < d / 4; i += BT_NORM_THREADS) {
+        const float4 v = xr[i], g = w ? w4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+        out[i] = make_float4(__fmul_rn(__fmul_rn(v.x, scale), g.x), __fmul_rn(__fmul_rn(v.y, scale), g.y),
+                             __fmul_rn(__fmul_rn(v.z, scale), g.z), __fmul_rn(__fmul_rn(v.w, scale), g.w));
+    }
 }
 
 // RoPE and KV append from the fused QKV rows y[b][qkv_rows]: thread (b, t, j)
@@ -159,7 +168,8 @@ __global__ void bt_set_kernel(BatchRequest r, unsigned *req, unsigned nseq)
 int launch_bt_add_norm(float *x, const float *delta, const float *w, float *xn, unsigned d, float eps, unsigned nseq,
     cudaStream_t s)
 {
-    bt_add_norm_kernel<<<nseq, 256, 0, s>>>(x, delta, w, xn, d, eps);
+    if (d % 4) return -1;
+    bt_add_norm_kernel<<<nseq, BT_NORM_THREADS, 0, s>>>(x, delta, w, xn, d, eps);
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

@@ -1322,16 +1322,19 @@ extern "C" int fyb_batch_decode_greedy(void *batch, const uint32_t *tokens, cons
 }
 
 // Milliseconds per greedy step of `steps` graph replays (CUDA events on the
-// plan's stream, after one untimed step that captures the graph); < 0 on error.
+// plan's stream), after two untimed steps from the same tokens and positions
+// (the first sizes the scratch, the second captures the graph); < 0 on error.
 extern "C" double fyb_batch_time_greedy(void *batch, const uint32_t *tokens, const uint32_t *positions, size_t steps)
 {
     Batch *bt = (Batch *)batch;
     if (!bt || !tokens || !positions || steps == 0) return -1.0;
     DeviceScope scope(bt->p->ctx->device);
     cudaStream_t s = bt->p->ctx->stream;
-    if (grow((void **)&bt->log, &bt->log_bytes, (steps + 2) * bt->B * 4, true)) return -1.0;
-    if (batch_set(bt, tokens, positions, steps + 2)) return -1.0;
+    if (grow((void **)&bt->log, &bt->log_bytes, steps * bt->B * 4, true)) return -1.0;
+    if (batch_set(bt, tokens, positions, steps)) return -1.0;
     for (int w = 0; w < 2; ++w) if (batch_run(bt, true)) return -1.0;  // sizes, then captures
+    // the timed steps start again from the given tokens and positions
+    if (batch_set(bt, tokens, positions, steps)) return -1.0;
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0); cudaEventCreate(&e1);
     cudaEventRecord(e0, s);

@@ -204,7 +204,8 @@ double fyb_plan_time_projection(void *plan, unsigned layer, unsigned which, unsi
    fyb_batch_decode_greedy: `steps` greedy steps on the device from
    tokens / positions (each position + steps <= capacity); out [steps][B].
    fyb_batch_time_greedy: milliseconds per greedy step over `steps` graph
-   replays (CUDA events), after two untimed steps; < 0 on error.
+   replays (CUDA events) from tokens / positions (each position + steps <=
+   capacity), after two untimed steps from the same start; < 0 on error.
    fyb_batch_launches_per_step: kernels in the last step enqueued. */
 void *fyb_batch_create(void *plan, unsigned batch);
 void fyb_batch_free(void *batch);
