@@ -66,10 +66,12 @@ __global__ void __launch_bounds__(BT_NORM_THREADS) bt_add_norm_kernel(float *x, 
 // owns rows j and j + 8 of tile t, the pair (2i, 2i + 1) of one head
 // (llm_cpu.c:298-327; q and K rotated, V copied). q goes to q[b][H * hd] in
 // natural order; K and V are rounded to fp16 into sequence b's cache row
-// positions[b] (per layer: [seq][kv head][capacity][hd]).
+// positions[b] (per layer: [seq][kv head][capacity][hd]). Row b writes the
+// cache of sequence b / slot_div: slot_div 1 for a batch of sequences, the
+// row count when the rows are consecutive positions of one sequence.
 __global__ void bt_rope_kv_kernel(const float *y, unsigned qkv_rows, unsigned H, unsigned Hkv, unsigned hd,
     const unsigned *positions, const float *rope_cos, const float *rope_sin, float *q, __half *kc, __half *vc,
-    unsigned capacity, unsigned nseq)
+    unsigned capacity, unsigned nseq, unsigned slot_div)
 {
     const unsigned tiles = qkv_rows / 16, tq = H * hd / 16, tk = Hkv * hd / 16;
     const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -94,7 +96,7 @@ __global__ void bt_rope_kv_kernel(const float *y, unsigned qkv_rows, unsigned H,
         return;
     }
     const unsigned kvh = rowA / hd, dd = rowA % hd;
-    __half *dst = (seg == 1 ? kc : vc) + (((size_t)b * Hkv + kvh) * capacity + pos) * hd + dd;
+    __half *dst = (seg == 1 ? kc : vc) + (((size_t)(b / slot_div) * Hkv + kvh) * capacity + pos) * hd + dd;
     *reinterpret_cast<__half2 *>(dst) = __halves2half2(__float2half_rn(a), __float2half_rn(c2));
 }
 
@@ -175,12 +177,12 @@ int launch_bt_add_norm(float *x, const float *delta, const float *w, float *xn, 
 
 int launch_bt_rope_kv(const float *y, unsigned qkv_rows, unsigned H, unsigned Hkv, unsigned hd,
     const unsigned *positions, const float *rope_cos, const float *rope_sin, float *q, __half *kc, __half *vc,
-    unsigned capacity, unsigned nseq, cudaStream_t s)
+    unsigned capacity, unsigned nseq, unsigned slot_div, cudaStream_t s)
 {
-    if (qkv_rows % 16 || hd % 16) return -1;
+    if (qkv_rows % 16 || hd % 16 || slot_div == 0) return -1;
     const unsigned n = nseq * (qkv_rows / 16) * 8;
     bt_rope_kv_kernel<<<(n + 255) / 256, 256, 0, s>>>(y, qkv_rows, H, Hkv, hd, positions, rope_cos, rope_sin, q, kc,
-                                                        vc, capacity, nseq);
+                                                        vc, capacity, nseq, slot_div);
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

@@ -217,7 +217,7 @@ int launch_bt_add_norm(float *x, const float *delta, const float *w, float *xn, 
     cudaStream_t s);
 int launch_bt_rope_kv(const float *y, unsigned qkv_rows, unsigned H, unsigned Hkv, unsigned hd,
     const unsigned *positions, const float *rope_cos, const float *rope_sin, float *q, __half *kc, __half *vc,
-    unsigned capacity, unsigned nseq, cudaStream_t s);
+    unsigned capacity, unsigned nseq, unsigned slot_div, cudaStream_t s);
 int launch_bt_swiglu(const float *y, unsigned ffn, float *h, unsigned nseq, cudaStream_t s);
 int launch_bt_argmax(const float *logits, unsigned V, unsigned *req, unsigned nseq, unsigned *tokens_out, unsigned *log,
     bool advance, unsigned *error, cudaStream_t s);

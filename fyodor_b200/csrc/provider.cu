@@ -28,6 +28,13 @@
 #include <string>
 #include <vector>
 
+// the batched step (defined after the plan): also the plan's prompt chunker
+namespace fyb { struct Plan; }
+struct Batch;
+static void batch_free(Batch *bt);
+static Batch *batch_create(fyb::Plan *p, unsigned batch, bool chunk);
+static int prefill_chunks(fyb::Plan *p, Batch *bt, const uint32_t *tokens, size_t count, size_t position, float *out);
+
 namespace fyb {
 
 static bool debug_enabled() { return std::getenv("NYA_CUDA_DEBUG") != nullptr; }
@@ -368,6 +375,10 @@ struct Plan {
     unsigned char **peers_dev = nullptr;  // [tp_size] device pointers to every rank's region
     std::vector<unsigned char *> peers;   // host copy; peers opened through IPC are closed on free
     bool connected = false;
+    // chunked prefill: prompt chunks of up to BATCH_MAX tokens through the
+    // batched step, writing this plan's own KV cache (created on first use)
+    ::Batch *prefill = nullptr;
+    bool prefill_tried = false;
 };
 
 static void *plan_alloc(Plan *p, size_t bytes)
@@ -388,6 +399,7 @@ static void plan_free(void *opaque)
 {
     Plan *p = (Plan *)opaque;
     if (!p) return;
+    if (p->prefill) ::batch_free(p->prefill);
     {
         DeviceScope scope(p->ctx->device);
         cudaStreamSynchronize(p->ctx->stream);
@@ -1005,6 +1017,22 @@ static int plan_token(void *opaque, uint32_t token, size_t position, int logits,
     return 0;
 }
 
+// Prefill in chunks of up to BATCH_MAX prompt tokens: every weight read
+// once per chunk, causal attention inside the chunk. 1 when the plan has no
+// chunker (tensor-parallel shards, NYA_CUDA_CHUNKED_PREFILL=0, a geometry the
+// batched step does not take): the caller steps token by token.
+static int prefill_chunked(Plan *p, const uint32_t *tokens, size_t count, size_t position, float *out)
+{
+    if (!p->prefill && !p->prefill_tried) {
+        p->prefill_tried = true;
+        const char *env = std::getenv("NYA_CUDA_CHUNKED_PREFILL");
+        if (!(env && !std::strcmp(env, "0")) && p->tp_size == 1) p->prefill = ::batch_create(p, BATCH_MAX, true);
+        if (p->prefill) p->stats.prefill_batch = BATCH_MAX;
+    }
+    if (!p->prefill) return 1;
+    return ::prefill_chunks(p, p->prefill, tokens, count, position, out);
+}
+
 static int plan_prefill(void *opaque, const uint32_t *tokens, size_t count, size_t position, float *out)
 {
     Plan *p = (Plan *)opaque;
@@ -1014,6 +1042,14 @@ static int plan_prefill(void *opaque, const uint32_t *tokens, size_t count, size
     if (position + count > p->fail_after) { p->failed = true; return -1; }
     DeviceScope scope(p->ctx->device);
     if (!scope.ok) return plan_fail(p, position);
+    if (count > 1) {  // prompt chunks through the batched step (resident.inc:585-595 chunks prefill too)
+        const int r = prefill_chunked(p, tokens, count, position, out);
+        if (r == 0) {
+            p->valid = position + count;
+            return 0;
+        }
+        if (r != 1) return plan_fail(p, position);
+    }  // r == 1: no chunker for this plan; one decode step per token
     for (size_t i = 0; i < count; ++i) {
         const bool last = i + 1 == count;
         if (set_request(p, tokens[i], (unsigned)(position + i)) || run_step(p, last ? STEP_LOGITS : STEP_NO_LOGITS))
@@ -1106,9 +1142,12 @@ extern "C" const nya_backend_interface *nya_cuda_backend(void)
 struct Batch {
     Plan *p = nullptr;
     unsigned B = 0;
+    unsigned rows = 0;    // rows of the step being enqueued (B for a batch of sequences)
+    unsigned ws_rows = 0; // query rows the attention workspace's counters were last laid out for
+    bool chunk = false;   // rows are consecutive positions of one sequence in the plan's own cache
     size_t capacity = 0;
     std::vector<void *> allocations;
-    __half *kc = nullptr, *vc = nullptr;  // [layer][seq][kv head][capacity][hd]
+    __half *kc = nullptr, *vc = nullptr;  // [layer][seq][kv head][capacity][hd] (chunk: the plan's cache)
     float *x = nullptr, *xn = nullptr, *delta = nullptr, *y = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
     float *logits = nullptr;             // [B][V]
     unsigned *req = nullptr;             // [B] tokens | [B] positions | [B] lengths | step
@@ -1136,7 +1175,7 @@ static void batch_free(Batch *bt)
     cudaStreamSynchronize(bt->p->ctx->stream);
     for (auto &g : bt->graphs) if (g) cudaGraphExecDestroy(g);
     for (void *a : bt->allocations) cudaFree(a);  // the attention workspace among them
-    for (void *a : {(void *)bt->log, (void *)bt->counters, (void *)bt->partials, bt->gemm})  // grown buffers
+    for (void *a : {(void *)bt->log, (void *)bt->counters, (void *)bt->partials, (void *)bt->gemm})  // grown buffers
         if (a) cudaFree(a);
     cudaGetLastError();
     delete bt;
@@ -1146,13 +1185,20 @@ static AttentionLaunch batch_attention(const Batch *bt, unsigned l)
 {
     const Plan *p = bt->p;
     const size_t per_seq = (size_t)p->Hkv * bt->capacity * p->hd;
+    const unsigned slots = bt->chunk ? 1u : bt->B;
     AttentionLaunch A;
     A.q = bt->q;
-    A.k = bt->kc + (size_t)l * bt->B * per_seq;
-    A.v = bt->vc + (size_t)l * bt->B * per_seq;
+    A.k = bt->kc + (size_t)l * slots * per_seq;
+    A.v = bt->vc + (size_t)l * slots * per_seq;
     A.seq_stride = per_seq;
-    A.lengths = bt->req + 2 * bt->B;
-    A.nseq = bt->B; A.heads = p->H; A.kv_heads = p->Hkv; A.head_dim = p->hd;
+    if (bt->chunk) {  // one sequence, the chunk's rows as causal queries; length of the last row
+        A.nseq = 1; A.queries = std::max(1u, bt->rows);
+        A.lengths = bt->req + 2 * bt->B + A.queries - 1;
+    } else {
+        A.nseq = bt->B;
+        A.lengths = bt->req + 2 * bt->B;
+    }
+    A.heads = p->H; A.kv_heads = p->Hkv; A.head_dim = p->hd;
     A.capacity = (unsigned)bt->capacity;
     A.scale = 1.0f / std::sqrt((float)p->hd);
     A.out = bt->attn;
@@ -1163,34 +1209,40 @@ static AttentionLaunch batch_attention(const Batch *bt, unsigned l)
 
 // One batched step reading tokens and positions from bt->req; greedy steps
 // advance every sequence to its argmax token at the next position.
-static int batch_enqueue(Batch *bt, bool greedy)
+static int batch_enqueue(Batch *bt, bool greedy, bool logits = true)
 {
     Plan *p = bt->p;
     cudaStream_t s = p->ctx->stream;
     const int sms = p->ctx->sms;
-    const unsigned B = bt->B;
+    const unsigned B = bt->B, R = bt->chunk ? bt->rows : B, slots = bt->chunk ? 1u : B;
     const Scratch sc{&bt->counters, &bt->counters_bytes, &bt->partials, &bt->partials_bytes, &bt->gemm,
                      &bt->gemm_bytes};
     const size_t per_seq = (size_t)p->Hkv * bt->capacity * p->hd;
     bt->launches = 0;
 #define BRUN(expr) do { const int r_ = (expr); ++bt->launches; if (r_) return r_; } while (0)
-    BRUN(launch_gather_batch(p->embd, p->embd_row_bytes, p->embd_type, p->d, bt->req, B, bt->x, s));
+    BRUN(launch_gather_batch(p->embd, p->embd_row_bytes, p->embd_type, p->d, bt->req, R, bt->x, s));
     for (unsigned l = 0; l < p->nl; ++l) {
         const LayerW &L = p->layers[l];
         const size_t qkv_rows = (size_t)L.qkv.tiles * 16, gu_rows = (size_t)L.gateup.tiles * 16;
-        BRUN(launch_bt_add_norm(bt->x, l ? bt->delta : nullptr, L.attn_norm, bt->xn, p->d, p->eps, B, s));
-        BRUN(device_matmul(&L.qkv, nullptr, 0, qkv_rows, p->d, L.qkv.type, bt->xn, bt->y, B, sc, s, sms));
+        BRUN(launch_bt_add_norm(bt->x, l ? bt->delta : nullptr, L.attn_norm, bt->xn, p->d, p->eps, R, s));
+        BRUN(device_matmul(&L.qkv, nullptr, 0, qkv_rows, p->d, L.qkv.type, bt->xn, bt->y, R, sc, s, sms));
         BRUN(launch_bt_rope_kv(bt->y, (unsigned)qkv_rows, p->H, p->Hkv, p->hd, bt->req + B, p->rope_cos, p->rope_sin,
-                               bt->q, bt->kc + (size_t)l * B * per_seq, bt->vc + (size_t)l * B * per_seq,
-                               (unsigned)bt->capacity, B, s));
+                               bt->q, bt->kc + (size_t)l * slots * per_seq, bt->vc + (size_t)l * slots * per_seq,
+                               (unsigned)bt->capacity, R, bt->chunk ? R : 1u, s));
         BRUN(launch_attention(batch_attention(bt, l), s));
-        BRUN(device_matmul(&L.o, nullptr, 0, p->d, (size_t)p->H * p->hd, L.o.type, bt->attn, bt->delta, B, sc, s, sms));
-        BRUN(launch_bt_add_norm(bt->x, bt->delta, L.ffn_norm, bt->xn, p->d, p->eps, B, s));
-        BRUN(device_matmul(&L.gateup, nullptr, 0, gu_rows, p->d, L.gateup.type, bt->xn, bt->y, B, sc, s, sms));
-        BRUN(launch_bt_swiglu(bt->y, p->ffn, bt->h, B, s));
-        BRUN(device_matmul(&L.down, nullptr, 0, p->d, p->ffn, L.down.type, bt->h, bt->delta, B, sc, s, sms));
+        BRUN(device_matmul(&L.o, nullptr, 0, p->d, (size_t)p->H * p->hd, L.o.type, bt->attn, bt->delta, R, sc, s, sms));
+        BRUN(launch_bt_add_norm(bt->x, bt->delta, L.ffn_norm, bt->xn, p->d, p->eps, R, s));
+        BRUN(device_matmul(&L.gateup, nullptr, 0, gu_rows, p->d, L.gateup.type, bt->xn, bt->y, R, sc, s, sms));
+        BRUN(launch_bt_swiglu(bt->y, p->ffn, bt->h, R, s));
+        BRUN(device_matmul(&L.down, nullptr, 0, p->d, p->ffn, L.down.type, bt->h, bt->delta, R, sc, s, sms));
     }
-    BRUN(launch_bt_add_norm(bt->x, bt->delta, p->out_norm, bt->xn, p->d, p->eps, B, s));
+    if (!logits) return 0;  // a prompt chunk before the last: only the KV cache matters
+    BRUN(launch_bt_add_norm(bt->x, bt->delta, p->out_norm, bt->xn, p->d, p->eps, R, s));
+    if (bt->chunk) {  // the logits of the chunk's last token only
+        BRUN(device_matmul(&p->out_head, nullptr, 0, p->V, p->d, p->out_head.type, bt->xn + (size_t)(R - 1) * p->d,
+                           bt->logits, 1, sc, s, sms));
+        return 0;
+    }
     BRUN(device_matmul(&p->out_head, nullptr, 0, p->V, p->d, p->out_head.type, bt->xn, bt->logits, B, sc, s, sms));
     BRUN(launch_bt_argmax(bt->logits, p->V, bt->req, B, bt->tokens, bt->log, greedy, p->err_dev, s));
 #undef BRUN
@@ -1234,17 +1286,22 @@ static int batch_set(Batch *bt, const uint32_t *tokens, const uint32_t *position
     return launch_bt_set(r, bt->req, bt->B, bt->p->ctx->stream);
 }
 
-extern "C" void *fyb_batch_create(void *plan, unsigned batch)
+// A batch of `batch` sequences with their own caches, or (chunk) a prompt
+// chunker of up to `batch` consecutive positions of the plan's own sequence.
+static Batch *batch_create(Plan *p, unsigned batch, bool chunk)
 {
-    Plan *p = (Plan *)plan;
-    if (!p || p->failed || batch < 1 || batch > BATCH_MAX || p->tp_size != 1 || p->hd % 16 || p->ffn % 8) return nullptr;
+    if (!p || p->failed || batch < 1 || batch > BATCH_MAX || p->tp_size != 1 || p->hd % 16 || p->ffn % 8 ||
+        p->d % 4)
+        return nullptr;
     DeviceScope scope(p->ctx->device);
     if (!scope.ok) return nullptr;
     Batch *bt = new Batch;
     bt->p = p;
     bt->B = batch;
+    bt->rows = batch;
+    bt->chunk = chunk;
     bt->capacity = p->capacity;
-    const size_t kv = (size_t)p->nl * batch * p->Hkv * bt->capacity * p->hd;
+    const size_t kv = chunk ? 0 : (size_t)p->nl * batch * p->Hkv * bt->capacity * p->hd;
     const size_t qkv_rows = (size_t)p->layers[0].qkv.tiles * 16;
     const size_t ywidth = std::max<size_t>(qkv_rows, (size_t)p->layers[0].gateup.tiles * 16);
     bool ok = true;
@@ -1254,22 +1311,27 @@ extern "C" void *fyb_batch_create(void *plan, unsigned batch)
         bt->allocations.push_back(d);
         return d;
     };
-    bt->kc = (__half *)A(kv * 2); bt->vc = (__half *)A(kv * 2);
+    if (chunk) {
+        bt->kc = p->kcache; bt->vc = p->vcache;
+    } else {
+        bt->kc = (__half *)A(kv * 2); bt->vc = (__half *)A(kv * 2);
+    }
     bt->x = (float *)A((size_t)batch * p->d * 4); bt->xn = (float *)A((size_t)batch * p->d * 4);
     bt->delta = (float *)A((size_t)batch * p->d * 4);
     bt->y = (float *)A((size_t)batch * ywidth * 4);
     bt->q = (float *)A((size_t)batch * p->H * p->hd * 4); bt->attn = (float *)A((size_t)batch * p->H * p->hd * 4);
     bt->h = (float *)A((size_t)batch * p->ffn * 4);
-    bt->logits = (float *)A((size_t)batch * p->V * 4);
+    bt->logits = (float *)A((size_t)(chunk ? 1 : batch) * p->V * 4);
     bt->req = (unsigned *)A((3 * BATCH_MAX + 1) * 4); bt->tokens = (unsigned *)A(BATCH_MAX * 4);
     // partitions of each (sequence, KV head): about two waves of the SMs at the longest context
-    bt->splits = (unsigned)std::max<size_t>(1, std::min<size_t>(16, (size_t)2 * p->ctx->sms / (batch * p->Hkv)));
+    const size_t seqs = chunk ? 1 : batch;
+    bt->splits = (unsigned)std::max<size_t>(1, std::min<size_t>(16, (size_t)2 * p->ctx->sms / (seqs * p->Hkv)));
     if (ok) {
         AttentionLaunch L = batch_attention(bt, 0);
         bt->attn_ws_bytes = attention_workspace_bytes(L);
         bt->attn_ws = A(bt->attn_ws_bytes);
     }
-    if (ok) ok = cudaMemset(bt->kc, 0, kv * 2) == cudaSuccess && cudaMemset(bt->vc, 0, kv * 2) == cudaSuccess &&
+    if (ok) ok = (chunk || (cudaMemset(bt->kc, 0, kv * 2) == cudaSuccess && cudaMemset(bt->vc, 0, kv * 2) == cudaSuccess)) &&
                  cudaMemset(bt->attn_ws, 0, bt->attn_ws_bytes) == cudaSuccess &&
                  cudaMemset(bt->req, 0, (3 * BATCH_MAX + 1) * 4) == cudaSuccess &&
                  grow((void **)&bt->log, &bt->log_bytes, (size_t)BATCH_MAX * 4, true) == 0 &&
@@ -1279,6 +1341,39 @@ extern "C" void *fyb_batch_create(void *plan, unsigned batch)
         return nullptr;
     }
     return bt;
+}
+
+extern "C" void *fyb_batch_create(void *plan, unsigned batch) { return batch_create((Plan *)plan, batch, false); }
+
+static int prefill_chunks(Plan *p, Batch *bt, const uint32_t *tokens, size_t count, size_t position, float *out)
+{
+    cudaStream_t s = p->ctx->stream;
+    for (size_t c0 = 0; c0 < count; c0 += bt->B) {
+        const unsigned R = (unsigned)std::min<size_t>(bt->B, count - c0);
+        BatchRequest r = {};
+        for (unsigned i = 0; i < R; ++i) {
+            r.token[i] = tokens[c0 + i];
+            r.position[i] = (unsigned)(position + c0 + i);
+        }
+        bt->rows = R;
+        // the attention workspace keeps its counters after the partials, at an
+        // offset set by the query rows: a chunk of another size starts from zero
+        if (R != bt->ws_rows && cudaMemsetAsync(bt->attn_ws, 0, bt->attn_ws_bytes, s) != cudaSuccess) return -2;
+        bt->ws_rows = R;
+        if (launch_bt_set(r, bt->req, bt->B, s)) return -2;
+        const int e = batch_enqueue(bt, false, c0 + R == count);
+        p->stats.kernel_launches += bt->launches + 1;
+        if (e) return -2;
+    }
+    ++p->stats.downloads;
+    ++p->stats.synchronizations;
+    if (cudaMemcpyAsync(out, bt->logits, (size_t)p->V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess || *(volatile unsigned *)p->err_host)
+        return -2;
+    for (size_t i = 0; i < p->V; ++i) if (!std::isfinite(out[i])) return -2;
+    const nya_llm_tokenizer &tk = p->m->tokenizer;
+    for (size_t i = 0; i < tk.suppressed_count; ++i) out[tk.suppressed_tokens[i]] = -INFINITY;
+    return 0;
 }
 
 extern "C" void fyb_batch_free(void *batch) { batch_free((Batch *)batch); }

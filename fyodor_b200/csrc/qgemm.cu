@@ -284,7 +284,7 @@ constexpr size_t QM_COUNTER_BYTES = 4096;  // up to 1024 tile groups
 
 // ===========================================================================
 // The same product on the 5th-generation tensor cores (tcgen05), for
-// TC_MIN_NV..16 vectors. A first small kernel (tc_limbs_kernel) splits the
+// tc_min_nv(type)..16 vectors. A first small kernel (tc_limbs_kernel) splits the
 // vectors once into the B operand of every 256-column block: four signed
 // 7-bit limbs per value (the split of the mma.sync path), stored as
 // canonical K-major core matrices, followed by the block's x constants
@@ -329,7 +329,9 @@ constexpr size_t QM_COUNTER_BYTES = 4096;  // up to 1024 tile groups
 constexpr unsigned TC_THREADS = 576;              // 18 warps
 constexpr unsigned TC_STAGE0 = 2, TC_NSTAGE = 8;  // staging warps 2..9
 constexpr unsigned TC_EPI0 = 10, TC_NEPI = 8;     // epilogue warps 10..17
-constexpr unsigned TC_MIN_NV = 9;  // below it the mma.sync kernel is faster (measured)
+// Fewest vectors that run on tcgen05; below it the mma.sync kernel is
+// faster (measured: Q4_K up to 8 vectors, Q6_K up to 4).
+FYB_HOST_DEV unsigned tc_min_nv(unsigned type) { return type == T_Q6_K ? 5u : 9u; }
 #ifndef FYB_TC_SLEEP_NS
 #define FYB_TC_SLEEP_NS 64
 #endif
@@ -941,7 +943,7 @@ size_t qgemm_workspace_bytes(unsigned type, size_t rows, size_t cols, size_t nv,
     if (nv < 3 || nv > 2 * QM_MAX_PAIRS || cols % 256 || sms > 1024) return 0;
     size_t sb, cn, tb = 0, bb = 0;
     qm_plan(type, (unsigned)rows, (unsigned)cols, (unsigned)nv, sms, &sb, &cn);
-    if (nv >= TC_MIN_NV) {
+    if (nv >= tc_min_nv(type)) {
         tc_plan(type, (unsigned)rows, (unsigned)cols, (unsigned)nv, sms, &tb);
         bb = tc_bops_bytes(tc_n((unsigned)nv), (unsigned)(cols / 256));
     }
@@ -989,7 +991,7 @@ int launch_qgemm(const QWeights &w, unsigned rows, const float *x, float *y, siz
         return -1;
     if (workspace_bytes < qgemm_workspace_bytes(w.type, rows, w.cols, nv, sms)) return -1;
     unsigned char *ws = reinterpret_cast<unsigned char *>(workspace);
-    if (nv >= TC_MIN_NV) {
+    if (nv >= tc_min_nv(w.type)) {
         size_t tb;
         TcParams p = tc_plan(w.type, rows, w.cols, nv, sms, &tb);
         if (p.G) {

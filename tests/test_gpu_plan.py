@@ -78,17 +78,54 @@ def test_greedy_64_steps(provider, name, cfg, tokens):
 
 
 def test_prefill_then_decode_matches_tokens(provider):
+    """plan_prefill (one chunk of 8 prompt tokens through the batched step)
+    against plan_token steps and the fp16-KV oracle: the two GPU paths sum in
+    different orders, so they meet on the oracle's bound, not bitwise."""
     name, cfg, tokens = SMALL_MODELS[0]
     m = F.SynthModel(**cfg)
     a = provider.plan(m, 32)
     b = provider.plan(m, 32)
+    ref16 = O.Session(m.ptr, 32, m.vocabulary, kv_f16=True)
     assert a.prefill(np.array(tokens[:8], np.uint32), 0) == 0
     la = a.logits.copy()
+    assert a.stats()["prefill_batch"] == 16  # the chunked path ran
     for i, t in enumerate(tokens[:8]):
         assert b.token(t, i, logits=(i == 7)) == 0
-    assert scaled_error(la, b.logits) <= 1e-6
+        e = ref16.forward(t, i)
+    assert logit_error(la, e) <= 1e-3 and logit_error(b.logits, e) <= 1e-3
+    assert np.argmax(la) == np.argmax(b.logits) == np.argmax(e)
     assert a.token(tokens[8], 8) == 0 and b.token(tokens[8], 8) == 0
-    assert scaled_error(a.logits, b.logits) <= 1e-6
+    e = ref16.forward(tokens[8], 8)
+    assert logit_error(a.logits, e) <= 1e-3 and logit_error(b.logits, e) <= 1e-3
+
+
+@pytest.mark.parametrize("name,cfg,tokens", SMALL_MODELS)
+def test_chunked_prefill(provider, name, cfg, tokens):
+    """Prompts of 37 tokens (chunks of 16, 16 and 5) at positions 0 and then
+    3 (a second prefill after the first three tokens rewrites the rest):
+    logits of the last token and every cached K/V row against the fp16-KV
+    oracle."""
+    m = F.SynthModel(**cfg)
+    prompt = bench_tokens(37, m.vocabulary, 5)
+    plan = provider.plan(m, 48)
+    ref16 = O.Session(m.ptr, 48, m.vocabulary, kv_f16=True)
+    assert plan.prefill(prompt, 0) == 0
+    for i, t in enumerate(prompt):
+        e = ref16.forward(int(t), i, logits=i == len(prompt) - 1)
+    assert logit_error(plan.logits, e) <= 1e-3, logit_error(plan.logits, e)
+    assert np.argmax(plan.logits) == np.argmax(e)
+    kv = plan.read_kv(cfg["layers"] - 1, 0, len(prompt))
+    k16, v16 = ref16.read_kv(cfg["layers"] - 1, 0, len(prompt), m.kv_dim)
+    assert logit_error(kv[0], k16) <= 2e-3 and logit_error(kv[1], v16) <= 2e-3
+    second = bench_tokens(30, m.vocabulary, 11)
+    assert plan.prefill(second, 3) == 0
+    for i, t in enumerate(second):
+        e = ref16.forward(int(t), 3 + i, logits=i == len(second) - 1)
+    assert logit_error(plan.logits, e) <= 1e-3, logit_error(plan.logits, e)
+    assert np.argmax(plan.logits) == np.argmax(e)
+    t = int(np.argmax(e))
+    assert plan.token(t, 33) == 0
+    assert logit_error(plan.logits, ref16.forward(t, 33)) <= 1e-3
 
 
 def test_plan_argument_validation(provider):
