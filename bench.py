@@ -344,6 +344,18 @@ def run_provider(args):
     mv_c2 = matvec_c2(cpu=with_cpu) if rank == 0 and world == 1 else None
     mv_c1 = matvec_c1(cpu=with_cpu) if rank == 0 and world == 1 else None
     batch16 = batch_decode(16, steps=2, plan=plan, model=model) if rank == 0 and world == 1 else None
+    verify = None
+    if world == 1:  # speculative verification of an 8-token draft at position 512 (one pass, all logits to the host)
+        draft = bench_tokens(8, model.vocabulary, 77)
+        plan.verify(draft, PROMPT)
+        t0 = time.perf_counter()
+        for _ in range(5):
+            if plan.verify(draft, PROMPT) is None:
+                raise SystemExit("draft verification failed")
+        vs = (time.perf_counter() - t0) / 5
+        verify = {"draft_tokens": 8, "ms": round(vs * 1e3, 3), "tok_s": round(8 / vs, 1),
+                  "how": "fyb_plan_verify at positions 512..519 with [8][V] host logits, wall clock; "
+                         "one decode step per draft token would take 8 x %.3f ms" % (per_launch_ms,)}
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -378,6 +390,7 @@ def run_provider(args):
         "matvec_c2": mv_c2,
         "matvec_c1": mv_c1,
         "batch_decode": batch16,
+        "verify_draft": verify,
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,

@@ -114,6 +114,7 @@ def _load():
     lib.fyb_plan_trace.restype = C.c_long
     lib.fyb_plan_trace.argtypes = [_P, C.c_uint32, C.c_size_t, _P, C.c_size_t, _P, _P, C.c_size_t]
     lib.fyb_plan_decode_greedy.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t, _P]
+    lib.fyb_plan_verify.argtypes = [_P, _P, C.c_size_t, C.c_size_t, _P]
     lib.fyb_plan_time_greedy.restype = C.c_double
     lib.fyb_plan_time_greedy.argtypes = [_P, C.c_uint32, C.c_size_t, C.c_size_t]
     lib.fyb_plan_launches_per_token.restype = C.c_ulonglong
@@ -145,7 +146,7 @@ lib = _load()
 EXPORTS = ["nya_cuda_backend", "fyb_version", "fyb_device_count", "fyb_dequantize", "fyb_quant_matmul_workspace",
            "fyb_quant_matmul", "fyb_quant_repack", "fyb_quant_matmul_prepared", "fyb_attention_workspace",
            "fyb_attention_decode", "fyb_attention_verify",
-           "fyb_attention_decode_static", "fyb_plan_decode_greedy",
+           "fyb_attention_decode_static", "fyb_plan_decode_greedy", "fyb_plan_verify",
            "fyb_plan_time_greedy", "fyb_plan_launches_per_token", "fyb_plan_decode_form", "fyb_plan_profile", "fyb_plan_trace",
            "fyb_plan_tp_info", "fyb_plan_tp_handle", "fyb_plan_tp_connect", "fyb_plan_tp_disconnect",
            "fyb_plan_tp_connect_local", "fyb_plan_error", "fyb_plan_time_projection",
@@ -373,6 +374,13 @@ class Plan:
         v = np.empty((count, width), np.float32)
         r = self.api.plan_read_kv(self.ptr, layer, position, count, _ptr(k), _ptr(v), count * width)
         return (k, v) if r == 0 else None
+
+    def verify(self, tokens, position):
+        """Logits [k][V] of k draft tokens at positions position.. (one pass)."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        out = np.empty((len(t), self.model.vocabulary), np.float32)
+        r = lib.fyb_plan_verify(C.c_void_p(self.ptr), _ptr(t), len(t), position, _ptr(out))
+        return out if r == 0 else None
 
     def decode_greedy(self, token, position, steps):
         out = np.empty(steps, np.uint32)

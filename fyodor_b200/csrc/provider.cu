@@ -1021,7 +1021,7 @@ static int plan_token(void *opaque, uint32_t token, size_t position, int logits,
 // once per chunk, causal attention inside the chunk. 1 when the plan has no
 // chunker (tensor-parallel shards, NYA_CUDA_CHUNKED_PREFILL=0, a geometry the
 // batched step does not take): the caller steps token by token.
-static int prefill_chunked(Plan *p, const uint32_t *tokens, size_t count, size_t position, float *out)
+static ::Batch *plan_chunker(Plan *p)
 {
     if (!p->prefill && !p->prefill_tried) {
         p->prefill_tried = true;
@@ -1029,8 +1029,14 @@ static int prefill_chunked(Plan *p, const uint32_t *tokens, size_t count, size_t
         if (!(env && !std::strcmp(env, "0")) && p->tp_size == 1) p->prefill = ::batch_create(p, BATCH_MAX, true);
         if (p->prefill) p->stats.prefill_batch = BATCH_MAX;
     }
-    if (!p->prefill) return 1;
-    return ::prefill_chunks(p, p->prefill, tokens, count, position, out);
+    return p->prefill;
+}
+
+static int prefill_chunked(Plan *p, const uint32_t *tokens, size_t count, size_t position, float *out)
+{
+    ::Batch *bt = plan_chunker(p);
+    if (!bt) return 1;
+    return ::prefill_chunks(p, bt, tokens, count, position, out);
 }
 
 static int plan_prefill(void *opaque, const uint32_t *tokens, size_t count, size_t position, float *out)
@@ -1145,6 +1151,7 @@ struct Batch {
     unsigned rows = 0;    // rows of the step being enqueued (B for a batch of sequences)
     unsigned ws_rows = 0; // query rows the attention workspace's counters were last laid out for
     bool chunk = false;   // rows are consecutive positions of one sequence in the plan's own cache
+    bool all_logits = false;  // chunk: logits of every row (verification), not only the last
     size_t capacity = 0;
     std::vector<void *> allocations;
     __half *kc = nullptr, *vc = nullptr;  // [layer][seq][kv head][capacity][hd] (chunk: the plan's cache)
@@ -1238,9 +1245,10 @@ static int batch_enqueue(Batch *bt, bool greedy, bool logits = true)
     }
     if (!logits) return 0;  // a prompt chunk before the last: only the KV cache matters
     BRUN(launch_bt_add_norm(bt->x, bt->delta, p->out_norm, bt->xn, p->d, p->eps, R, s));
-    if (bt->chunk) {  // the logits of the chunk's last token only
-        BRUN(device_matmul(&p->out_head, nullptr, 0, p->V, p->d, p->out_head.type, bt->xn + (size_t)(R - 1) * p->d,
-                           bt->logits, 1, sc, s, sms));
+    if (bt->chunk) {  // the logits of the chunk's last token, or of every row when verifying a draft
+        const unsigned n = bt->all_logits ? R : 1u;
+        BRUN(device_matmul(&p->out_head, nullptr, 0, p->V, p->d, p->out_head.type, bt->xn + (size_t)(R - n) * p->d,
+                           bt->logits, n, sc, s, sms));
         return 0;
     }
     BRUN(device_matmul(&p->out_head, nullptr, 0, p->V, p->d, p->out_head.type, bt->xn, bt->logits, B, sc, s, sms));
@@ -1321,7 +1329,7 @@ static Batch *batch_create(Plan *p, unsigned batch, bool chunk)
     bt->y = (float *)A((size_t)batch * ywidth * 4);
     bt->q = (float *)A((size_t)batch * p->H * p->hd * 4); bt->attn = (float *)A((size_t)batch * p->H * p->hd * 4);
     bt->h = (float *)A((size_t)batch * p->ffn * 4);
-    bt->logits = (float *)A((size_t)(chunk ? 1 : batch) * p->V * 4);
+    bt->logits = (float *)A((size_t)batch * p->V * 4);
     bt->req = (unsigned *)A((3 * BATCH_MAX + 1) * 4); bt->tokens = (unsigned *)A(BATCH_MAX * 4);
     // partitions of each (sequence, KV head): about two waves of the SMs at the longest context
     const size_t seqs = chunk ? 1 : batch;
@@ -1345,9 +1353,12 @@ static Batch *batch_create(Plan *p, unsigned batch, bool chunk)
 
 extern "C" void *fyb_batch_create(void *plan, unsigned batch) { return batch_create((Plan *)plan, batch, false); }
 
+// Prompt chunks into the plan's cache; out receives the logits of the last
+// token, or with bt->all_logits (one chunk, a draft to verify) [count][V].
 static int prefill_chunks(Plan *p, Batch *bt, const uint32_t *tokens, size_t count, size_t position, float *out)
 {
     cudaStream_t s = p->ctx->stream;
+    if (bt->all_logits && count > bt->B) return -1;
     for (size_t c0 = 0; c0 < count; c0 += bt->B) {
         const unsigned R = (unsigned)std::min<size_t>(bt->B, count - c0);
         BatchRequest r = {};
@@ -1367,12 +1378,38 @@ static int prefill_chunks(Plan *p, Batch *bt, const uint32_t *tokens, size_t cou
     }
     ++p->stats.downloads;
     ++p->stats.synchronizations;
-    if (cudaMemcpyAsync(out, bt->logits, (size_t)p->V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+    const size_t rows = bt->all_logits ? count : 1;
+    if (cudaMemcpyAsync(out, bt->logits, rows * p->V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaStreamSynchronize(s) != cudaSuccess || *(volatile unsigned *)p->err_host)
         return -2;
-    for (size_t i = 0; i < p->V; ++i) if (!std::isfinite(out[i])) return -2;
+    for (size_t i = 0; i < rows * p->V; ++i) if (!std::isfinite(out[i])) return -2;
     const nya_llm_tokenizer &tk = p->m->tokenizer;
-    for (size_t i = 0; i < tk.suppressed_count; ++i) out[tk.suppressed_tokens[i]] = -INFINITY;
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t i = 0; i < tk.suppressed_count; ++i) out[r * p->V + tk.suppressed_tokens[i]] = -INFINITY;
+    return 0;
+}
+
+// Speculative verification: the count (1..16) draft tokens at positions
+// [position, position + count) of the plan's sequence in one chunk, every
+// row's logits to out [count][V] (suppressed ids -inf), the draft's K/V rows
+// written to the cache (the caller continues from the accepted prefix and
+// rewrites the rest, as the engine's session does).
+extern "C" int fyb_plan_verify(void *opaque, const uint32_t *tokens, size_t count, size_t position, float *out)
+{
+    Plan *p = (Plan *)opaque;
+    if (!p || !tokens || !out || count == 0 || count > BATCH_MAX || p->failed || !p->connected ||
+        position > p->capacity || count > p->capacity - position || (position != 0 && position > p->valid))
+        return -1;
+    for (size_t i = 0; i < count; ++i) if (tokens[i] >= p->V) return -1;
+    DeviceScope scope(p->ctx->device);
+    if (!scope.ok) return -1;
+    Batch *bt = plan_chunker(p);
+    if (!bt) return -1;  // no chunker for this plan (tensor-parallel shard, or chunking switched off)
+    bt->all_logits = true;
+    const int r = prefill_chunks(p, bt, tokens, count, position, out);
+    bt->all_logits = false;
+    if (r) return plan_fail(p, position);
+    p->valid = position + count;
     return 0;
 }
 

@@ -133,6 +133,18 @@ int fyb_attention_decode_static(const float *q, const void *k_cache, const void 
    token. `plan` is a state returned by the vtable's plan_create. */
 int fyb_plan_decode_greedy(void *plan, uint32_t token, size_t position, size_t steps, uint32_t *tokens_out);
 
+/* Speculative verification (the engine's serial draft check,
+   backend/core/llm_cpu.c:1274-1305, as one pass): count (1..16) draft tokens
+   at positions [position, position + count) of a single-GPU plan's sequence
+   (position <= the valid prefix), causal attention inside the draft, every
+   weight read once for all of them; the logits of every draft position to
+   logits [count][V] (suppressed ids -inf). The draft's K/V rows stay in the
+   cache: the caller continues from the accepted prefix, whose later positions
+   the next call rewrites. 0 / -1 invalid or no chunker (tensor-parallel
+   shards, NYA_CUDA_CHUNKED_PREFILL=0) / -1 and a failed plan on a device
+   error. */
+int fyb_plan_verify(void *plan, const uint32_t *tokens, size_t count, size_t position, float *logits);
+
 /* Times `steps` device-side greedy steps with CUDA events on the plan's
    stream (no host synchronization between steps); returns milliseconds or
    a negative value on failure. */

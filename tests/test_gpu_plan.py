@@ -242,3 +242,29 @@ def test_ring_sizes_match(ring):
         r2 = run(b, NYA_CUDA_RING_BYTES=ring)
         assert r2.returncode == 0, r2.stderr
         assert (np.load(a) == np.load(b)).all()
+
+
+@pytest.mark.parametrize("name,cfg,tokens", SMALL_MODELS)
+def test_verify_draft(provider, name, cfg, tokens):
+    """fyb_plan_verify: a prompt, then an 8-token draft checked in one pass
+    (every row's logits against the fp16-KV oracle at its position), then a
+    second draft from inside the first (the rejected tail is rewritten),
+    then a plain decode step after it."""
+    m = F.SynthModel(**cfg)
+    plan = provider.plan(m, 48)
+    ref16 = O.Session(m.ptr, 48, m.vocabulary, kv_f16=True)
+    prompt = bench_tokens(11, m.vocabulary, 2)
+    assert plan.prefill(prompt, 0) == 0
+    for i, t in enumerate(prompt):
+        ref16.forward(int(t), i, logits=False)
+    for start, draft in ((11, bench_tokens(8, m.vocabulary, 7)), (14, bench_tokens(16, m.vocabulary, 9))):
+        got = plan.verify(draft, start)
+        assert got is not None and got.shape == (len(draft), m.vocabulary)
+        for i, t in enumerate(draft):
+            e = ref16.forward(int(t), start + i)
+            assert logit_error(got[i], e) <= 1e-3, (start, i, logit_error(got[i], e))
+            assert np.argmax(got[i]) == np.argmax(e)
+    t = int(np.argmax(e))
+    assert plan.token(t, 30) == 0
+    assert logit_error(plan.logits, ref16.forward(t, 30)) <= 1e-3
+    assert plan.verify(bench_tokens(17, m.vocabulary), 0) is None  # more than one chunk
