@@ -112,7 +112,7 @@ def double_reference(data, type_id, xs, cols, rows, chunk=8192):
 @pytest.mark.parametrize("type_id", [F.Q4_K, F.Q6_K])
 @pytest.mark.parametrize("rows,cols", SWEEP)
 def test_projection_sweep(provider, type_id, rows, cols):
-    """C2 shapes with BASELINE value distributions; batches 1, 2, 4, 8 and 16.
+    """C2 shapes with the benchmark's value distributions; batches 1, 2, 4, 8 and 16.
     Bounds: the reference's forward-error bound against the double dot,
     |a - s| <= 1e-6 (1 + sum|w x|), and the north-star 1e-3 relative."""
     nbytes = rows * F.row_bytes(type_id, cols)
@@ -132,7 +132,7 @@ def test_projection_sweep(provider, type_id, rows, cols):
 
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (1000, 14336), (37, 32768)])
 def test_q8_0_matvec(provider, rows, cols):
-    """C1 (Q8_0 4096x4096, BASELINE value distribution: int8 uniform in
+    """C1 (Q8_0 4096x4096, the benchmark's value distribution: int8 uniform in
     [-127, 127], d = |N(0,1)| * 0.01) and row widths that split a row over 2
     and 4 warps; batches 1, 5 and 8 through the engine's matvec / matmul.
     Bounds as in test_projection_sweep, and the engine's own scalar Q8_0
