@@ -1331,9 +1331,10 @@ static Batch *batch_create(Plan *p, unsigned batch, bool chunk)
     bt->h = (float *)A((size_t)batch * p->ffn * 4);
     bt->logits = (float *)A((size_t)batch * p->V * 4);
     bt->req = (unsigned *)A((3 * BATCH_MAX + 1) * 4); bt->tokens = (unsigned *)A(BATCH_MAX * 4);
-    // partitions of each (sequence, KV head): about two waves of the SMs at the longest context
+    // partitions of each (sequence, KV head): about four waves of the SMs, 4..16
     const size_t seqs = chunk ? 1 : batch;
-    bt->splits = (unsigned)std::max<size_t>(1, std::min<size_t>(16, (size_t)2 * p->ctx->sms / (seqs * p->Hkv)));
+    bt->splits = (unsigned)std::max<size_t>(4, std::min<size_t>(16, ((size_t)4 * p->ctx->sms + seqs * p->Hkv - 1) /
+                                                                        (seqs * p->Hkv)));
     if (ok) {
         AttentionLaunch L = batch_attention(bt, 0);
         bt->attn_ws_bytes = attention_workspace_bytes(L);
