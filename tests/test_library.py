@@ -86,3 +86,19 @@ def test_shared_file_model(tmp_path):
     other = F.SynthModel(layers=2, embedding=512, heads=4, kv_heads=2, feed_forward=1024, vocabulary=1024,
                          context=64, seed=10, path=None)
     assert not (other.tensor_bytes(4) == ref.tensor_bytes(4)).all()
+
+
+def test_batch_and_verify_reject_bad_arguments():
+    """The batched-decode and draft-verification entry points validate their
+    arguments before touching a device: a missing plan or batch is refused."""
+    import numpy as np
+    tok = np.zeros(16, np.uint32)
+    out = np.zeros(16, np.float32)
+    p = C.c_void_p(tok.ctypes.data)
+    assert not F.lib.fyb_batch_create(None, 4)
+    assert F.lib.fyb_batch_step(None, p, p, None, None) == -1
+    assert F.lib.fyb_batch_decode_greedy(None, p, p, 4, p) == -1
+    assert F.lib.fyb_batch_time_greedy(None, p, p, 4) < 0
+    assert F.lib.fyb_batch_launches_per_step(None) == 0
+    F.lib.fyb_batch_free(None)  # a no-op
+    assert F.lib.fyb_plan_verify(None, p, 8, 0, C.c_void_p(out.ctypes.data)) == -1
