@@ -355,8 +355,15 @@ struct Plan {
     nya_compute_stats stats;
     unsigned long long launches = 0;  // counted while enqueuing
     std::vector<uint16_t> kv_stage;
-    // profiling: when set, an event is recorded after every launch
+    // profiling: when set, an event is recorded after every launch (second:
+    // kernel class | projection << 4)
     std::vector<std::pair<cudaEvent_t, int>> *marks = nullptr;
+    // NYA_CUDA_PROFILE=1: every step runs the per-operation kernels without
+    // graphs, timed per kernel class and per projection, printed at plan_free
+    bool profile = false;
+    double prof_ms[4] = {0, 0, 0, 0};     // matrix, attention, other, prefill chunks
+    double prof_proj_ms[5] = {0, 0, 0, 0, 0};
+    unsigned long long prof_proj_calls[5] = {0, 0, 0, 0, 0}, prof_steps = 0;
     // persistent decode kernel (decode.cu); dec_grid == 0: per-kernel launches
     int dec_grid = 0;
     DecodeLayer *dec_layers = nullptr;
@@ -399,6 +406,22 @@ static void plan_free(void *opaque)
 {
     Plan *p = (Plan *)opaque;
     if (!p) return;
+    if (p->profile) {
+        std::fprintf(stderr,
+                     "fyodor_b200 profile: steps=%llu kernel GPU milliseconds: matrix=%.3f attention=%.3f other=%.3f "
+                     "prefill_chunks=%.3f (per-operation kernels, graphs off)\n",
+                     p->prof_steps, p->prof_ms[0], p->prof_ms[1], p->prof_ms[2], p->prof_ms[3]);
+        static const char *names[5] = {"qkv", "o", "gateup", "down", "logits"};
+        const QWeights *w[5] = {p->layers.empty() ? nullptr : &p->layers[0].qkv,
+                                p->layers.empty() ? nullptr : &p->layers[0].o,
+                                p->layers.empty() ? nullptr : &p->layers[0].gateup,
+                                p->layers.empty() ? nullptr : &p->layers[0].down, &p->out_head};
+        for (int k = 0; k < 5; ++k)
+            if (p->prof_proj_calls[k] && w[k])
+                std::fprintf(stderr, "fyodor_b200 matrix profile: projection=%s type=%u rows=%u columns=%u calls=%llu "
+                             "milliseconds=%.6f\n", names[k], w[k]->type, w[k]->tiles * 16, w[k]->cols,
+                             p->prof_proj_calls[k], p->prof_proj_ms[k]);
+    }
     if (p->prefill) ::batch_free(p->prefill);
     {
         DeviceScope scope(p->ctx->device);
@@ -583,9 +606,10 @@ static int enqueue_step(Plan *p, StepMode mode)
     cudaStream_t s = p->ctx->stream;
     const bool pdl = true;
     p->launches = 0;
-    int kc = KC_OTHER;
+    int kc = KC_OTHER, proj = 0;  // proj: 1 QKV, 2 O, 3 gate/up, 4 down, 5 logits (matrix launches)
 #define RUN(expr) do { int r_ = (expr); ++p->launches; if (r_) return r_; \
-        if (p->marks) { cudaEvent_t ev; cudaEventCreate(&ev); cudaEventRecord(ev, s); p->marks->push_back({ev, kc}); } } while (0)
+        if (p->marks) { cudaEvent_t ev; cudaEventCreate(&ev); cudaEventRecord(ev, s); \
+                        p->marks->push_back({ev, kc | (kc == KC_MATRIX ? proj << 4 : 0)}); } } while (0)
     RUN(launch_gather(p->embd, p->embd_row_bytes, p->embd_type, p->d, p->request, 0, p->x[0], s, false));
     int cur = 0;
     bool pending = false;
@@ -595,6 +619,7 @@ static int enqueue_step(Plan *p, StepMode mode)
         L.x = p->x[cur];
         if (pending) { L.delta = p->delta; L.x_out = p->x[cur ^ 1]; }
         L.pdl = pdl;
+        proj = 1;
         RUN(launch_qgemv(L, s));
         if (pending) cur ^= 1;
 
@@ -606,16 +631,19 @@ static int enqueue_step(Plan *p, StepMode mode)
         kc = KC_MATRIX;
         QgemvLaunch O = o_launch(p, l);
         O.pdl = pdl;
+        proj = 2;
         RUN(launch_qgemv(O, s));
 
         QgemvLaunch G = gateup_launch(p, l);
         G.x = p->x[cur]; G.delta = p->delta; G.x_out = p->x[cur ^ 1];
         G.pdl = pdl;
+        proj = 3;
         RUN(launch_qgemv(G, s));
         cur ^= 1;
 
         QgemvLaunch D = down_launch(p, l);
         D.pdl = pdl;
+        proj = 4;
         RUN(launch_qgemv(D, s));
         pending = true;
     }
@@ -625,6 +653,7 @@ static int enqueue_step(Plan *p, StepMode mode)
     Lg.x = p->x[cur];
     Lg.delta = pending ? p->delta : nullptr;
     Lg.pdl = pdl;
+    proj = 5;
     RUN(launch_qgemv(Lg, s));
     kc = KC_OTHER;
     if (mode == STEP_GREEDY) RUN(launch_advance(p, pdl));
@@ -632,8 +661,39 @@ static int enqueue_step(Plan *p, StepMode mode)
     return 0;
 }
 
+// A step under NYA_CUDA_PROFILE: the per-operation kernels with an event after
+// each, their times added per kernel class and per projection.
+static int run_step_profiled(Plan *p, StepMode mode)
+{
+    cudaStream_t s = p->ctx->stream;
+    std::vector<std::pair<cudaEvent_t, int>> marks;
+    p->marks = &marks;
+    cudaEvent_t start;
+    cudaEventCreate(&start);
+    cudaEventRecord(start, s);
+    int r = enqueue_step(p, mode);
+    p->marks = nullptr;
+    p->stats.kernel_launches += p->launches;
+    if (cudaStreamSynchronize(s) != cudaSuccess) r = -2;
+    cudaEvent_t prev = start;
+    for (auto &m : marks) {
+        float ms = 0.f;
+        if (!r && cudaEventElapsedTime(&ms, prev, m.first) == cudaSuccess) {
+            p->prof_ms[m.second & 15] += ms;
+            const int proj = m.second >> 4;
+            if (proj >= 1 && proj <= 5) { p->prof_proj_ms[proj - 1] += ms; ++p->prof_proj_calls[proj - 1]; }
+        }
+        prev = m.first;
+    }
+    for (auto &m : marks) cudaEventDestroy(m.first);
+    cudaEventDestroy(start);
+    ++p->prof_steps;
+    return r;
+}
+
 static int run_step(Plan *p, StepMode mode)
 {
+    if (p->profile) return run_step_profiled(p, mode);
     cudaStream_t s = p->ctx->stream;
     if (!p->use_graphs || p->marks) {
         const int r = enqueue_step(p, mode);
@@ -944,15 +1004,22 @@ static void *plan_create(void *opaque, const nya_llm_context *m, size_t capacity
                      cudaMemsetAsync(p->attn_ws, 0, p->attn_ws_bytes, c->stream) == cudaSuccess;
     }
     if (ok) ok = setup_persistent(p);
-    if (ok && !p->dec_grid) {  // the per-operation step: every projection within the GEMV's limits
+    bool per_op = true;  // the per-operation step: every projection within the GEMV's limits
+    {
         const size_t ks[3] = {d, (size_t)H * hd, ffn};
         for (size_t k : ks)
             if (!qgemv_supported(m->layers[0].query->type, k, 1) || !qgemv_supported(m->output->type, d, 1) ||
-                !qgemv_supported(m->layers[0].feed_forward_down->type, k, 1)) {
-                plan_free(p);
-                return plan_decline("geometry beyond the per-operation step's GEMV");
-            }
+                !qgemv_supported(m->layers[0].feed_forward_down->type, k, 1))
+                per_op = false;
     }
+    if (ok && !p->dec_grid && !per_op) {
+        plan_free(p);
+        return plan_decline("geometry beyond the per-operation step's GEMV");
+    }
+    // NYA_CUDA_PROFILE=1 (resident.inc:176-183): every step runs the
+    // per-operation kernels without graphs, timed per class and projection
+    if (const char *prof = std::getenv("NYA_CUDA_PROFILE"))
+        p->profile = !std::strcmp(prof, "1") && per_op && p->tp_size == 1;
     if (ok && p->tp_size > 1) {
         if (!p->dec_grid) {  // only the persistent kernel exchanges partial sums
             debug("tensor parallelism needs the persistent decode kernel", cudaSuccess);
@@ -1360,6 +1427,9 @@ static int prefill_chunks(Plan *p, Batch *bt, const uint32_t *tokens, size_t cou
 {
     cudaStream_t s = p->ctx->stream;
     if (bt->all_logits && count > bt->B) return -1;
+    cudaEvent_t t0 = nullptr, t1 = nullptr;  // NYA_CUDA_PROFILE: the chunks' time as one class
+    if (p->profile && cudaEventCreate(&t0) == cudaSuccess && cudaEventCreate(&t1) == cudaSuccess)
+        cudaEventRecord(t0, s);
     for (size_t c0 = 0; c0 < count; c0 += bt->B) {
         const unsigned R = (unsigned)std::min<size_t>(bt->B, count - c0);
         BatchRequest r = {};
@@ -1380,9 +1450,16 @@ static int prefill_chunks(Plan *p, Batch *bt, const uint32_t *tokens, size_t cou
     ++p->stats.downloads;
     ++p->stats.synchronizations;
     const size_t rows = bt->all_logits ? count : 1;
+    if (t1) cudaEventRecord(t1, s);
     if (cudaMemcpyAsync(out, bt->logits, rows * p->V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaStreamSynchronize(s) != cudaSuccess || *(volatile unsigned *)p->err_host)
         return -2;
+    if (t1) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, t0, t1) == cudaSuccess) p->prof_ms[3] += ms;
+        cudaEventDestroy(t0);
+        cudaEventDestroy(t1);
+    }
     for (size_t i = 0; i < rows * p->V; ++i) if (!std::isfinite(out[i])) return -2;
     const nya_llm_tokenizer &tk = p->m->tokenizer;
     for (size_t r = 0; r < rows; ++r)
@@ -1839,7 +1916,7 @@ extern "C" int fyb_plan_profile(void *opaque, uint32_t token, size_t position, s
         cudaEvent_t prev = start;
         for (auto &m : marks) {
             float ms = 0.f;
-            if (!r && cudaEventElapsedTime(&ms, prev, m.first) == cudaSuccess) out[m.second] += ms;
+            if (!r && cudaEventElapsedTime(&ms, prev, m.first) == cudaSuccess) out[m.second & 15] += ms;
             prev = m.first;
         }
         for (auto &m : marks) cudaEventDestroy(m.first);

@@ -268,3 +268,35 @@ def test_verify_draft(provider, name, cfg, tokens):
     assert plan.token(t, 30) == 0
     assert logit_error(plan.logits, ref16.forward(t, 30)) <= 1e-3
     assert plan.verify(bench_tokens(17, m.vocabulary), 0) is None  # more than one chunk
+
+
+def test_profile_switch():
+    """NYA_CUDA_PROFILE=1 (the reference's switch, resident.inc:176-183):
+    steps run the per-operation kernels without graphs, still match the
+    oracle, and plan_free prints the per-class and per-projection times."""
+    code = ("import numpy as np, fyodor_b200 as F, oracle as O\n"
+            "from tests.patterns import SMALL_MODELS\n"
+            "name, cfg, tokens = SMALL_MODELS[0]\n"
+            "m=F.SynthModel(**cfg)\n"
+            "pr=F.Provider()\n"
+            "p=pr.plan(m,32)\n"
+            "ref=O.Session(m.ptr,32,m.vocabulary,kv_f16=True)\n"
+            "assert p.prefill(np.array(tokens[:5],np.uint32),0)==0\n"
+            "for i,t in enumerate(tokens[:5]): e=ref.forward(t,i,logits=i==4)\n"
+            "err=[float(np.max(np.abs(p.logits-e))/(1+np.max(np.abs(e))))]\n"
+            "for i,t in enumerate(tokens[5:9]):\n"
+            "    assert p.token(t,5+i)==0\n"
+            "    e=ref.forward(t,5+i); err.append(float(np.max(np.abs(p.logits-e))/(1+np.max(np.abs(e)))))\n"
+            "st=p.stats()\n"
+            "print('ERR',max(err),'CAPTURES',st['graph_captures'])\n"
+            "p.close()\n")
+    r = _env_run(code, NYA_CUDA_PROFILE=1)
+    assert r.returncode == 0, r.stderr
+    line = [x for x in r.stdout.splitlines() if x.startswith("ERR")][0].split()
+    assert float(line[1]) <= 1e-3 and line[3] == "0"  # oracle parity; no graph was captured
+    prof = [x for x in r.stderr.splitlines() if x.startswith("fyodor_b200 profile:")]
+    assert prof and "steps=4" in prof[0], r.stderr
+    vals = dict(kv.split("=") for kv in prof[0].split("milliseconds:")[1].split("(")[0].split())
+    assert float(vals["matrix"]) > 0 and float(vals["attention"]) > 0 and float(vals["prefill_chunks"]) > 0
+    shapes = [x for x in r.stderr.splitlines() if x.startswith("fyodor_b200 matrix profile:")]
+    assert len(shapes) == 5 and all("calls=" in x for x in shapes), r.stderr
