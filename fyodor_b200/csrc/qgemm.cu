@@ -1,9 +1,13 @@
 // qgemm.cu - weight-reusing small-batch GEMM on the integer tensor cores:
 // Y[v][r] = sum_k W[r][k] X[v][k] for 3..16 input vectors (the engine's
 // matmul, backend/include/compute.h:80-83; its reference small-batch path
-// keeps one weight pass per batch, CUDA/gemm.cu:53-95).
+// keeps one weight pass per batch, CUDA/gemm.cu:53-95). Two kernels, both
+// reading every weight unit from HBM once per call: qgemm_kernel (legacy
+// mma.sync integer MMAs, below) for the smaller batches and qgemm_tc_kernel
+// (tcgen05 with the operand in tensor memory, further down) from
+// tc_min_nv(type) vectors on; launch_qgemm picks between them.
 //
-// Every weight unit (16 rows x 256 columns, repacked as for the GEMV) is
+// qgemm_kernel: every weight unit (16 rows x 256 columns, repacked as for the GEMV) is
 // read from HBM once per call and multiplied against all vectors while it
 // sits in shared memory: the x limbs of all vectors are B operands next to
 // each other (two vectors x four limbs per m16n8 MMA), so one unit feeds
