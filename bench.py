@@ -461,6 +461,13 @@ def run_provider_70b(args):
         raise SystemExit("prefill failed")
     first = int(np.argmax(plan.logits))
     setup_s = time.perf_counter() - t_setup
+    barrier(dist)
+    t0 = time.perf_counter()  # the same prompt again, as in the 8B line
+    if plan.prefill(prompt, 0) != 0 or int(np.argmax(plan.logits)) != first:
+        raise SystemExit("second prefill failed")
+    prefill_s = max_over_ranks(dist, time.perf_counter() - t0)
+    prefill = {"tokens": PROMPT, "ms": round(prefill_s * 1e3, 2), "tok_s": round(PROMPT / prefill_s, 1),
+               "chunk_tokens": int(plan.stats()["prefill_batch"])}
     for _ in range(args.warmup):
         if plan.time_greedy(first, PROMPT, DECODE) < 0:
             raise SystemExit("warm-up failed")
@@ -503,7 +510,7 @@ def run_provider_70b(args):
                      "kernel": "decode_kernel (persistent, one launch per token; %d B per launch per GPU)" % int(bpt),
                      "us_per_launch": round(per_launch_ms * 1000, 2), "peak_source": peak_kind,
                      "tok_s_at_peak": round(hbm * 1e9 / bpt, 1)},
-        "gpu_launches": int(launches), "clocks": clocks.summary(), "setup_s": round(setup_s, 1),
+        "gpu_launches": int(launches), "clocks": clocks.summary(), "prefill": prefill, "setup_s": round(setup_s, 1),
         "cpu_baseline": None,
     }
     if rank == 0:
